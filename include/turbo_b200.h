@@ -1,0 +1,90 @@
+/* turbo_b200.h -- the C ABI of libturbo_b200.so, the B200-native CUDA backend
+ * of TurboEmbed.
+ *
+ * The product is one symbol, the backend table the reference core links:
+ *
+ *   turbo_cuda_backend   replaces the reference's own `turbo_cuda_backend`
+ *                        (core/cuda/backend.cpp:3780-3809), the table of
+ *                        include/turbo/turbo_backend.h:455-627 that the core
+ *                        imports in core/src/cuda.rs:8-17 and registers first
+ *                        in core/src/backend/mod.rs:338-360. Every function of
+ *                        the table keeps the reference's argument meaning,
+ *                        status codes and error fields.
+ *
+ * The rest are test hooks, as the reference exports its own `turbo_cuda_*`
+ * hooks for its integration tests (core/cuda/backend.cpp:3811-4103, bound in
+ * core/src/cuda.rs:25-76). Each allocates and synchronises freely: none is
+ * on the run path.
+ */
+#ifndef TURBO_B200_H
+#define TURBO_B200_H
+
+#include "turbo/turbo_abi.h"
+
+#define TB_EXPORT __attribute__((visibility("default")))
+#define TB_STRINGIFY_(x) #x
+#define TB_STRINGIFY(x) TB_STRINGIFY_(x)
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The backend table (core/cuda/backend.cpp:3780-3809). */
+TB_EXPORT extern const turbo_backend turbo_cuda_backend;
+
+/* The table by function, for loaders that resolve functions only. */
+TB_EXPORT const turbo_backend *turbo_b200_backend(void);
+
+/* Device allocations this library has made since it was loaded, for the
+ * test that a warm run allocates nothing (reference: turbo_cuda_allocations,
+ * core/cuda/backend.cpp:3811, used by core/tests/cuda_runs.rs:202-290). */
+TB_EXPORT uint64_t turbo_cuda_allocations(void);
+
+/* Fault injection on the host: the `after`-th next session allocation
+ * fails as out of memory (0 = the next one; -1 turns it off). Tests the
+ * error path of session_open without touching the GPU (the reference's
+ * injection hook is turbo_cuda_fail_variant, core/cuda/backend.cpp:3988). */
+TB_EXPORT void turbo_cuda_fail_allocation(int32_t after);
+
+/* The label benchmarks are filed under (core/cuda/backend.cpp:3830). */
+TB_EXPORT const char *turbo_cuda_arch_label(void);
+
+/* One GEMM y = epi(a w^T + bias) on the device, operands given as host F32
+ * and narrowed to dtype (TURBO_DTYPE_F16 / BF16 / F32) first, run through
+ * `variant` 0 (the tcgen05 kernel) or 1 (the FFMA kernel), the result
+ * widened back into y_out. epi is 0 store, 1 GELU, 2 residual (y_in holds
+ * y's starting values), 3 gated (interleaved gate/up columns; y is
+ * [M, N/2]), 4 RoPE on the columns below 2 * (N / 3) with head_dim, pos [M],
+ * cos/sin [positions][head_dim / 2]. The kernel check the reference runs
+ * against cuBLAS (turbo_cuda_gemm_check, core/cuda/backend.cpp:3626-3772). */
+TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t variant, uint32_t epi, uint32_t M, uint32_t N,
+                                        uint32_t K, const float *a, const float *w, const float *bias,
+                                        const float *y_in, float *y_out, uint32_t head_dim, const int32_t *pos,
+                                        const float *cos_t, const float *sin_t, uint32_t positions,
+                                        turbo_error *err);
+
+/* Attention over `batch` rows packed one after another (row b has lens[b]
+ * tokens), qkv [tokens, 3 * hidden] host F32 narrowed to dtype, live [tokens]
+ * the mask entries, window < 0 for whole rows. variant 0 is the F16/BF16
+ * tensor-core kernel, 1 the F32 kernel. ctx_out [tokens, hidden]. */
+TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, uint32_t batch, const int32_t *lens,
+                                             const float *qkv, const uint8_t *live, uint32_t heads,
+                                             uint32_t head_dim, int32_t window, float *ctx_out, turbo_error *err);
+
+/* Bench hooks (no counterpart needed in the reference, whose bench times the
+ * public API): mark the last written batch as written again, so the next
+ * session_run computes on the plan already in device memory; turn on event
+ * pairs around every GEMM and attention launch; and read the device time of
+ * the last run (events on the context's stream around its launches) and,
+ * when profiling, the summed GEMM and attention launch times, the GEMM
+ * launch count and their algorithmic FLOPs (2 M N K each). */
+TB_EXPORT int32_t turbo_b200_session_rerun(void *session);
+TB_EXPORT int32_t turbo_b200_session_profile(void *session, uint32_t on);
+TB_EXPORT int32_t turbo_b200_session_times(void *session, float *run_ms, float *gemm_ms, float *attn_ms,
+                                           uint32_t *gemm_launches, double *gemm_flops);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TURBO_B200_H */

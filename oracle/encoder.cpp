@@ -1,0 +1,533 @@
+// encoder.cpp -- TEST INFRASTRUCTURE ONLY: the CPU oracle (see oracle.h).
+//
+// A restatement of the reference's CPU encoder arithmetic, each part citing
+// the reference file it follows (paths inside the reference project):
+//   packing            core/src/cpu/encoder/mod.rs:377-421  (Encoder::pack)
+//   lookup + LN        core/src/cpu/encoder/job.rs:114-131  (Job::lookup)
+//   rotary embed       core/src/cpu/encoder/job.rs:148-165  (Job::embed)
+//   LayerNorm          core/src/cpu/kernels/rowwise.rs:10-29 (F64 sums in 8 lanes)
+//   linear layers      core/src/cpu/kernels/mod.rs:1-19, gemm.rs:64-135
+//                      (each output one FMA chain over k = 0.., then + bias)
+//   GELU               rowwise.rs:57-81 (restated with libm erf in F64)
+//   attention          core/src/cpu/kernels/attend.rs:95-198 (scores as FMA
+//                      chains over d, * scale, masked/out-of-window keys -inf,
+//                      exp, sum in 16 lanes + fixed tree, p *= 1/sum,
+//                      context as FMA chains over keys)
+//   RoPE, gated MLP    core/src/cpu/kernels/pairs.rs:56-131
+//   rotary layers      core/src/cpu/encoder/rotary/mod.rs:87-175
+//   pooling, L2        core/src/cpu/encoder/mod.rs:426-484, job.rs:171-190
+//   rope table         core/src/rope.rs:20-38
+//   rerank head        core/src/session/rerank.rs:170-188
+// Compiled with -ffp-contract=off so only the explicit fmaf calls fuse,
+// as the reference's AVX2/AVX-512 kernels fuse exactly the GEMM and
+// attention chains.
+#include "oracle.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <thread>
+#include <vector>
+
+namespace {
+
+constexpr int LANES = 16;
+
+struct Model {
+    const turbo_backend_model *d;
+    bool modern = false;
+    uint32_t h = 0, heads = 0, dh = 0, inter = 0;
+    std::vector<std::vector<float>> own;  // widened copies when the model is not F32
+    std::vector<const float *> t;         // every tensor as F32
+
+    const float *tensor(uint32_t i) const { return t[i]; }
+};
+
+float half_to_float(uint16_t v) {
+    uint32_t s = (v >> 15) & 1, e = (v >> 10) & 31, m = v & 1023;
+    float f;
+    if (e == 0) f = std::ldexp((float)m, -24);
+    else if (e == 31) f = m ? std::numeric_limits<float>::quiet_NaN() : std::numeric_limits<float>::infinity();
+    else f = std::ldexp((float)(m | 1024), (int)e - 25);
+    return s ? -f : f;
+}
+
+float bf16_to_float(uint16_t v) {
+    uint32_t bits = (uint32_t)v << 16;
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+bool load(const turbo_backend_model *d, Model &m) {
+    m.d = d;
+    m.modern = d->family == TURBO_FAMILY_MODERNBERT;
+    if (!m.modern && d->family != TURBO_FAMILY_BERT && d->family != TURBO_FAMILY_ROBERTA) return false;
+    m.h = d->hidden;
+    m.heads = d->heads;
+    m.dh = d->hidden / d->heads;
+    m.inter = d->intermediate;
+    m.t.resize(d->tensor_count, nullptr);
+    for (uint32_t i = 0; i < d->tensor_count; ++i) {
+        const turbo_backend_tensor &x = d->tensors[i];
+        if (!x.data) continue;
+        if (d->dtype == TURBO_DTYPE_F32) {
+            m.t[i] = (const float *)x.data;
+        } else {
+            size_t n = x.shape[0] * (x.ndim == 2 ? x.shape[1] : 1);
+            std::vector<float> w(n);
+            const uint16_t *s = (const uint16_t *)x.data;
+            for (size_t k = 0; k < n; ++k)
+                w[k] = d->dtype == TURBO_DTYPE_F16 ? half_to_float(s[k]) : bf16_to_float(s[k]);
+            m.own.push_back(std::move(w));
+            m.t[i] = m.own.back().data();
+        }
+    }
+    return true;
+}
+
+// Split [0, n) over threads and run f(lo, hi) on each part.
+template <class F>
+void parallel(size_t n, unsigned threads, F f) {
+    if (n == 0) return;
+    unsigned k = (unsigned)std::min<size_t>(threads, n);
+    if (k <= 1) {
+        f(size_t(0), n);
+        return;
+    }
+    std::vector<std::thread> pool;
+    size_t per = (n + k - 1) / k;
+    for (unsigned i = 0; i < k; ++i) {
+        size_t lo = i * per, hi = std::min(n, lo + per);
+        if (lo >= hi) break;
+        pool.emplace_back([=] { f(lo, hi); });
+    }
+    for (auto &th : pool) th.join();
+}
+
+// rowwise.rs:10-29: mean and biased variance in F64, element i in lane
+// i % 8, the lanes added in one fixed order; y = ((y-mean)*inv as F32)*w + b.
+double lanes8(const double *s) { return ((s[0] + s[4]) + (s[1] + s[5])) + ((s[2] + s[6]) + (s[3] + s[7])); }
+
+void layer_norm(float *y, const float *w, const float *b, uint32_t n, double eps) {
+    double s[8] = {0};
+    for (uint32_t i = 0; i < n; ++i) s[i % 8] += (double)y[i];
+    double mean = lanes8(s) / (double)n;
+    double v[8] = {0};
+    for (uint32_t i = 0; i < n; ++i) {
+        double c = (double)y[i] - mean;
+        v[i % 8] += c * c;
+    }
+    double var = lanes8(v) / (double)n;
+    double inv = 1.0 / std::sqrt(var + (double)(float)eps);
+    for (uint32_t i = 0; i < n; ++i) {
+        float z = (float)(((double)y[i] - mean) * inv);
+        y[i] = z * w[i] + (b ? b[i] : 0.0f);
+    }
+}
+
+float gelu(float x) { return (float)(0.5 * (double)x * (1.0 + std::erf((double)x * 0.70710678118654752440))); }
+
+enum Epi { EPI_STORE, EPI_GELU, EPI_RESIDUAL };
+
+// y[t, o] = epi(chain_k x[t,k] w[o,k], b[o]) for every token: w [n, k]
+// row-major as the model stores it. Weights are transposed once into
+// [k][n] so the chains of 16 neighbouring outputs run side by side (the
+// compiler vectorises the o loop); each output is still one chain over k.
+struct Linear {
+    std::vector<float> wt;  // [k][n]
+    uint32_t n = 0, k = 0;
+    void pack(const float *w, uint32_t n_, uint32_t k_) {
+        n = n_;
+        k = k_;
+        wt.assign((size_t)n * k, 0.0f);
+        for (uint32_t o = 0; o < n; ++o)
+            for (uint32_t i = 0; i < k; ++i) wt[(size_t)i * n + o] = w[(size_t)o * k + i];
+    }
+};
+
+void linear(const Linear &L, const float *x, size_t ldx, size_t tokens, const float *bias, float *y,
+            size_t ldy, Epi epi, unsigned threads) {
+    const uint32_t n = L.n, k = L.k;
+    constexpr int TB = 4, OB = 32;
+    parallel((tokens + TB - 1) / TB, threads, [&](size_t lo, size_t hi) {
+        for (size_t tb = lo; tb < hi; ++tb) {
+            size_t t0 = tb * TB, tn = std::min<size_t>(TB, tokens - t0);
+            for (uint32_t o0 = 0; o0 < n; o0 += OB) {
+                uint32_t on = std::min<uint32_t>(OB, n - o0);
+                float acc[TB][OB];
+                std::memset(acc, 0, sizeof(acc));
+                for (uint32_t i = 0; i < k; ++i) {
+                    const float *w = &L.wt[(size_t)i * n + o0];
+                    float wv[OB];
+                    for (int j = 0; j < OB; ++j) wv[j] = j < (int)on ? w[j] : 0.0f;
+                    for (size_t r = 0; r < tn; ++r) {
+                        float a = x[(t0 + r) * ldx + i];
+                        for (int j = 0; j < OB; ++j) acc[r][j] = std::fma(a, wv[j], acc[r][j]);
+                    }
+                }
+                for (size_t r = 0; r < tn; ++r) {
+                    float *dst = y + (t0 + r) * ldy + o0;
+                    for (uint32_t j = 0; j < on; ++j) {
+                        float v = acc[r][j] + (bias ? bias[o0 + j] : 0.0f);
+                        if (epi == EPI_GELU) dst[j] = gelu(v);
+                        else if (epi == EPI_RESIDUAL) dst[j] += v;
+                        else dst[j] = v;
+                    }
+                }
+            }
+        }
+    });
+}
+
+struct Packing {
+    uint32_t batch = 0, seq = 0;
+    std::vector<uint32_t> start, len;  // per row
+    std::vector<uint32_t> row, pos;    // per packed token
+    size_t tokens = 0;
+};
+
+// mod.rs:377-421: each row through its last live token, or through a
+// range's furthest column when that is further.
+Packing pack(const turbo_backend_embed_rows *r, const turbo_token_range *ranges, uint32_t count) {
+    Packing p;
+    p.batch = r->batch;
+    p.seq = r->seq;
+    uint32_t stride = r->row_stride ? r->row_stride : r->seq;
+    std::vector<uint32_t> furthest(r->batch, 0);
+    for (uint32_t i = 0; i < count; ++i) furthest[ranges[i].row] = std::max(furthest[ranges[i].row], ranges[i].end);
+    size_t t = 0;
+    for (uint32_t b = 0; b < r->batch; ++b) {
+        uint32_t live = 0;
+        for (uint32_t c = 0; c < r->seq; ++c)
+            if (r->mask[(size_t)b * stride + c]) live = c + 1;
+        uint32_t len = count ? std::max(live, furthest[b]) : live;
+        p.start.push_back((uint32_t)t);
+        p.len.push_back(len);
+        for (uint32_t c = 0; c < len; ++c) {
+            p.row.push_back(b);
+            p.pos.push_back(c);
+        }
+        t += len;
+    }
+    p.tokens = t;
+    return p;
+}
+
+// attend.rs:95-198 for every query of one row in one head. qkv is
+// [tokens, 3h] (Q at head*d, K at h + head*d, V at 2h + head*d).
+void attend_row_head(const Model &m, const float *qkv, float *ctx, const Packing &P,
+                     const turbo_backend_embed_rows *r, uint32_t b, uint32_t head, size_t window,
+                     std::vector<float> &scratch) {
+    const uint32_t h = m.h, d = m.dh, len = P.len[b];
+    const size_t ld = 3 * (size_t)h;
+    const uint32_t lp = (len + LANES - 1) / LANES * LANES;
+    const uint32_t stride = r->row_stride ? r->row_stride : r->seq;
+    const float *base = qkv + (size_t)P.start[b] * ld;
+    scratch.assign((size_t)d * lp + 2 * (size_t)lp + d, 0.0f);
+    float *kt = scratch.data();          // [d][lp], keys transposed
+    float *masked = kt + (size_t)d * lp; // [lp]
+    float *sc = masked + lp;             // [lp]
+    float *acc = sc + lp;                // [d]
+    for (uint32_t j = 0; j < len; ++j)
+        for (uint32_t c = 0; c < d; ++c) kt[(size_t)c * lp + j] = base[j * ld + h + head * d + c];
+    const float NEG = -std::numeric_limits<float>::infinity();
+    for (uint32_t j = 0; j < lp; ++j)
+        masked[j] = (j < len && r->mask[(size_t)b * stride + j] != 0) ? 0.0f : NEG;
+    const float scale = 1.0f / std::sqrt((float)d);
+    for (uint32_t i = 0; i < len; ++i) {
+        const float *q = base + i * ld + head * d;
+        for (uint32_t j = 0; j < lp; ++j) sc[j] = 0.0f;
+        for (uint32_t c = 0; c < d; ++c) {
+            const float qc = q[c];
+            const float *kc = kt + (size_t)c * lp;
+            for (uint32_t j = 0; j < lp; ++j) sc[j] = std::fma(qc, kc[j], sc[j]);
+        }
+        for (uint32_t j = 0; j < lp; ++j) sc[j] = sc[j] * scale + masked[j];
+        if (window != (size_t)-1) {
+            for (uint32_t j = 0; j < lp; ++j) {
+                size_t dist = i > j ? i - j : j - i;
+                if (dist > window) sc[j] = NEG;
+            }
+        }
+        float mx = NEG;
+        for (uint32_t j = 0; j < lp; ++j) mx = sc[j] > mx ? sc[j] : mx;
+        float *out = ctx + ((size_t)P.start[b] + i) * h + head * d;
+        if (mx == NEG) {
+            for (uint32_t c = 0; c < d; ++c) out[c] = 0.0f;
+            continue;
+        }
+        for (uint32_t j = 0; j < lp; ++j) sc[j] = std::exp(sc[j] - mx);
+        float lanes[LANES] = {0};
+        for (uint32_t j = 0; j < lp; ++j) lanes[j % LANES] += sc[j];
+        for (int w = LANES / 2; w > 0; w /= 2)
+            for (int l = 0; l < w; ++l) lanes[l] += lanes[l + w];
+        const float inv = 1.0f / lanes[0];
+        for (uint32_t j = 0; j < lp; ++j) sc[j] *= inv;
+        for (uint32_t c = 0; c < d; ++c) acc[c] = 0.0f;
+        for (uint32_t j = 0; j < len; ++j) {
+            const float pj = sc[j];
+            const float *v = base + j * ld + 2 * h + head * d;
+            for (uint32_t c = 0; c < d; ++c) acc[c] = std::fma(pj, v[c], acc[c]);
+        }
+        for (uint32_t c = 0; c < d; ++c) out[c] = acc[c];
+    }
+}
+
+void attention(const Model &m, const float *qkv, float *ctx, const Packing &P, const turbo_backend_embed_rows *r,
+               size_t window, unsigned threads) {
+    const size_t items = (size_t)P.batch * m.heads;
+    parallel(items, threads, [&](size_t lo, size_t hi) {
+        std::vector<float> scratch;
+        for (size_t it = lo; it < hi; ++it) {
+            uint32_t b = (uint32_t)(it / m.heads), head = (uint32_t)(it % m.heads);
+            if (P.len[b]) attend_row_head(m, qkv, ctx, P, r, b, head, window, scratch);
+        }
+    });
+}
+
+// pairs.rs:56-101: Q and K of each head rotated pair (c, c + d/2) by the
+// token's position with the layer's cos/sin, in F32 with two roundings.
+void rope(const Model &m, float *qkv, const Packing &P, const float *cos_t, const float *sin_t, unsigned threads) {
+    const uint32_t h = m.h, d = m.dh, half = d / 2;
+    parallel(P.tokens, threads, [&](size_t lo, size_t hi) {
+        for (size_t t = lo; t < hi; ++t) {
+            const float *cs = cos_t + (size_t)P.pos[t] * half, *sn = sin_t + (size_t)P.pos[t] * half;
+            for (uint32_t part = 0; part < 2; ++part) {
+                for (uint32_t head = 0; head < m.heads; ++head) {
+                    float *x = qkv + t * 3 * h + part * h + head * d;
+                    for (uint32_t i = 0; i < half; ++i) {
+                        float x1 = x[i], x2 = x[i + half];
+                        float a = x1 * cs[i], bq = x2 * sn[i];
+                        float c = x2 * cs[i], e = x1 * sn[i];
+                        x[i] = a - bq;
+                        x[i + half] = c + e;
+                    }
+                }
+            }
+        }
+    });
+}
+
+void norm_all(float *x, size_t tokens, uint32_t h, const float *w, const float *b, double eps, unsigned threads) {
+    parallel(tokens, threads, [&](size_t lo, size_t hi) {
+        for (size_t t = lo; t < hi; ++t) layer_norm(x + t * h, w, b, h, eps);
+    });
+}
+
+// Returns the packed tokens' final hidden states.
+std::vector<float> encode(const Model &m, const turbo_backend_embed_rows *r, const Packing &P, unsigned threads) {
+    const turbo_backend_model *d = m.d;
+    const uint32_t h = m.h, I = m.inter;
+    const size_t T = P.tokens;
+    const uint32_t stride = r->row_stride ? r->row_stride : r->seq;
+    std::vector<float> x(T * h), xn, qkv(T * 3 * h), ctx(T * h), ffn;
+    const double eps = d->layer_norm_eps;
+    if (!m.modern) {
+        // job.rs:114-131
+        const float *word = m.tensor(TURBO_BERT_WORD_EMBEDDINGS), *pos = m.tensor(TURBO_BERT_POSITION_EMBEDDINGS),
+                    *ty = m.tensor(TURBO_BERT_TOKEN_TYPE_EMBEDDINGS);
+        parallel(T, threads, [&](size_t lo, size_t hi) {
+            for (size_t t = lo; t < hi; ++t) {
+                size_t at = (size_t)P.row[t] * stride + P.pos[t];
+                uint32_t id = (uint32_t)r->ids[at], tt = r->types ? (uint32_t)r->types[at] : 0;
+                uint32_t p = P.pos[t] + d->position_offset;
+                float *dst = &x[t * h];
+                for (uint32_t i = 0; i < h; ++i)
+                    dst[i] = word[(size_t)id * h + i] + pos[(size_t)p * h + i] + ty[(size_t)tt * h + i];
+                layer_norm(dst, m.tensor(TURBO_BERT_EMBEDDINGS_LN_WEIGHT), m.tensor(TURBO_BERT_EMBEDDINGS_LN_BIAS), h,
+                           eps);
+            }
+        });
+        ffn.resize(T * I);
+        for (uint32_t l = 0; l < d->layers; ++l) {
+            auto w = [&](uint32_t k) { return m.tensor(TURBO_BERT_EMBEDDING_TENSORS + l * TURBO_BERT_LAYER_TENSORS + k); };
+            // Q, K and V rows as one [3h, h] product, as the reference packs them.
+            std::vector<float> wqkv((size_t)3 * h * h), bqkv(3 * h);
+            for (int part = 0; part < 3; ++part) {
+                std::memcpy(&wqkv[(size_t)part * h * h], w(TURBO_BERT_Q_WEIGHT + 2 * part), sizeof(float) * h * h);
+                std::memcpy(&bqkv[(size_t)part * h], w(TURBO_BERT_Q_BIAS + 2 * part), sizeof(float) * h);
+            }
+            Linear Lqkv, Lo, L1, L2;
+            Lqkv.pack(wqkv.data(), 3 * h, h);
+            Lo.pack(w(TURBO_BERT_ATTN_OUT_WEIGHT), h, h);
+            L1.pack(w(TURBO_BERT_FFN_IN_WEIGHT), I, h);
+            L2.pack(w(TURBO_BERT_FFN_OUT_WEIGHT), h, I);
+            linear(Lqkv, x.data(), h, T, bqkv.data(), qkv.data(), 3 * h, EPI_STORE, threads);
+            attention(m, qkv.data(), ctx.data(), P, r, (size_t)-1, threads);
+            linear(Lo, ctx.data(), h, T, w(TURBO_BERT_ATTN_OUT_BIAS), x.data(), h, EPI_RESIDUAL, threads);
+            norm_all(x.data(), T, h, w(TURBO_BERT_ATTN_LN_WEIGHT), w(TURBO_BERT_ATTN_LN_BIAS), eps, threads);
+            linear(L1, x.data(), h, T, w(TURBO_BERT_FFN_IN_BIAS), ffn.data(), I, EPI_GELU, threads);
+            linear(L2, ffn.data(), I, T, w(TURBO_BERT_FFN_OUT_BIAS), x.data(), h, EPI_RESIDUAL, threads);
+            norm_all(x.data(), T, h, w(TURBO_BERT_FFN_LN_WEIGHT), w(TURBO_BERT_FFN_LN_BIAS), eps, threads);
+        }
+        return x;
+    }
+    // ModernBERT: rotary/mod.rs:87-175.
+    const float *word = m.tensor(TURBO_MODERNBERT_WORD_EMBEDDINGS);
+    parallel(T, threads, [&](size_t lo, size_t hi) {
+        for (size_t t = lo; t < hi; ++t) {
+            size_t at = (size_t)P.row[t] * stride + P.pos[t];
+            std::memcpy(&x[t * h], word + (size_t)r->ids[at] * h, sizeof(float) * h);
+            layer_norm(&x[t * h], m.tensor(TURBO_MODERNBERT_EMBEDDINGS_LN_WEIGHT), nullptr, h, eps);
+        }
+    });
+    xn.resize(T * h);
+    std::vector<float> gu(T * 2 * (size_t)I);
+    ffn.resize(T * I);
+    const size_t positions = d->max_positions, pairs = d->rope_pairs, halftab = positions * pairs;
+    const size_t window = d->attention_window ? d->attention_window / 2 : (size_t)-1;
+    for (uint32_t l = 0; l < d->layers; ++l) {
+        auto w = [&](uint32_t k) {
+            return m.tensor(TURBO_MODERNBERT_EMBEDDING_TENSORS + l * TURBO_MODERNBERT_LAYER_TENSORS + k);
+        };
+        bool global = d->global_every == 0 || l % d->global_every == 0;
+        const float *cos_t = d->rope_table + (global ? 0 : 2 * halftab), *sin_t = cos_t + halftab;
+        const float *src = x.data();
+        if (l > 0) {
+            std::memcpy(xn.data(), x.data(), sizeof(float) * T * h);
+            norm_all(xn.data(), T, h, w(TURBO_MODERNBERT_ATTN_LN_WEIGHT), nullptr, eps, threads);
+            src = xn.data();
+        }
+        Linear Lqkv, Lo, L1, L2;
+        Lqkv.pack(w(TURBO_MODERNBERT_QKV_WEIGHT), 3 * h, h);
+        Lo.pack(w(TURBO_MODERNBERT_ATTN_OUT_WEIGHT), h, h);
+        L1.pack(w(TURBO_MODERNBERT_FFN_IN_WEIGHT), 2 * I, h);
+        L2.pack(w(TURBO_MODERNBERT_FFN_OUT_WEIGHT), h, I);
+        linear(Lqkv, src, h, T, nullptr, qkv.data(), 3 * h, EPI_STORE, threads);
+        rope(m, qkv.data(), P, cos_t, sin_t, threads);
+        attention(m, qkv.data(), ctx.data(), P, r, global ? (size_t)-1 : window, threads);
+        linear(Lo, ctx.data(), h, T, nullptr, x.data(), h, EPI_RESIDUAL, threads);
+        std::memcpy(xn.data(), x.data(), sizeof(float) * T * h);
+        norm_all(xn.data(), T, h, w(TURBO_MODERNBERT_FFN_LN_WEIGHT), nullptr, eps, threads);
+        linear(L1, xn.data(), h, T, nullptr, gu.data(), 2 * I, EPI_STORE, threads);
+        // pairs.rs:112-131 with the activated half's rows first (turbo_backend.h:126).
+        parallel(T, threads, [&](size_t lo, size_t hi) {
+            for (size_t t = lo; t < hi; ++t)
+                for (uint32_t j = 0; j < I; ++j) {
+                    float g = gu[t * 2 * I + j], u = gu[t * 2 * I + I + j];
+                    float a = d->activation == TURBO_ACTIVATION_SILU ? (float)(g / (1.0 + std::exp(-(double)g))) : gelu(g);
+                    ffn[t * I + j] = a * u;
+                }
+        });
+        linear(L2, ffn.data(), I, T, nullptr, x.data(), h, EPI_RESIDUAL, threads);
+    }
+    norm_all(x.data(), T, h, m.tensor(TURBO_MODERNBERT_FINAL_NORM_WEIGHT), nullptr, eps, threads);
+    return x;
+}
+
+// mod.rs:445-467: the mean over live tokens of the columns, in F32 in column
+// order, scaled by 1/n; all columns when none is live.
+void mean(const float *x, const Packing &P, const turbo_backend_embed_rows *r, uint32_t b, uint32_t c0, uint32_t c1,
+          uint32_t h, float *dst, uint32_t od) {
+    const uint32_t stride = r->row_stride ? r->row_stride : r->seq;
+    const int32_t *mask = r->mask + (size_t)b * stride;
+    bool live_only = false;
+    for (uint32_t c = c0; c < c1; ++c) live_only |= mask[c] != 0;
+    for (uint32_t j = 0; j < od; ++j) dst[j] = 0.0f;
+    uint32_t n = 0;
+    for (uint32_t c = c0; c < c1; ++c) {
+        if (live_only && mask[c] == 0) continue;
+        const float *row = x + ((size_t)P.start[b] + c) * h;
+        for (uint32_t j = 0; j < od; ++j) dst[j] += row[j];
+        ++n;
+    }
+    float inv = 1.0f / (float)n;
+    for (uint32_t j = 0; j < od; ++j) dst[j] *= inv;
+}
+
+// mod.rs:472-484
+void finish(float *dst, uint32_t od, uint32_t normalize) {
+    if (normalize != TURBO_NORMALIZE_L2) return;
+    double s = 0.0;
+    for (uint32_t j = 0; j < od; ++j) s += (double)dst[j] * (double)dst[j];
+    double norm = std::max(std::sqrt(s), 1e-12);
+    float inv = (float)(1.0 / norm);
+    for (uint32_t j = 0; j < od; ++j) dst[j] *= inv;
+}
+
+}  // namespace
+
+extern "C" int32_t oracle_encode(const turbo_backend_model *model, const turbo_backend_embed_rows *rows,
+                                 const turbo_token_range *ranges, uint32_t count, uint32_t threads, float *out) {
+    Model m;
+    if (!load(model, m)) return TURBO_E_UNSUPPORTED;
+    unsigned th = threads ? threads : std::max(1u, std::thread::hardware_concurrency());
+    Packing P = pack(rows, ranges, count);
+    std::vector<float> x = encode(m, rows, P, th);
+    const uint32_t h = m.h, od = rows->output_dim ? rows->output_dim : h;
+    if (count == 0) {
+        for (uint32_t b = 0; b < rows->batch; ++b) {
+            float *dst = out + (size_t)b * od;
+            const float *start = &x[(size_t)P.start[b] * h];
+            if (rows->pooling == TURBO_POOLING_CLS) std::memcpy(dst, start, sizeof(float) * od);
+            else if (rows->pooling == TURBO_POOLING_LAST)
+                std::memcpy(dst, start + (size_t)(P.len[b] - 1) * h, sizeof(float) * od);
+            else mean(x.data(), P, rows, b, 0, P.len[b], h, dst, od);
+            finish(dst, od, rows->normalize);
+        }
+        return 0;
+    }
+    for (uint32_t i = 0; i < count; ++i) {
+        const turbo_token_range &g = ranges[i];
+        float *dst = out + (size_t)i * od;
+        mean(x.data(), P, rows, g.row, g.start, std::min(g.end, P.len[g.row]), h, dst, od);
+        finish(dst, od, rows->normalize);
+    }
+    return 0;
+}
+
+extern "C" int64_t oracle_hidden_states(const turbo_backend_model *model, const turbo_backend_embed_rows *rows,
+                                        uint32_t threads, float *states, uint64_t cap, uint32_t *row_spans) {
+    Model m;
+    if (!load(model, m)) return -TURBO_E_UNSUPPORTED;
+    unsigned th = threads ? threads : std::max(1u, std::thread::hardware_concurrency());
+    Packing P = pack(rows, nullptr, 0);
+    std::vector<float> x = encode(m, rows, P, th);
+    if (x.size() > cap) return -TURBO_E_CAPACITY;
+    std::memcpy(states, x.data(), sizeof(float) * x.size());
+    for (uint32_t b = 0; b < rows->batch; ++b) {
+        row_spans[2 * b] = P.start[b];
+        row_spans[2 * b + 1] = P.len[b];
+    }
+    return (int64_t)P.tokens;
+}
+
+extern "C" void oracle_rope_table(double global_theta, double local_theta, uint32_t positions, uint32_t pairs,
+                                  float *out) {
+    const float width = (float)(2 * pairs);
+    size_t at = 0;
+    for (double theta : {global_theta, local_theta}) {
+        std::vector<float> inv(pairs);
+        for (uint32_t i = 0; i < pairs; ++i) {
+            // rope.rs:28: 1.0 / (theta^e rounded to F32), the division in F32.
+            float e = (float)(2 * i) / width;
+            inv[i] = 1.0f / (float)std::pow((double)(float)theta, (double)e);
+        }
+        for (uint32_t p = 0; p < positions; ++p)
+            for (uint32_t i = 0; i < pairs; ++i) out[at++] = (float)std::cos((double)((float)p * inv[i]));
+        for (uint32_t p = 0; p < positions; ++p)
+            for (uint32_t i = 0; i < pairs; ++i) out[at++] = (float)std::sin((double)((float)p * inv[i]));
+    }
+}
+
+extern "C" void oracle_rerank_head(const float *x, uint32_t n, uint32_t hidden, const float *pooler_w,
+                                   const float *pooler_b, const float *cls_w, const float *cls_b, float *scores) {
+    std::vector<float> pooled(hidden);
+    for (uint32_t r = 0; r < n; ++r) {
+        const float *in = x + (size_t)r * hidden;
+        const float *hv = in;
+        if (pooler_w) {
+            for (uint32_t o = 0; o < hidden; ++o) {
+                double s = (double)pooler_b[o];
+                for (uint32_t i = 0; i < hidden; ++i) s += (double)pooler_w[(size_t)o * hidden + i] * (double)in[i];
+                pooled[o] = (float)std::tanh(s);
+            }
+            hv = pooled.data();
+        }
+        double v = (double)cls_b[0];
+        for (uint32_t i = 0; i < hidden; ++i) v += (double)cls_w[i] * (double)hv[i];
+        scores[r] = (float)v;
+    }
+}

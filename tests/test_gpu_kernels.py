@@ -1,0 +1,163 @@
+"""Each CUDA kernel alone, through the library's check hooks, against numpy on
+the same narrowed operands (F64 arithmetic): the tcgen05 GEMM with every
+epilogue, the FFMA GEMM, and both attentions."""
+import numpy as np
+import pytest
+
+from turboembed_b200 import abi, models, runtime
+
+pytestmark = pytest.mark.gpu
+
+F16, BF16, F32 = abi.TURBO_DTYPE_F16, abi.TURBO_DTYPE_BF16, abi.TURBO_DTYPE_F32
+
+
+def narrow(x, dtype):
+    x = np.asarray(x, np.float32)
+    if dtype == F16:
+        return x.astype(np.float16).astype(np.float32)
+    if dtype == BF16:
+        return models.from_bf16_bits(models.to_bf16_bits(x))
+    return x
+
+
+def gelu(x):
+    from math import erf
+    return 0.5 * x * (1.0 + np.vectorize(erf)(x / np.sqrt(2.0)))
+
+
+def rel_err(got, want):
+    return np.abs(got - want).max() / max(np.abs(want).max(), 1e-30)
+
+
+def ref_gemm(dtype, epi, a, w, bias, y_in, head_dim=0, pos=None, cos=None, sin=None):
+    a64, w64 = narrow(a, dtype).astype(np.float64), narrow(w, dtype).astype(np.float64)
+    y = a64 @ w64.T + (0 if bias is None else bias.astype(np.float64))
+    if epi == 1:
+        y = gelu(y)
+    elif epi == 2:
+        y = narrow(y_in, dtype).astype(np.float64) + y
+    elif epi == 3:
+        y = gelu(y[:, 0::2]) * y[:, 1::2]
+    elif epi == 4:
+        h = w.shape[0] // 3
+        half = head_dim // 2
+        for part in range(2):
+            for hd in range(h // head_dim):
+                c0 = part * h + hd * head_dim
+                x1, x2 = y[:, c0:c0 + half].copy(), y[:, c0 + half:c0 + head_dim].copy()
+                cs, sn = cos[pos].astype(np.float64), sin[pos].astype(np.float64)
+                y[:, c0:c0 + half] = x1 * cs - x2 * sn
+                y[:, c0 + half:c0 + head_dim] = x2 * cs + x1 * sn
+    return y
+
+
+SHAPES = [(128, 256, 64), (300, 768, 768), (77, 96, 32), (1000, 2304, 768), (257, 384, 1536), (129, 3072, 768)]
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_tcgen05_gemm_epilogues(dtype, shape, epi):
+    M, N, K = shape
+    rng = np.random.default_rng(M * 7 + N + K + epi)
+    a = rng.standard_normal((M, K), np.float32)
+    w = rng.standard_normal((N, K), np.float32) * np.float32(1 / np.sqrt(K))
+    bias = rng.standard_normal(N).astype(np.float32)
+    y_in = rng.standard_normal((M, N // 2 if epi == 3 else N)).astype(np.float32) if epi == 2 else None
+    got = runtime.gemm_check(dtype, 0, epi, a, w, bias, y_in)
+    want = ref_gemm(dtype, epi, a, w, bias, y_in)
+    tol = 8e-3 if dtype == BF16 else 1.5e-3
+    assert rel_err(got, want) < tol
+    # The FFMA kernel on the same narrowed operands agrees as closely.
+    simt = runtime.gemm_check(dtype, 1, epi, a, w, bias, y_in)
+    assert rel_err(got, simt) < tol
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+@pytest.mark.parametrize("head_dim,h", [(64, 768), (32, 384), (16, 32)])
+def test_tcgen05_gemm_rope(dtype, head_dim, h):
+    M, K = 200, h
+    rng = np.random.default_rng(head_dim)
+    a = rng.standard_normal((M, K), np.float32)
+    w = rng.standard_normal((3 * h, K), np.float32) * np.float32(1 / np.sqrt(K))
+    tab = models.rope_table(160000.0, 10000.0, 300, head_dim // 2)
+    cos, sin = tab[0, 0], tab[0, 1]
+    pos = rng.integers(0, 300, size=M).astype(np.int32)
+    got = runtime.gemm_check(dtype, 0, 4, a, w, None, None, head_dim, pos, cos, sin)
+    want = ref_gemm(dtype, 4, a, w, None, None, head_dim, pos, cos, sin)
+    tol = 8e-3 if dtype == BF16 else 1.5e-3
+    assert rel_err(got, want) < tol
+    simt = runtime.gemm_check(dtype, 1, 4, a, w, None, None, head_dim, pos, cos, sin)
+    assert rel_err(got, simt) < tol
+
+
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_ffma_gemm_f32_is_one_chain_over_k(epi):
+    M, N, K = 150, 160, 200
+    rng = np.random.default_rng(epi)
+    a = rng.standard_normal((M, K), np.float32)
+    w = rng.standard_normal((N, K), np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    y_in = rng.standard_normal((M, N // 2 if epi == 3 else N)).astype(np.float32) if epi == 2 else None
+    got = runtime.gemm_check(F32, 1, epi, a, w, bias, y_in)
+    want = ref_gemm(F32, epi, a, w, bias, y_in)
+    assert np.abs(got - want).max() < 1e-4 * max(1.0, np.abs(want).max())
+    # Same bits on a second launch.
+    assert np.array_equal(got, runtime.gemm_check(F32, 1, epi, a, w, bias, y_in))
+
+
+def ref_attention(qkv, lens, live, heads, d, window):
+    h = heads * d
+    out = np.zeros((qkv.shape[0], h))
+    start = 0
+    for n in lens:
+        q = qkv[start:start + n, :h].astype(np.float64)
+        k = qkv[start:start + n, h:2 * h].astype(np.float64)
+        v = qkv[start:start + n, 2 * h:].astype(np.float64)
+        lv = live[start:start + n].astype(bool)
+        for hd in range(heads):
+            sl = slice(hd * d, (hd + 1) * d)
+            s = q[:, sl] @ k[:, sl].T / np.sqrt(d)
+            ok = np.broadcast_to(lv[None, :], s.shape).copy()
+            if window >= 0:
+                i = np.arange(n)
+                ok &= np.abs(i[:, None] - i[None, :]) <= window
+            s = np.where(ok, s, -np.inf)
+            m = s.max(1, keepdims=True)
+            dead = ~np.isfinite(m)
+            p = np.exp(np.where(dead, 0, s - np.where(dead, 0, m)))
+            p = np.where(ok, p, 0)
+            den = p.sum(1, keepdims=True)
+            o = (p @ v[:, sl]) / np.where(den > 0, den, 1)
+            out[start:start + n, sl] = np.where(den > 0, o, 0)
+        start += n
+    return out
+
+
+CASES = [([64], 2, 64, -1), ([300, 5, 129], 12, 64, -1), ([70, 200], 4, 32, -1), ([64, 33], 2, 16, 4),
+         ([500, 130], 2, 64, 64), ([1], 1, 64, -1)]
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+@pytest.mark.parametrize("case", CASES)
+def test_mma_attention(dtype, case):
+    lens, heads, d, window = case
+    T = sum(lens)
+    rng = np.random.default_rng(T + d)
+    qkv = narrow(rng.standard_normal((T, 3 * heads * d)).astype(np.float32) * 2, dtype)
+    live = (rng.random(T) > 0.15).astype(np.uint8)
+    got = runtime.attention_check(dtype, 0, lens, qkv, live, heads, d, window)
+    want = ref_attention(qkv, lens, live, heads, d, window)
+    assert np.abs(got - want).max() < (3e-2 if dtype == BF16 else 5e-3)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_f32_attention(case):
+    lens, heads, d, window = case
+    T = sum(lens)
+    rng = np.random.default_rng(T + d + 1)
+    qkv = rng.standard_normal((T, 3 * heads * d)).astype(np.float32)
+    live = (rng.random(T) > 0.15).astype(np.uint8)
+    got = runtime.attention_check(F32, 1, lens, qkv, live, heads, d, window)
+    want = ref_attention(qkv, lens, live, heads, d, window)
+    assert np.abs(got - want).max() < 2e-5

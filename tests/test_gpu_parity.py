@@ -1,0 +1,231 @@
+"""End-to-end parity through the `turbo_cuda_backend` table (libturbo_b200.so)
+against the reference's golden vectors and the CPU oracle on the same seeded
+weights and rows.
+
+Bounds (the reference's own, docs/benchmarks.md:959-963 and
+core/tests/cuda_runs.rs:67-74): EXACT (F32) cosine >= 0.9999 and max-abs
+<= 1e-4; F16/BF16 cosine >= 0.999, max-abs reported.
+"""
+import numpy as np
+import pytest
+
+from conftest import cosine, load_golden, mask_from_lengths, rerank_rows
+from oracle import oracle
+from turboembed_b200 import abi, models, runtime
+
+pytestmark = pytest.mark.gpu
+
+EXACT, FASTEST, MODEL = abi.TURBO_PRECISION_EXACT, abi.TURBO_PRECISION_FASTEST, abi.TURBO_PRECISION_MODEL
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    b = runtime.Backend()
+    assert b.device_count() >= 1, "no B200 listed by the backend"
+    c = b.context(0)
+    yield c
+    c.release()
+
+
+def check(got, want, precision, note=""):
+    cos = cosine(got, want).min()
+    mad = np.abs(got - want).max()
+    print(f"{note} cos={cos:.7f} max_abs={mad:.3e}")
+    if precision == EXACT:
+        assert cos >= 0.9999 and mad <= 1e-4, (cos, mad)
+    else:
+        assert cos >= 0.999, (cos, mad)
+    return cos, mad
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST, MODEL])
+def test_tiny_bert_reference_cases(ctx, precision):
+    a, meta = load_golden("tiny_bert")
+    d = models.bert_desc(a, meta)
+    m = ctx.load(d)
+    s = m.session(16, 64, precision)
+    mask = mask_from_lengths(a["lengths"], 64)
+    got = s.embed(a["ids"], mask)
+    check(got, a["embeddings"], precision, "tiny-bert vs upstream")
+    check(got, oracle.encode(d, a["ids"], mask), precision, "tiny-bert vs oracle")
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_tiny_modernbert_reference_cases(ctx, precision):
+    a, meta = load_golden("tiny_modernbert")
+    d = models.modernbert_desc(a, meta)
+    m = ctx.load(d)
+    s = m.session(9, 64, precision)
+    mask = mask_from_lengths(a["lengths"], 64)
+    got = s.embed(a["ids"], mask, normalize=abi.TURBO_NORMALIZE_NONE)
+    check(got, a["embeddings"], precision, "tiny-modernbert vs upstream")
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_tiny_xlmr_position_offset(ctx, precision):
+    a, meta = load_golden("tiny_xlmr")
+    d = models.bert_desc(a, meta)
+    m = ctx.load(d)
+    s = m.session(8, 64, precision)
+    got = s.embed(a["ids"], a["mask"])
+    check(got, a["embeddings"], precision, "tiny-xlmr vs transformers")
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_rerank_scores(ctx, precision):
+    a, meta = load_golden("tiny_bert")
+    d = models.bert_desc(a, meta)
+    m = ctx.load(d)
+    s = m.session(8, 32, precision, task=abi.TURBO_TASK_RERANK)
+    ids, types, mask, pair, z = rerank_rows()
+    cls = s.embed(ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
+    sc = oracle.rerank_head(cls, z["pooler_w"], z["pooler_b"], z["cls_w"], z["cls_b"])
+    scores = np.full(4, -np.inf)
+    for i, p in enumerate(pair):
+        scores[p] = max(scores[p], sc[i])
+    ref = z["scores"].ravel()
+    bound = 1e-4 if precision == EXACT else 1e-2 * np.abs(ref).max()  # cuda_rerank.rs:29, :144
+    assert np.abs(scores - ref).max() < bound
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("pooling", [abi.TURBO_POOLING_MEAN, abi.TURBO_POOLING_CLS, abi.TURBO_POOLING_LAST])
+def test_poolings_and_cut_vs_oracle(ctx, precision, pooling):
+    d = models.synthetic("minilm", 0, layers=2)
+    ids, mask, lens = models.rows_bert(5, 6, 16, 128, 128)
+    mask[1, 5] = 0  # a hole: a masked key inside the row
+    m = ctx.load(d)
+    s = m.session(8, 128, precision)
+    for od, norm in [(0, abi.TURBO_NORMALIZE_L2), (128, abi.TURBO_NORMALIZE_L2), (384, abi.TURBO_NORMALIZE_NONE)]:
+        got = s.embed(ids, mask, pooling=pooling, normalize=norm, output_dim=od)
+        want = oracle.encode(d, ids, mask, pooling=pooling, normalize=norm, output_dim=od)
+        check(got, want, precision, f"minilm pooling={pooling} od={od}")
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_ranges_vs_oracle_and_whole_row_equals_row_mean(ctx, precision):
+    d = models.synthetic("minilm", 0, layers=2)
+    ids, mask, lens = models.rows_bert(6, 5, 40, 128, 128)
+    ranges = models.ranges_tiling(7, lens, 8, 40)
+    m = ctx.load(d)
+    s = m.session(8, 128, precision, max_ranges=len(ranges) + 8)
+    s.write_ranges(ids, mask, ranges)
+    s.run()
+    got = s.read()
+    want = oracle.encode(d, ids, mask, ranges=ranges)
+    check(got, want, precision, "ranges")
+    whole = np.array([(r, 0, int(n)) for r, n in enumerate(lens)], np.uint32)
+    s.write_ranges(ids, mask, whole)
+    s.run()
+    by_range = s.read().copy()
+    by_row = s.embed(ids, mask)
+    assert np.array_equal(by_range, by_row)  # cuda_ranges.rs:40: bit for bit
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_bert_base_shape_vs_oracle(ctx, precision):
+    d = models.synthetic("bert-base", 1, layers=2)
+    ids, mask, lens = models.rows_bert(11, 6, 64, 512, 512)
+    m = ctx.load(d)
+    s = m.session(8, 512, precision)
+    got = s.embed(ids, mask, pooling=abi.TURBO_POOLING_CLS)
+    want = oracle.encode(d, ids, mask, pooling=abi.TURBO_POOLING_CLS)
+    check(got, want, precision, "bert-base 2 layers")
+    s.release()
+    m.release()
+
+
+def test_bf16_model_runs_in_bf16(ctx):
+    d = models.synthetic("bert-base", 2, dtype=abi.TURBO_DTYPE_BF16, layers=2)
+    ids, mask, types, lens = models.rows_rerank(3, 4, seq=512)
+    m = ctx.load(d)
+    s = m.session(4, 512, MODEL, task=abi.TURBO_TASK_RERANK)
+    assert s.compute_dtype == abi.TURBO_DTYPE_BF16
+    got = s.embed(ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
+    want = oracle.encode(d, ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
+    check(got, want, MODEL, "bf16 rerank body")
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_modernbert_long_rows_local_and_global_layers(ctx, precision):
+    d = models.synthetic("modernbert-base", 3, layers=3)
+    ids, mask, lens = models.rows_long(4, 2, 200, 700, 700, 100, 50367)
+    m = ctx.load(d)
+    s = m.session(2, 700, precision)
+    got = s.embed(ids, mask)
+    want = oracle.encode(d, ids, mask)
+    check(got, want, precision, "modernbert 3 layers")
+    s.release()
+    m.release()
+
+
+def test_warm_run_allocates_nothing_and_repeats_its_bits(ctx):
+    a, meta = load_golden("tiny_bert")
+    m = ctx.load(models.bert_desc(a, meta))
+    s = m.session(16, 64, FASTEST)
+    mask = mask_from_lengths(a["lengths"], 64)
+    first = s.embed(a["ids"], mask).copy()
+    lib = runtime.library()
+    before = lib.turbo_cuda_allocations()
+    s.write(a["ids"], mask)
+    run = s.run()
+    second = s.read()
+    assert lib.turbo_cuda_allocations() == before
+    assert run.device_allocs == 0 and run.host_allocs == 0
+    assert run.placement == abi.TURBO_PLACE_DEVICE and run.h2d_bytes > 0
+    assert np.array_equal(first, second)
+    s.release()
+    m.release()
+
+
+def test_errors_name_their_field(ctx):
+    a, meta = load_golden("tiny_bert")
+    m = ctx.load(models.bert_desc(a, meta))
+    with pytest.raises(runtime.TurboError) as e:
+        m.session(4, 64, EXACT, cpu_threads=2)
+    assert e.value.code == abi.TURBO_E_UNSUPPORTED_OPTION and e.value.field == 6
+    s = m.session(4, 64, EXACT)
+    with pytest.raises(runtime.TurboError) as e:
+        s.run()
+    assert e.value.code == abi.TURBO_E_INVALID_STATE
+    ids = np.zeros((5, 64), np.int32)
+    with pytest.raises(runtime.TurboError) as e:
+        s.write(ids, np.ones_like(ids))
+    assert e.value.code == abi.TURBO_E_CAPACITY
+    runtime.library().turbo_cuda_fail_allocation(0)
+    with pytest.raises(runtime.TurboError) as e:
+        m.session(4, 64, EXACT)
+    assert e.value.code == abi.TURBO_E_OUT_OF_MEMORY
+    runtime.library().turbo_cuda_fail_allocation(-1)
+    m.session(4, 64, EXACT).release()
+    s.release()
+    m.release()
+
+
+def test_output_exports_as_a_cuda_pointer(ctx):
+    a, meta = load_golden("tiny_bert")
+    m = ctx.load(models.bert_desc(a, meta))
+    s = m.session(16, 64, FASTEST)
+    s.write(a["ids"], mask_from_lengths(a["lengths"], 64))
+    run = s.run()
+    import ctypes as C
+    h, err = abi.turbo_native_handle(), abi.new_error()
+    h.struct_size = C.sizeof(h)
+    assert s.t.buffer_export(run.output, abi.TURBO_HANDLE_CUDA_PTR, C.byref(h), C.byref(err)) == 0
+    assert h.kind == abi.TURBO_HANDLE_CUDA_PTR and h.aux == 0 and h.handle != 0
+    s.release()
+    m.release()

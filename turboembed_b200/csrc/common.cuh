@@ -1,0 +1,75 @@
+// common.cuh -- element types, conversions and warp reductions shared by the
+// B200 kernels. Everything here is sm_100a device code or plain host code.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tb {
+
+// The element type a buffer holds. F32 is the EXACT tier's; F16 and BF16
+// the FASTEST and MODEL tiers'.
+enum class Dt : int { F32 = 0, F16 = 1, BF16 = 2 };
+
+template <class T> struct Elem;
+template <> struct Elem<float> {
+    static constexpr Dt dt = Dt::F32;
+    __device__ __forceinline__ static float to(float v) { return v; }
+    __device__ __forceinline__ static float from(float v) { return v; }
+};
+template <> struct Elem<__half> {
+    static constexpr Dt dt = Dt::F16;
+    __device__ __forceinline__ static float to(__half v) { return __half2float(v); }
+    __device__ __forceinline__ static __half from(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static constexpr Dt dt = Dt::BF16;
+    __device__ __forceinline__ static float to(__nv_bfloat16 v) { return __bfloat162float(v); }
+    __device__ __forceinline__ static __nv_bfloat16 from(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <class T> __device__ __forceinline__ float ld(const T *p) { return Elem<T>::to(*p); }
+template <class T> __device__ __forceinline__ void st(T *p, float v) { *p = Elem<T>::from(v); }
+
+// Two floats packed into one 32-bit word of T pairs (T = half or bf16).
+template <class T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+template <class T> __device__ __forceinline__ float2 unpack2(uint32_t w);
+template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+    return __half22float2(*reinterpret_cast<__half2 *>(&w));
+}
+template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&w));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// GELU with the error function, as the reference's encoders use
+// (core/src/cpu/kernels/rowwise.rs:57, upstream's "gelu"): CUDA's erff.
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+}  // namespace tb

@@ -1,0 +1,194 @@
+// hooks.cpp -- test hooks of libturbo_b200.so: single kernels on host data,
+// so the tests can check one kernel at a time against numpy and the oracle.
+// They allocate and synchronise; nothing on the run path calls them.
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../include/turbo_b200.h"
+#include "kernels.h"
+
+using namespace tb;
+
+namespace {
+
+int32_t hook_fail(turbo_error *err, int32_t code, const char *what, cudaError_t e) {
+    if (err) {
+        err->code = code;
+        err->field = 0;
+        snprintf(err->message, TURBO_ERROR_MESSAGE_LEN, "%s: %s", what, e == cudaSuccess ? "" : cudaGetErrorString(e));
+    }
+    return code;
+}
+
+struct Dev {
+    std::vector<void *> ptrs;
+    ~Dev() {
+        for (void *p : ptrs) cudaFree(p);
+    }
+    void *get(size_t bytes) {
+        void *p = nullptr;
+        if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return nullptr;
+        cudaMemset(p, 0, bytes ? bytes : 16);
+        ptrs.push_back(p);
+        return p;
+    }
+};
+
+bool dt_of(uint32_t dtype, Dt *dt) {
+    if (dtype == TURBO_DTYPE_F32) *dt = Dt::F32;
+    else if (dtype == TURBO_DTYPE_F16) *dt = Dt::F16;
+    else if (dtype == TURBO_DTYPE_BF16) *dt = Dt::BF16;
+    else return false;
+    return true;
+}
+
+// Host F32 -> device buffer of dt.
+void *to_device(Dev &dv, Dt dt, const float *h, size_t n, cudaError_t *e) {
+    float *f = (float *)dv.get(n * 4);
+    if (!f) {
+        *e = cudaErrorMemoryAllocation;
+        return nullptr;
+    }
+    if (h) *e = cudaMemcpy(f, h, n * 4, cudaMemcpyHostToDevice);
+    if (dt == Dt::F32) return f;
+    void *d = dv.get(n * 2);
+    if (!d) {
+        *e = cudaErrorMemoryAllocation;
+        return nullptr;
+    }
+    *e = narrow(dt, f, d, (int64_t)n, 0);
+    return d;
+}
+
+__attribute__((unused)) void widen_host(Dt dt, const void *dev, float *h, size_t n) {
+    if (dt == Dt::F32) {
+        cudaMemcpy(h, dev, n * 4, cudaMemcpyDeviceToHost);
+        return;
+    }
+    std::vector<uint16_t> raw(n);
+    cudaMemcpy(raw.data(), dev, n * 2, cudaMemcpyDeviceToHost);
+    for (size_t i = 0; i < n; ++i) {
+        uint16_t v = raw[i];
+        if (dt == Dt::BF16) {
+            uint32_t b = (uint32_t)v << 16;
+            memcpy(&h[i], &b, 4);
+        } else {
+            uint32_t s = (v >> 15) & 1, ex = (v >> 10) & 31, m = v & 1023;
+            float f;
+            if (ex == 0) f = ldexpf((float)m, -24);
+            else if (ex == 31) f = m ? NAN : INFINITY;
+            else f = ldexpf((float)(m | 1024), (int)ex - 25);
+            h[i] = s ? -f : f;
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t variant, uint32_t epi, uint32_t M,
+                                                   uint32_t N, uint32_t K, const float *a, const float *w,
+                                                   const float *bias, const float *y_in, float *y_out,
+                                                   uint32_t head_dim, const int32_t *pos, const float *cos_t,
+                                                   const float *sin_t, uint32_t positions, turbo_error *err) {
+    Dt dt;
+    if (!dt_of(dtype, &dt)) return hook_fail(err, TURBO_E_INVALID_ENUM, "dtype", cudaSuccess);
+    if (variant == 0 && dt == Dt::F32) return hook_fail(err, TURBO_E_UNSUPPORTED, "tcgen05 takes F16/BF16", cudaSuccess);
+    Dev dv;
+    cudaError_t e = cudaSuccess;
+    const size_t out_cols = epi == EPI_GATED ? N / 2 : N;
+    void *da = to_device(dv, dt, a, (size_t)M * K, &e);
+    void *dw = e == cudaSuccess ? to_device(dv, dt, w, (size_t)N * K, &e) : nullptr;
+    void *dy = e == cudaSuccess ? to_device(dv, dt, y_in, (size_t)M * out_cols, &e) : nullptr;
+    float *db = nullptr, *dcos = nullptr, *dsin = nullptr;
+    int32_t *dpos = nullptr;
+    if (e == cudaSuccess && bias) {
+        db = (float *)dv.get((size_t)N * 4);
+        e = cudaMemcpy(db, bias, (size_t)N * 4, cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess && epi == EPI_ROPE) {
+        const size_t tab = (size_t)positions * (head_dim / 2);
+        dcos = (float *)dv.get(tab * 4);
+        dsin = (float *)dv.get(tab * 4);
+        dpos = (int32_t *)dv.get((size_t)M * 4);
+        e = cudaMemcpy(dcos, cos_t, tab * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(dsin, sin_t, tab * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(dpos, pos, (size_t)M * 4, cudaMemcpyHostToDevice);
+    }
+    int *fault = (int *)dv.get(4);
+    if (e != cudaSuccess || !fault) return hook_fail(err, TURBO_E_RUNTIME, "gemm_check setup", e);
+    Epilogue ep;
+    ep.kind = (int)epi;
+    ep.bias = db;
+    ep.out = dy;
+    ep.ldo = (int64_t)out_cols;
+    ep.cos = dcos;
+    ep.sin = dsin;
+    ep.tok_pos = dpos;
+    ep.head_dim = (int)head_dim;
+    ep.rope_cols = (int)(2 * (N / 3));
+    if (variant == 0) {
+        TcMaps maps;
+        maps.bn = N % 256 == 0 ? 256 : 128;
+        e = make_operand_map(dt, da, M, K, K, 128, &maps.a);
+        if (e == cudaSuccess) e = make_operand_map(dt, dw, N, K, K, maps.bn, &maps.w);
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+        if (e == cudaSuccess) e = gemm_tc(dt, maps, (int)M, (int)N, (int)K, ep, sms, fault, 0);
+    } else {
+        if (epi == EPI_ROPE) {
+            Epilogue e2 = ep;
+            e2.kind = EPI_STORE;
+            e = gemm_simt(dt, da, K, dw, (int)M, (int)N, (int)K, e2, 0);
+            if (e == cudaSuccess) e = rope_qk(dt, dy, dpos, dcos, dsin, (int)M, (int)(N / 3), (int)head_dim, 0);
+        } else {
+            e = gemm_simt(dt, da, K, dw, (int)M, (int)N, (int)K, ep, 0);
+        }
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "gemm_check", e);
+    int f = 0;
+    cudaMemcpy(&f, fault, 4, cudaMemcpyDeviceToHost);
+    if (f) return hook_fail(err, TURBO_E_RUNTIME, "gemm_check: the kernel's fault word is set", cudaSuccess);
+    widen_host(dt, dy, y_out, (size_t)M * out_cols);
+    if (err) err->code = 0, err->message[0] = 0;
+    return TURBO_OK;
+}
+
+extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, uint32_t batch,
+                                                        const int32_t *lens, const float *qkv, const uint8_t *live,
+                                                        uint32_t heads, uint32_t head_dim, int32_t window,
+                                                        float *ctx_out, turbo_error *err) {
+    Dt dt;
+    if (!dt_of(dtype, &dt)) return hook_fail(err, TURBO_E_INVALID_ENUM, "dtype", cudaSuccess);
+    const int h = (int)(heads * head_dim);
+    std::vector<AttnItem> items;
+    int T = 0, max_len = 0;
+    const int qt = variant == 0 ? ATTN_MMA_QUERIES : ATTN_F32_QUERIES;
+    for (uint32_t b = 0; b < batch; ++b) {
+        for (int q0 = 0; q0 < lens[b]; q0 += qt) items.push_back(AttnItem{T, lens[b], q0, 0});
+        T += lens[b];
+        max_len = lens[b] > max_len ? lens[b] : max_len;
+    }
+    Dev dv;
+    cudaError_t e = cudaSuccess;
+    void *dq = to_device(dv, dt, qkv, (size_t)T * 3 * h, &e);
+    void *dc = e == cudaSuccess ? to_device(dv, dt, nullptr, (size_t)T * h, &e) : nullptr;
+    uint8_t *dl = (uint8_t *)dv.get((size_t)T);
+    AttnItem *di = (AttnItem *)dv.get(items.size() * sizeof(AttnItem));
+    if (e == cudaSuccess && dl && di) {
+        e = cudaMemcpy(dl, live, (size_t)T, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(di, items.data(), items.size() * sizeof(AttnItem), cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "attention_check setup", e);
+    if (variant == 0) e = attention_mma(dt, dq, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, 0);
+    else if (dt == Dt::F32)
+        e = attention_f32((const float *)dq, (float *)dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window,
+                          max_len, 0);
+    else return hook_fail(err, TURBO_E_UNSUPPORTED, "the F32 attention takes F32", cudaSuccess);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "attention_check", e);
+    widen_host(dt, dc, ctx_out, (size_t)T * h);
+    if (err) err->code = 0, err->message[0] = 0;
+    return TURBO_OK;
+}

@@ -1,0 +1,110 @@
+// kernels.h -- host-side launchers of the B200 kernels, called by backend.cpp.
+// Every launcher is asynchronous on the given stream and returns the launch
+// status (cudaGetLastError), never throwing.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace tb {
+
+// What a GEMM does with each output once its sum over k is complete.
+// y[t, o] = epi(sum_k a[t, k] w[o, k]), w stored [N, K] as the model does.
+enum EpiKind : int {
+    EPI_STORE = 0,     // y = acc + b
+    EPI_GELU = 1,      // y = gelu_erf(acc + b)
+    EPI_RESIDUAL = 2,  // y += acc + b (the residual stream, in place)
+    EPI_GATED = 3,     // y[:, j] = act(acc[:, 2j] + b) * (acc[:, 2j+1] + b): weights interleaved
+    EPI_ROPE = 4,      // as STORE, then Q and K columns (< rope_cols) rotated by position
+};
+
+struct Epilogue {
+    int kind = EPI_STORE;
+    const float *bias = nullptr;  // [N] F32, or null for none
+    void *out = nullptr;          // y, element type = the GEMM's
+    int64_t ldo = 0;              // y's row stride, elements
+    int act = 1;                  // EPI_GATED: 1 GELU (erf), 2 SiLU
+    // EPI_ROPE: cos/sin tables [positions][head_dim / 2] F32 for this layer's
+    // base, each token's position, the head width, and the first column
+    // that is not rotated (2 * hidden: V is left alone).
+    const float *cos = nullptr, *sin = nullptr;
+    const int32_t *tok_pos = nullptr;
+    int head_dim = 0, rope_cols = 0;
+};
+
+// The packed batch of one run, in device memory: each packed token's id,
+// type, column in its row and liveness (its mask entry), and each row's
+// first packed token. Written by the host at embed_write.
+struct Packed {
+    const int32_t *tok_id = nullptr;
+    const int32_t *tok_type = nullptr;  // null: every type 0
+    const int32_t *tok_pos = nullptr;
+    const uint8_t *tok_live = nullptr;
+    int tokens = 0;
+};
+
+// One vector the pool kernel writes: the mean (or the one token) of a row's
+// columns [c0, c1) starting at packed token `start`.
+struct PoolItem {
+    int32_t start;      // the row's first packed token
+    int32_t c0, c1;     // columns, relative to the row
+    int32_t live_only;  // 1: only live columns count; 0: every column (a range of mask-0 columns)
+};
+
+// One attention work item: `q_count` queries from query `q0` of a row whose
+// tokens start at packed token `start` and number `len`.
+struct AttnItem {
+    int32_t start, len, q0, pad;
+};
+
+// dst[i] = src[i] narrowed from F32 to F16 or BF16 (round to nearest even).
+cudaError_t narrow(Dt dt, const float *src, void *dst, int64_t n, cudaStream_t s);
+
+cudaError_t embed_layer_norm(Dt dt, void *x, const Packed &p, const float *word, const float *pos,
+                             const float *type, int pos_offset, const float *ln_w, const float *ln_b,
+                             int hidden, double eps, cudaStream_t s);
+// dst = LayerNorm(src) over each token's `hidden` values; dst may equal src.
+// ln_b may be null (a norm with weight alone).
+cudaError_t layer_norm(Dt dt, const void *src, void *dst, const float *ln_w, const float *ln_b, int tokens,
+                       int hidden, double eps, cudaStream_t s);
+cudaError_t pool_vectors(Dt dt, const void *x, const uint8_t *tok_live, const PoolItem *items, int count,
+                         int hidden, int output_dim, int normalize_l2, float *out, cudaStream_t s);
+// In place on qkv [tokens, 3 * hidden]: Q and K of each head rotated pair
+// (i, i + d/2) by the token's position.
+cudaError_t rope_qk(Dt dt, void *qkv, const int32_t *tok_pos, const float *cos, const float *sin, int tokens,
+                    int hidden, int head_dim, cudaStream_t s);
+
+// FFMA GEMM (any element type, F32 sums, one chain over k per output in
+// k order): the EXACT tier's, and the reference variant tests compare the
+// tensor-core GEMM with. EPI_ROPE is not taken here (rope_qk follows).
+cudaError_t gemm_simt(Dt dt, const void *a, int64_t lda, const void *w, int M, int N, int K,
+                      const Epilogue &epi, cudaStream_t s);
+
+// tcgen05 GEMM (F16/BF16 operands, F32 sums in TMEM) over TMA tensor maps
+// made by make_operand_map. Returns cudaErrorNotSupported for shapes it does
+// not take (K or N not a multiple of 8 / 32).
+struct TcMaps {
+    CUtensorMap a, w;
+    int bn = 256;
+};
+cudaError_t make_operand_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                             uint32_t box_rows, CUtensorMap *out);
+cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilogue &epi, int sms,
+                    int *fault, cudaStream_t s);
+
+// Attention within each row and head, Q/K/V read from qkv [tokens, 3h],
+// context written to ctx [tokens, h]. window < 0: whole row; else query i
+// reads keys j with |i - j| <= window.
+cudaError_t attention_f32(const float *qkv, float *ctx, const uint8_t *tok_live, const AttnItem *items,
+                          int n_items, int heads, int head_dim, int hidden, int window, int max_len,
+                          cudaStream_t s);
+cudaError_t attention_mma(Dt dt, const void *qkv, void *ctx, const uint8_t *tok_live, const AttnItem *items,
+                          int n_items, int heads, int head_dim, int hidden, int window, cudaStream_t s);
+// Query tile of attention_mma's items.
+constexpr int ATTN_MMA_QUERIES = 64;
+constexpr int ATTN_F32_QUERIES = 32;
+
+}  // namespace tb

@@ -1,0 +1,251 @@
+// rowwise.cu -- the HBM-bound kernels around the encoder's contractions:
+// embedding gather + LayerNorm, LayerNorm, RoPE on Q/K, and pooling fused
+// with the Matryoshka cut and L2 normalisation.
+//
+// Semantics follow the reference's CPU encoder (the definition the GPU must
+// match): lookup job.rs:114-131, LayerNorm rowwise.rs:10-29 (mean and
+// variance summed in F64, (y - mean) * inv rounded to F32, then * w + b),
+// pooling mod.rs:426-484 (mean in F32 in column order, 1/n as F32, cut
+// before L2, L2 norm in F64 with a 1e-12 floor).
+#include "kernels.h"
+
+namespace tb {
+namespace {
+
+constexpr int MAXV = 32;  // values per lane: hidden up to 1024
+
+// One warp per token: x = LN(word[id] + pos[p + offset] + type[ty]).
+template <class T>
+__global__ void __launch_bounds__(256) embed_ln_kernel(T *__restrict__ x, Packed p, const float *__restrict__ word,
+                                                       const float *__restrict__ pos, const float *__restrict__ type,
+                                                       int pos_offset, const float *__restrict__ ln_w,
+                                                       const float *__restrict__ ln_b, int h, double eps) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < p.tokens; t += warps) {
+        const float *wr = word + (int64_t)p.tok_id[t] * h;
+        const float *pr = pos ? pos + (int64_t)(p.tok_pos[t] + pos_offset) * h : nullptr;
+        const float *tr = type ? type + (int64_t)(p.tok_type ? p.tok_type[t] : 0) * h : nullptr;
+        float v[MAXV];
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            int c = lane + 32 * i;
+            v[i] = 0.0f;
+            if (c < h) {
+                float a = wr[c];
+                if (pr) a += pr[c];
+                if (tr) a += tr[c];
+                v[i] = a;
+                s += (double)a;
+            }
+        }
+        const double mean = warp_sum(s) / h;
+        double q = 0.0;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            int c = lane + 32 * i;
+            if (c < h) {
+                double d = (double)v[i] - mean;
+                q += d * d;
+            }
+        }
+        const double inv = 1.0 / sqrt(warp_sum(q) / h + (double)(float)eps);
+        T *out = x + (int64_t)t * h;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            int c = lane + 32 * i;
+            if (c < h) {
+                float z = (float)(((double)v[i] - mean) * inv);
+                st(out + c, z * ln_w[c] + (ln_b ? ln_b[c] : 0.0f));
+            }
+        }
+    }
+}
+
+template <class T>
+__global__ void __launch_bounds__(256) ln_kernel(const T *__restrict__ src, T *dst, const float *__restrict__ ln_w,
+                                                 const float *__restrict__ ln_b, int tokens, int h, double eps) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < tokens; t += warps) {
+        const T *in = src + (int64_t)t * h;
+        float v[MAXV];
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            int c = lane + 32 * i;
+            v[i] = c < h ? ld(in + c) : 0.0f;
+            s += (double)v[i];
+        }
+        const double mean = warp_sum(s) / h;
+        double q = 0.0;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            int c = lane + 32 * i;
+            if (c < h) {
+                double d = (double)v[i] - mean;
+                q += d * d;
+            }
+        }
+        const double inv = 1.0 / sqrt(warp_sum(q) / h + (double)(float)eps);
+        T *out = dst + (int64_t)t * h;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            int c = lane + 32 * i;
+            if (c < h) {
+                float z = (float)(((double)v[i] - mean) * inv);
+                st(out + c, z * ln_w[c] + (ln_b ? ln_b[c] : 0.0f));
+            }
+        }
+    }
+}
+
+// One block per output vector. Each thread owns columns tid, tid + blockDim,
+// .. of the cut and sums its tokens in column (position) order, as the
+// reference's mean does; L2 in F64 over the block.
+template <class T>
+__global__ void __launch_bounds__(256) pool_kernel(const T *__restrict__ x, const uint8_t *__restrict__ live,
+                                                   const PoolItem *__restrict__ items, int h, int od, int l2,
+                                                   float *__restrict__ out) {
+    constexpr int PER = 4;  // columns per thread: output_dim up to 1024
+    const PoolItem it = items[blockIdx.x];
+    float acc[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) acc[i] = 0.0f;
+    int n = 0;
+    for (int c = it.c0; c < it.c1; ++c) {
+        const int64_t tok = (int64_t)it.start + c;
+        if (it.live_only && !live[tok]) continue;
+        const T *row = x + tok * h;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            int j = threadIdx.x + i * blockDim.x;
+            if (j < od) acc[i] += ld(row + j);
+        }
+        ++n;
+    }
+    const float inv_n = 1.0f / (float)(n > 0 ? n : 1);
+    double sq = 0.0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        acc[i] *= inv_n;
+        int j = threadIdx.x + i * blockDim.x;
+        if (j < od) sq += (double)acc[i] * (double)acc[i];
+    }
+    float scale = 1.0f;
+    if (l2) {
+        __shared__ double part[32];
+        sq = warp_sum(sq);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            double v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0;
+            v = warp_sum(v);
+            if (threadIdx.x == 0) part[0] = v;
+        }
+        __syncthreads();
+        double norm = fmax(sqrt(part[0]), 1e-12);
+        scale = (float)(1.0 / norm);
+    }
+    float *dst = out + (int64_t)blockIdx.x * od;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        int j = threadIdx.x + i * blockDim.x;
+        if (j < od) dst[j] = l2 ? acc[i] * scale : acc[i];
+    }
+}
+
+// One thread per (token, part, pair): Q (part 0) and K (part 1) rotated.
+template <class T>
+__global__ void rope_kernel(T *qkv, const int32_t *__restrict__ tok_pos, const float *__restrict__ cos_t,
+                            const float *__restrict__ sin_t, int tokens, int h, int d) {
+    const int half = d / 2;
+    const int per_token = h;  // 2 parts x h/2 pairs
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)tokens * per_token) return;
+    const int t = (int)(i / per_token), r = (int)(i % per_token);
+    const int part = r / (h / 2), pr = r % (h / 2);
+    const int head = pr / half, k = pr % half;
+    T *base = qkv + (int64_t)t * 3 * h + part * h + head * d;
+    const int p = tok_pos[t];
+    const float c = cos_t[(int64_t)p * half + k], sn = sin_t[(int64_t)p * half + k];
+    const float x1 = ld(base + k), x2 = ld(base + k + half);
+    st(base + k, __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn)));
+    st(base + k + half, __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn)));
+}
+
+template <class T> __global__ void narrow_kernel(const float *__restrict__ src, T *__restrict__ dst, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = Elem<T>::from(src[i]);
+}
+
+int grid_for(int64_t warps_needed) {
+    int64_t blocks = (warps_needed + 7) / 8;
+    return (int)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+}
+
+}  // namespace
+
+cudaError_t narrow(Dt dt, const float *src, void *dst, int64_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    int g = (int)((n + 255) / 256 < 148 * 32 ? (n + 255) / 256 : 148 * 32);
+    if (dt == Dt::F16) narrow_kernel<__half><<<g, 256, 0, s>>>(src, (__half *)dst, n);
+    else if (dt == Dt::BF16) narrow_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(src, (__nv_bfloat16 *)dst, n);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t embed_layer_norm(Dt dt, void *x, const Packed &p, const float *word, const float *pos, const float *type,
+                             int pos_offset, const float *ln_w, const float *ln_b, int hidden, double eps,
+                             cudaStream_t s) {
+    if (hidden > 32 * MAXV) return cudaErrorInvalidValue;
+    if (p.tokens == 0) return cudaSuccess;
+    int g = grid_for(p.tokens);
+    switch (dt) {
+    case Dt::F32: embed_ln_kernel<float><<<g, 256, 0, s>>>((float *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps); break;
+    case Dt::F16: embed_ln_kernel<__half><<<g, 256, 0, s>>>((__half *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps); break;
+    case Dt::BF16: embed_ln_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((__nv_bfloat16 *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t layer_norm(Dt dt, const void *src, void *dst, const float *ln_w, const float *ln_b, int tokens, int hidden,
+                       double eps, cudaStream_t s) {
+    if (hidden > 32 * MAXV) return cudaErrorInvalidValue;
+    if (tokens == 0) return cudaSuccess;
+    int g = grid_for(tokens);
+    switch (dt) {
+    case Dt::F32: ln_kernel<float><<<g, 256, 0, s>>>((const float *)src, (float *)dst, ln_w, ln_b, tokens, hidden, eps); break;
+    case Dt::F16: ln_kernel<__half><<<g, 256, 0, s>>>((const __half *)src, (__half *)dst, ln_w, ln_b, tokens, hidden, eps); break;
+    case Dt::BF16: ln_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((const __nv_bfloat16 *)src, (__nv_bfloat16 *)dst, ln_w, ln_b, tokens, hidden, eps); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t pool_vectors(Dt dt, const void *x, const uint8_t *tok_live, const PoolItem *items, int count, int hidden,
+                         int output_dim, int normalize_l2, float *out, cudaStream_t s) {
+    if (output_dim > 1024 || output_dim > hidden) return cudaErrorInvalidValue;
+    if (count == 0) return cudaSuccess;
+    switch (dt) {
+    case Dt::F32: pool_kernel<float><<<count, 256, 0, s>>>((const float *)x, tok_live, items, hidden, output_dim, normalize_l2, out); break;
+    case Dt::F16: pool_kernel<__half><<<count, 256, 0, s>>>((const __half *)x, tok_live, items, hidden, output_dim, normalize_l2, out); break;
+    case Dt::BF16: pool_kernel<__nv_bfloat16><<<count, 256, 0, s>>>((const __nv_bfloat16 *)x, tok_live, items, hidden, output_dim, normalize_l2, out); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t rope_qk(Dt dt, void *qkv, const int32_t *tok_pos, const float *cos, const float *sin, int tokens, int hidden,
+                    int head_dim, cudaStream_t s) {
+    if (tokens == 0) return cudaSuccess;
+    int64_t n = (int64_t)tokens * hidden;
+    int g = (int)((n + 255) / 256);
+    switch (dt) {
+    case Dt::F32: rope_kernel<float><<<g, 256, 0, s>>>((float *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim); break;
+    case Dt::F16: rope_kernel<__half><<<g, 256, 0, s>>>((__half *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim); break;
+    case Dt::BF16: rope_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((__nv_bfloat16 *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim); break;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace tb
