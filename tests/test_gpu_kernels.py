@@ -34,6 +34,8 @@ def ref_gemm(dtype, epi, a, w, bias, y_in, head_dim=0, pos=None, cos=None, sin=N
     y = a64 @ w64.T + (0 if bias is None else bias.astype(np.float64))
     if epi == 1:
         y = gelu(y)
+    elif epi == 5:
+        y = 0.5 * y * (1 + np.tanh(np.sqrt(2 / np.pi) * (y + 0.044715 * y ** 3)))
     elif epi == 2:
         y = narrow(y_in, dtype).astype(np.float64) + y
     elif epi == 3:
@@ -56,7 +58,7 @@ SHAPES = [(128, 256, 64), (300, 768, 768), (77, 96, 32), (1000, 2304, 768), (257
 
 @pytest.mark.parametrize("dtype", [F16, BF16])
 @pytest.mark.parametrize("shape", SHAPES)
-@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3, 5])
 def test_tcgen05_gemm_epilogues(dtype, shape, epi):
     M, N, K = shape
     rng = np.random.default_rng(M * 7 + N + K + epi)
@@ -148,10 +150,47 @@ def test_mma_attention(dtype, case):
     live = (rng.random(T) > 0.15).astype(np.uint8)
     got = runtime.attention_check(dtype, 0, lens, qkv, live, heads, d, window)
     want = ref_attention(qkv, lens, live, heads, d, window)
-    assert np.abs(got - want).max() < (3e-2 if dtype == BF16 else 5e-3)
+    # Output rounding to BF16 (8 significant bits) or F16 (11) bounds the error relative to its scale.
+    assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
 
 
-@pytest.mark.parametrize("case", CASES)
+TC_CASES = [([128], 2, 64, -1), ([300, 5, 129], 12, 64, -1), ([500, 130], 2, 64, 64), ([1], 1, 64, -1),
+            ([513, 7, 256, 1000], 3, 64, -1), ([900, 200], 2, 64, 64), ([64, 33], 2, 64, 4)]
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+@pytest.mark.parametrize("case", TC_CASES)
+def test_tcgen05_attention(dtype, case):
+    lens, heads, d, window = case
+    T = sum(lens)
+    rng = np.random.default_rng(T + d + 5)
+    qkv = narrow(rng.standard_normal((T, 3 * heads * d)).astype(np.float32) * 2, dtype)
+    live = (rng.random(T) > 0.15).astype(np.uint8)
+    got = runtime.attention_check(dtype, 2, lens, qkv, live, heads, d, window)
+    want = ref_attention(qkv, lens, live, heads, d, window)
+    # Output rounding to BF16 (8 significant bits) or F16 (11) bounds the error relative to its scale.
+    assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+def test_tcgen05_attention_rescales_when_the_max_grows(dtype):
+    # Key magnitudes ramp up along the row, so later 64-key chunks raise
+    # the running max far past the first: O in tensor memory is rescaled.
+    lens, heads, d = [400, 70], 2, 64
+    T = sum(lens)
+    rng = np.random.default_rng(99)
+    qkv = rng.standard_normal((T, 3 * heads * d)).astype(np.float32)
+    ramp = np.concatenate([np.linspace(0.2, 6.0, n) for n in lens]).astype(np.float32)
+    qkv[:, heads * d:2 * heads * d] *= ramp[:, None]
+    qkv = narrow(qkv, dtype)
+    live = np.ones(T, np.uint8)
+    got = runtime.attention_check(dtype, 2, lens, qkv, live, heads, d, -1)
+    want = ref_attention(qkv, lens, live, heads, d, -1)
+    # Output rounding to BF16 (8 significant bits) or F16 (11) bounds the error relative to its scale.
+    assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
+
+
+@pytest.mark.parametrize("case", CASES + [([40, 9], 4, 8, -1), ([70], 2, 128, 10)])
 def test_f32_attention(case):
     lens, heads, d, window = case
     T = sum(lens)
@@ -161,3 +200,16 @@ def test_f32_attention(case):
     got = runtime.attention_check(F32, 1, lens, qkv, live, heads, d, window)
     want = ref_attention(qkv, lens, live, heads, d, window)
     assert np.abs(got - want).max() < 2e-5
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+def test_simt_attention_takes_other_head_widths(dtype):
+    lens, heads, d = [40, 9, 64], 4, 8
+    T = sum(lens)
+    rng = np.random.default_rng(8)
+    qkv = narrow(rng.standard_normal((T, 3 * heads * d)).astype(np.float32), dtype)
+    live = (rng.random(T) > 0.1).astype(np.uint8)
+    got = runtime.attention_check(dtype, 1, lens, qkv, live, heads, d, -1)
+    want = ref_attention(qkv, lens, live, heads, d, -1)
+    # Output rounding to BF16 (8 significant bits) or F16 (11) bounds the error relative to its scale.
+    assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)

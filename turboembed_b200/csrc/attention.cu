@@ -6,8 +6,9 @@
 // sliding window (|i - j| > window), scores -inf; softmax over the row's keys;
 // a query that reads no live key gets a zero context.
 //
-//  attention_f32: the EXACT tier. One warp per query, scores in shared
-//    memory, F32 throughout.
+//  attention_simt: one warp per query, scores in shared memory, F32 sums:
+//    the EXACT tier's, and the F16/BF16 one for head widths other than
+//    16, 32 and 64.
 //  attention_mma: F16/BF16 operands with F32 sums, flash-style: 64 queries a
 //    block (16 a warp), keys in chunks of 64 through a double-buffered
 //    cp.async ring, online softmax in base 2, mma.sync m16n8k16. Chunks
@@ -17,13 +18,14 @@
 namespace tb {
 namespace {
 
-// ---------------------------------------------------------------- F32 -------
+// --------------------------------------------------------------- SIMT -------
 
 constexpr int F32_WARPS = 4;
 
+template <class T>
 __global__ void __launch_bounds__(F32_WARPS * 32)
-attn_f32_kernel(const float *__restrict__ qkv, float *__restrict__ ctx, const uint8_t *__restrict__ live,
-                const AttnItem *__restrict__ items, int d, int h, int window, int lp) {
+attn_simt_kernel(const T *__restrict__ qkv, T *__restrict__ ctx, const uint8_t *__restrict__ live,
+                 const AttnItem *__restrict__ items, int d, int h, int window, int lp) {
     extern __shared__ float sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnItem it = items[blockIdx.x];
@@ -32,9 +34,9 @@ attn_f32_kernel(const float *__restrict__ qkv, float *__restrict__ ctx, const ui
     float *qs = sc + lp;
     const float scale = 1.0f / sqrtf((float)d);
     const int64_t ld = 3 * (int64_t)h;
-    const float *base = qkv + (int64_t)it.start * ld;
+    const T *base = qkv + (int64_t)it.start * ld;
     for (int qi = it.q0 + warp; qi < min(it.q0 + ATTN_F32_QUERIES, it.len); qi += F32_WARPS) {
-        for (int c = lane; c < d; c += 32) qs[c] = base[qi * ld + head * d + c];
+        for (int c = lane; c < d; c += 32) qs[c] = ::tb::ld(base + qi * ld + head * d + c);
         __syncwarp();
         int lo = 0, hi = it.len;
         if (window >= 0) {
@@ -43,17 +45,17 @@ attn_f32_kernel(const float *__restrict__ qkv, float *__restrict__ ctx, const ui
         }
         float mx = -INFINITY;
         for (int j = lo + lane; j < hi; j += 32) {
-            const float *k = base + j * ld + h + head * d;
+            const T *k = base + j * ld + h + head * d;
             float s = 0.0f;
-            for (int c = 0; c < d; ++c) s = fmaf(qs[c], k[c], s);
+            for (int c = 0; c < d; ++c) s = fmaf(qs[c], ::tb::ld(k + c), s);
             s = live[it.start + j] ? s * scale : -INFINITY;
             sc[j - lo] = s;
             mx = fmaxf(mx, s);
         }
         mx = warp_max(mx);
-        float *out = ctx + ((int64_t)it.start + qi) * h + head * d;
+        T *out = ctx + ((int64_t)it.start + qi) * h + head * d;
         if (mx == -INFINITY) {
-            for (int c = lane; c < d; c += 32) out[c] = 0.0f;
+            for (int c = lane; c < d; c += 32) st(out + c, 0.0f);
             __syncwarp();
             continue;
         }
@@ -68,8 +70,8 @@ attn_f32_kernel(const float *__restrict__ qkv, float *__restrict__ ctx, const ui
         __syncwarp();
         for (int c = lane; c < d; c += 32) {
             float acc = 0.0f;
-            for (int j = lo; j < hi; ++j) acc = fmaf(sc[j - lo] * inv, base[j * ld + 2 * h + head * d + c], acc);
-            out[c] = acc;
+            for (int j = lo; j < hi; ++j) acc = fmaf(sc[j - lo] * inv, ::tb::ld(base + j * ld + 2 * h + head * d + c), acc);
+            st(out + c, acc);
         }
         __syncwarp();
     }
@@ -291,22 +293,39 @@ cudaError_t launch_mma(const void *qkv, void *ctx, const uint8_t *live, const At
     return cudaGetLastError();
 }
 
-}  // namespace
 
-cudaError_t attention_f32(const float *qkv, float *ctx, const uint8_t *tok_live, const AttnItem *items, int n_items,
-                          int heads, int head_dim, int hidden, int window, int max_len, cudaStream_t s) {
-    if (n_items == 0) return cudaSuccess;
+template <class T>
+cudaError_t launch_simt(const void *qkv, void *ctx, const uint8_t *tok_live, const AttnItem *items, int n_items,
+                        int heads, int head_dim, int hidden, int window, int max_len, cudaStream_t s) {
     int lp = (max_len + 31) / 32 * 32;
     size_t smem = (size_t)F32_WARPS * (lp + 128) * sizeof(float);
     if (head_dim > 128) return cudaErrorNotSupported;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(attn_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(attn_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
     dim3 grid(n_items, heads);
-    attn_f32_kernel<<<grid, F32_WARPS * 32, smem, s>>>(qkv, ctx, tok_live, items, head_dim, hidden, window, lp);
+    attn_simt_kernel<T><<<grid, F32_WARPS * 32, smem, s>>>((const T *)qkv, (T *)ctx, tok_live, items, head_dim, hidden,
+                                                           window, lp);
     return cudaGetLastError();
 }
+
+}  // namespace
+
+cudaError_t attention_simt(Dt dt, const void *qkv, void *ctx, const uint8_t *tok_live, const AttnItem *items,
+                           int n_items, int heads, int head_dim, int hidden, int window, int max_len, cudaStream_t s) {
+    if (n_items == 0) return cudaSuccess;
+    switch (dt) {
+    case Dt::F32: return launch_simt<float>(qkv, ctx, tok_live, items, n_items, heads, head_dim, hidden, window, max_len, s);
+    case Dt::F16: return launch_simt<__half>(qkv, ctx, tok_live, items, n_items, heads, head_dim, hidden, window, max_len, s);
+    case Dt::BF16:
+        return launch_simt<__nv_bfloat16>(qkv, ctx, tok_live, items, n_items, heads, head_dim, hidden, window, max_len, s);
+    }
+    return cudaErrorNotSupported;
+}
+
+bool attention_mma_takes(int head_dim) { return head_dim == 16 || head_dim == 32 || head_dim == 64; }
+
 
 cudaError_t attention_mma(Dt dt, const void *qkv, void *ctx, const uint8_t *tok_live, const AttnItem *items,
                           int n_items, int heads, int head_dim, int hidden, int window, cudaStream_t s) {

@@ -195,7 +195,7 @@ struct Session {
     cudaEvent_t uploaded = nullptr;
     bool upload_pending = false;
     // GEMM operand maps over x, xn, ctx, ffn (box rows 128)
-    CUtensorMap map_x{}, map_xn{}, map_ctx{}, map_ffn{};
+    CUtensorMap map_x{}, map_xn{}, map_ctx{}, map_ffn{}, map_qkv{}, map_qkv64{};
     // the written state
     bool written = false;
     int tokens = 0, batch = 0, n_vectors = 0, n_attn = 0, max_len = 0;
@@ -495,9 +495,14 @@ int32_t tb_model_load(void *ctx, const turbo_backend_model *d, void **out, turbo
     if (h % 32 != 0 || h > 1024 || heads == 0 || h % heads != 0)
         return fail(err, TURBO_E_UNSUPPORTED, 0, "hidden %d with %d heads is not built", h, heads);
     const int dh = h / heads;
-    if (dh != 16 && dh != 32 && dh != 64)
-        return fail(err, TURBO_E_UNSUPPORTED, 0, "head width %d is not built (16, 32 or 64)", dh);
-    if (d->intermediate % 32 != 0) return fail(err, TURBO_E_UNSUPPORTED, 0, "intermediate %u", d->intermediate);
+    if (dh % 8 != 0 || dh > 128)
+        return fail(err, TURBO_E_UNSUPPORTED, 0, "head width %d is not built (a multiple of 8, at most 128)", dh);
+    if (modern && 64 % dh != 0)
+        return fail(err, TURBO_E_UNSUPPORTED, 0, "a rotary head width of %d is not built (16, 32 or 64)", dh);
+    // The tensor-core GEMM writes 32 columns at a time: the FFN-in product
+    // (intermediate wide, or twice that when gated) must be a multiple of 32.
+    if (d->intermediate % (modern ? 16 : 32) != 0)
+        return fail(err, TURBO_E_UNSUPPORTED, 0, "intermediate %u is not built", d->intermediate);
     if (modern && (d->struct_size < offsetof(turbo_backend_model, global_every) + 4 || !d->rope_table))
         return fail(err, TURBO_E_UNSUPPORTED, 0, "a rotary model needs the rope table");
     if (modern && (d->mlp != TURBO_MLP_GATED || d->rope_pairs * 2 != (uint32_t)dh))
@@ -674,6 +679,23 @@ PlanLayout plan_layout(int tokens, int vectors, int attn_items) {
     return L;
 }
 
+// The session's attention kernel: tcgen05 for head width 64 at F16/BF16,
+// mma.sync for 16 and 32, the SIMT kernel at EXACT and for other widths.
+enum class AttnKind { TC, MMA, SIMT };
+AttnKind attention_kind(const Session *s) {
+    const int dh = s->m->hidden / s->m->heads;
+    if (s->dt == Dt::F32) return AttnKind::SIMT;
+    if (dh == 64) return AttnKind::TC;
+    return attention_mma_takes(dh) ? AttnKind::MMA : AttnKind::SIMT;
+}
+int attention_queries(const Session *s) {
+    switch (attention_kind(s)) {
+    case AttnKind::TC: return ATTN_TC_QUERIES;
+    case AttnKind::MMA: return ATTN_MMA_QUERIES;
+    default: return ATTN_F32_QUERIES;
+    }
+}
+
 Dt resolve_dt(const Model *m, uint32_t precision) {
     if (precision == TURBO_PRECISION_EXACT) return Dt::F32;
     if (precision == TURBO_PRECISION_FASTEST) return m->dtype == TURBO_DTYPE_BF16 ? Dt::BF16 : Dt::F16;
@@ -713,7 +735,7 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
     if (cap > (int64_t)1 << 30) return fail(err, TURBO_E_CAPACITY, 1, "max_batch x max_seq too large");
     s->cap_tokens = (int)cap;
     s->cap_vectors = std::max(s->max_batch, s->max_ranges);
-    const int qt = dt == Dt::F32 ? ATTN_F32_QUERIES : ATTN_MMA_QUERIES;
+    const int qt = attention_queries(s.get());
     s->max_attn_items = (int)(cap / qt) + s->max_batch + 1;
     s->lay = plan_layout(s->cap_tokens, s->cap_vectors, s->max_attn_items);
     const int h = m->hidden, I = m->inter;
@@ -756,6 +778,8 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         if (e == cudaSuccess) e = make_operand_map(dt, s->ctxb, rows, h, h, 128, &s->map_ctx);
         if (e == cudaSuccess) e = make_operand_map(dt, s->ffn, rows, I, I, 128, &s->map_ffn);
         if (e == cudaSuccess && m->modern) e = make_operand_map(dt, s->xn, rows, h, h, 128, &s->map_xn);
+        if (e == cudaSuccess) e = make_operand_map(dt, s->qkv, rows, 3 * h, 3 * h, 128, &s->map_qkv);
+        if (e == cudaSuccess) e = make_operand_map(dt, s->qkv, rows, 3 * h, 3 * h, 64, &s->map_qkv64);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return cuda_fail(err, e, "session_open");
@@ -877,7 +901,7 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
         }
     }
     // Attention work: query tiles of each row, the longest rows first.
-    const int qt = s->dt == Dt::F32 ? ATTN_F32_QUERIES : ATTN_MMA_QUERIES;
+    const int qt = attention_queries(s);
     std::vector<int> order(r->batch);
     for (uint32_t b = 0; b < r->batch; ++b) order[b] = (int)b;
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return s->row_len[a] > s->row_len[b]; });
@@ -970,9 +994,13 @@ cudaError_t encode(Session *s) {
     WeightSet &ws = m->set(dt);
     cudaError_t e;
     auto attention_raw = [&](int window) -> cudaError_t {
-        if (dt == Dt::F32)
-            return attention_f32((const float *)s->qkv, (float *)s->ctxb, pk.tok_live, items, s->n_attn, m->heads, dh, h,
-                                 window, s->max_len, st);
+        const AttnKind kind = attention_kind(s);
+        if (kind == AttnKind::TC)
+            return attention_tc(dt, s->map_qkv, s->map_qkv64, s->ctxb, pk.tok_live, items, s->n_attn, m->heads, dh, h, window,
+                                s->ctx->fault_dev, st);
+        if (kind == AttnKind::SIMT)
+            return attention_simt(dt, s->qkv, s->ctxb, pk.tok_live, items, s->n_attn, m->heads, dh, h, window,
+                                  s->max_len, st);
         return attention_mma(dt, s->qkv, s->ctxb, pk.tok_live, items, s->n_attn, m->heads, dh, h, window, st);
     };
     auto attention = [&](int window) -> cudaError_t {
@@ -992,7 +1020,10 @@ cudaError_t encode(Session *s) {
             if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T)) != cudaSuccess) return e;
             if ((e = layer_norm(dt, s->x, s->x, L.ln1_w, L.ln1_b, T, h, m->eps, st)) != cudaSuccess) return e;
             Epilogue f1;
-            f1.kind = EPI_GELU, f1.bias = L.ffn_in.bias, f1.out = s->ffn, f1.ldo = I;
+            // FASTEST takes the tanh form, as the reference's FASTEST does;
+            // EXACT and MODEL keep the erf form the CPU path computes.
+            f1.kind = s->precision == TURBO_PRECISION_FASTEST ? EPI_GELU_TANH : EPI_GELU;
+            f1.bias = L.ffn_in.bias, f1.out = s->ffn, f1.ldo = I;
             if ((e = linear(s, &s->map_x, s->x, L.ffn_in, f1, T)) != cudaSuccess) return e;
             Epilogue f2;
             f2.kind = EPI_RESIDUAL, f2.bias = L.ffn_out.bias, f2.out = s->x, f2.ldo = h;

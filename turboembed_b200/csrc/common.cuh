@@ -72,4 +72,18 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+// GELU in its tanh form, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
+// on the hardware tanh: what the reference's FASTEST tier computes by
+// default (core/cuda/kernels.cu:162, backend.cpp:1575-1582). Within about
+// 1e-3 of the erf form; used only on F16/BF16 sessions.
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+    return 0.5f * x * (1.0f + tanh_approx(u));
+}
+
 }  // namespace tb

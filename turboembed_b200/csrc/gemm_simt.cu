@@ -21,6 +21,7 @@ template <class T>
 __device__ __forceinline__ void epilogue_store(const Epilogue &e, int r, int c, float v) {
     T *y = (T *)e.out + (int64_t)r * e.ldo + c;
     if (e.kind == EPI_GELU) v = gelu_erf(v);
+    if (e.kind == EPI_GELU_TANH) v = gelu_tanh(v);
     if (e.kind == EPI_RESIDUAL) v = ld(y) + v;
     st(y, v);
 }

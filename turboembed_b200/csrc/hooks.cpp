@@ -164,7 +164,7 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
     const int h = (int)(heads * head_dim);
     std::vector<AttnItem> items;
     int T = 0, max_len = 0;
-    const int qt = variant == 0 ? ATTN_MMA_QUERIES : ATTN_F32_QUERIES;
+    const int qt = variant == 0 ? ATTN_MMA_QUERIES : variant == 2 ? ATTN_TC_QUERIES : ATTN_F32_QUERIES;
     for (uint32_t b = 0; b < batch; ++b) {
         for (int q0 = 0; q0 < lens[b]; q0 += qt) items.push_back(AttnItem{T, lens[b], q0, 0});
         T += lens[b];
@@ -181,13 +181,21 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
         if (e == cudaSuccess) e = cudaMemcpy(di, items.data(), items.size() * sizeof(AttnItem), cudaMemcpyHostToDevice);
     }
     if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "attention_check setup", e);
+    int *fault = (int *)dv.get(4);
     if (variant == 0) e = attention_mma(dt, dq, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, 0);
-    else if (dt == Dt::F32)
-        e = attention_f32((const float *)dq, (float *)dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window,
-                          max_len, 0);
-    else return hook_fail(err, TURBO_E_UNSUPPORTED, "the F32 attention takes F32", cudaSuccess);
+    else if (variant == 2) {
+        CUtensorMap map, map64;
+        e = make_operand_map(dt, dq, (uint64_t)T, (uint64_t)3 * h, (uint64_t)3 * h, 128, &map);
+        if (e == cudaSuccess) e = make_operand_map(dt, dq, (uint64_t)T, (uint64_t)3 * h, (uint64_t)3 * h, 64, &map64);
+        if (e == cudaSuccess)
+            e = attention_tc(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, fault, 0);
+    }
+    else e = attention_simt(dt, dq, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, max_len, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "attention_check", e);
+    int f = 0;
+    cudaMemcpy(&f, fault, 4, cudaMemcpyDeviceToHost);
+    if (f) return hook_fail(err, TURBO_E_RUNTIME, "attention_check: the kernel's fault word is set", cudaSuccess);
     widen_host(dt, dc, ctx_out, (size_t)T * h);
     if (err) err->code = 0, err->message[0] = 0;
     return TURBO_OK;

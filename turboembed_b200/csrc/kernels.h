@@ -19,6 +19,7 @@ enum EpiKind : int {
     EPI_RESIDUAL = 2,  // y += acc + b (the residual stream, in place)
     EPI_GATED = 3,     // y[:, j] = act(acc[:, 2j] + b) * (acc[:, 2j+1] + b): weights interleaved
     EPI_ROPE = 4,      // as STORE, then Q and K columns (< rope_cols) rotated by position
+    EPI_GELU_TANH = 5, // y = gelu_tanh(acc + b): the FASTEST tier's GELU
 };
 
 struct Epilogue {
@@ -98,12 +99,25 @@ cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilog
 // Attention within each row and head, Q/K/V read from qkv [tokens, 3h],
 // context written to ctx [tokens, h]. window < 0: whole row; else query i
 // reads keys j with |i - j| <= window.
-cudaError_t attention_f32(const float *qkv, float *ctx, const uint8_t *tok_live, const AttnItem *items,
-                          int n_items, int heads, int head_dim, int hidden, int window, int max_len,
-                          cudaStream_t s);
+// The SIMT attention (F32 sums, any element type, head width up to 128):
+// the EXACT tier's, and the F16/BF16 one for head widths the tensor-core
+// kernel does not take (attention_mma_takes).
+cudaError_t attention_simt(Dt dt, const void *qkv, void *ctx, const uint8_t *tok_live, const AttnItem *items,
+                           int n_items, int heads, int head_dim, int hidden, int window, int max_len,
+                           cudaStream_t s);
+bool attention_mma_takes(int head_dim);
 cudaError_t attention_mma(Dt dt, const void *qkv, void *ctx, const uint8_t *tok_live, const AttnItem *items,
                           int n_items, int heads, int head_dim, int hidden, int window, cudaStream_t s);
-// Query tile of attention_mma's items.
+// tcgen05 flash attention for head width 64 (F16/BF16): Q comes through a
+// TMA map over qkv [tokens, 3h] with [128 x 64] boxes, K and V through one
+// with [64 x 64] boxes (make_operand_map with box_rows 128 and 64); items of
+// 128 queries.
+cudaError_t attention_tc(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_map, void *ctx,
+                         const uint8_t *tok_live, const AttnItem *items, int n_items, int heads, int head_dim,
+                         int hidden, int window, int *fault, cudaStream_t s);
+
+// Query tile of each attention kernel's items.
+constexpr int ATTN_TC_QUERIES = 128;
 constexpr int ATTN_MMA_QUERIES = 64;
 constexpr int ATTN_F32_QUERIES = 32;
 

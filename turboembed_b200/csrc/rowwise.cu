@@ -7,6 +7,8 @@
 // variance summed in F64, (y - mean) * inv rounded to F32, then * w + b),
 // pooling mod.rs:426-484 (mean in F32 in column order, 1/n as F32, cut
 // before L2, L2 norm in F64 with a 1e-12 floor).
+#include <type_traits>
+
 #include "kernels.h"
 
 namespace tb {
@@ -63,39 +65,81 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(T *__restrict__ x, Packed
     }
 }
 
-template <class T>
-__global__ void __launch_bounds__(256) ln_kernel(const T *__restrict__ src, T *dst, const float *__restrict__ ln_w,
-                                                 const float *__restrict__ ln_b, int tokens, int h, double eps) {
-    const int lane = threadIdx.x & 31;
-    const int warps = (gridDim.x * blockDim.x) >> 5;
-    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < tokens; t += warps) {
-        const T *in = src + (int64_t)t * h;
-        float v[MAXV];
-        double s = 0.0;
+// 16 bytes of T as floats: 8 halves/bf16s or 4 floats.
+template <class T> struct Vec {
+    static constexpr int N = 16 / sizeof(T);
+    __device__ __forceinline__ static void load(const T *p, float *v) {
+        uint4 u = *reinterpret_cast<const uint4 *>(p);
+        if constexpr (sizeof(T) == 4) {
+            v[0] = __uint_as_float(u.x), v[1] = __uint_as_float(u.y), v[2] = __uint_as_float(u.z), v[3] = __uint_as_float(u.w);
+        } else {
+            uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int i = 0; i < MAXV; ++i) {
-            int c = lane + 32 * i;
-            v[i] = c < h ? ld(in + c) : 0.0f;
-            s += (double)v[i];
-        }
-        const double mean = warp_sum(s) / h;
-        double q = 0.0;
-#pragma unroll
-        for (int i = 0; i < MAXV; ++i) {
-            int c = lane + 32 * i;
-            if (c < h) {
-                double d = (double)v[i] - mean;
-                q += d * d;
+            for (int j = 0; j < 4; ++j) {
+                float2 f = unpack2<T>(w[j]);
+                v[2 * j] = f.x, v[2 * j + 1] = f.y;
             }
         }
-        const double inv = 1.0 / sqrt(warp_sum(q) / h + (double)(float)eps);
+    }
+    __device__ __forceinline__ static void store(T *p, const float *v) {
+        uint4 u;
+        if constexpr (sizeof(T) == 4) {
+            u.x = __float_as_uint(v[0]), u.y = __float_as_uint(v[1]), u.z = __float_as_uint(v[2]), u.w = __float_as_uint(v[3]);
+        } else {
+            u.x = pack2<T>(v[0], v[1]), u.y = pack2<T>(v[2], v[3]), u.z = pack2<T>(v[4], v[5]), u.w = pack2<T>(v[6], v[7]);
+        }
+        *reinterpret_cast<uint4 *>(p) = u;
+    }
+};
+
+// One warp per token, 16-byte accesses: lane l holds chunks l, l + 32, ..
+// of the row. Sums in F64 at F32 (the EXACT tier, as the reference's
+// LayerNorm sums), in F32 at F16/BF16.
+template <class T, int CPL>
+__global__ void __launch_bounds__(256) ln_vec_kernel(const T *__restrict__ src, T *dst, const float *__restrict__ ln_w,
+                                                     const float *__restrict__ ln_b, int tokens, int h, double eps) {
+    using V = Vec<T>;
+    using Acc = typename std::conditional<sizeof(T) == 4, double, float>::type;
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    const int chunks = h / V::N;
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < tokens; t += warps) {
+        const T *in = src + (int64_t)t * h;
+        float v[CPL][V::N];
+        Acc s = 0;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+                V::load(in + c * V::N, v[i]);
+#pragma unroll
+                for (int j = 0; j < V::N; ++j) s += (Acc)v[i][j];
+            }
+        }
+        const Acc mean = warp_sum(s) / (Acc)h;
+        Acc q = 0;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i)
+            if (lane + 32 * i < chunks)
+#pragma unroll
+                for (int j = 0; j < V::N; ++j) {
+                    const Acc d = (Acc)v[i][j] - mean;
+                    q += d * d;
+                }
+        const Acc inv = (Acc)1 / sqrt(warp_sum(q) / (Acc)h + (Acc)(float)eps);
         T *out = dst + (int64_t)t * h;
 #pragma unroll
-        for (int i = 0; i < MAXV; ++i) {
-            int c = lane + 32 * i;
-            if (c < h) {
-                float z = (float)(((double)v[i] - mean) * inv);
-                st(out + c, z * ln_w[c] + (ln_b ? ln_b[c] : 0.0f));
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+                float o[V::N];
+#pragma unroll
+                for (int j = 0; j < V::N; ++j) {
+                    const int col = c * V::N + j;
+                    const float z = (float)(((Acc)v[i][j] - mean) * inv);
+                    o[j] = z * ln_w[col] + (ln_b ? ln_b[col] : 0.0f);
+                }
+                V::store(out + c * V::N, o);
             }
         }
     }
@@ -210,17 +254,31 @@ cudaError_t embed_layer_norm(Dt dt, void *x, const Packed &p, const float *word,
     return cudaGetLastError();
 }
 
+template <class T>
+cudaError_t ln_launch(const void *src, void *dst, const float *w, const float *b, int tokens, int h, double eps,
+                      cudaStream_t s) {
+    const int chunks = h / Vec<T>::N, cpl = (chunks + 31) / 32;
+    const int g = grid_for(tokens);
+    const T *in = (const T *)src;
+    T *out = (T *)dst;
+    if (cpl <= 1) ln_vec_kernel<T, 1><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
+    else if (cpl <= 2) ln_vec_kernel<T, 2><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
+    else if (cpl <= 4) ln_vec_kernel<T, 4><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
+    else if (cpl <= 8) ln_vec_kernel<T, 8><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
 cudaError_t layer_norm(Dt dt, const void *src, void *dst, const float *ln_w, const float *ln_b, int tokens, int hidden,
                        double eps, cudaStream_t s) {
-    if (hidden > 32 * MAXV) return cudaErrorInvalidValue;
+    if (hidden > 32 * MAXV || hidden % 8 != 0) return cudaErrorInvalidValue;
     if (tokens == 0) return cudaSuccess;
-    int g = grid_for(tokens);
     switch (dt) {
-    case Dt::F32: ln_kernel<float><<<g, 256, 0, s>>>((const float *)src, (float *)dst, ln_w, ln_b, tokens, hidden, eps); break;
-    case Dt::F16: ln_kernel<__half><<<g, 256, 0, s>>>((const __half *)src, (__half *)dst, ln_w, ln_b, tokens, hidden, eps); break;
-    case Dt::BF16: ln_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((const __nv_bfloat16 *)src, (__nv_bfloat16 *)dst, ln_w, ln_b, tokens, hidden, eps); break;
+    case Dt::F32: return ln_launch<float>(src, dst, ln_w, ln_b, tokens, hidden, eps, s);
+    case Dt::F16: return ln_launch<__half>(src, dst, ln_w, ln_b, tokens, hidden, eps, s);
+    case Dt::BF16: return ln_launch<__nv_bfloat16>(src, dst, ln_w, ln_b, tokens, hidden, eps, s);
     }
-    return cudaGetLastError();
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t pool_vectors(Dt dt, const void *x, const uint8_t *tok_live, const PoolItem *items, int count, int hidden,
