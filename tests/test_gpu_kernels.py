@@ -53,7 +53,8 @@ def ref_gemm(dtype, epi, a, w, bias, y_in, head_dim=0, pos=None, cos=None, sin=N
     return y
 
 
-SHAPES = [(128, 256, 64), (300, 768, 768), (77, 96, 32), (1000, 2304, 768), (257, 384, 1536), (129, 3072, 768)]
+SHAPES = [(128, 256, 64), (300, 768, 768), (77, 96, 32), (1000, 2304, 768), (257, 384, 1536), (129, 3072, 768),
+          (2000, 768, 3072), (513, 512, 128)]
 
 
 @pytest.mark.parametrize("dtype", [F16, BF16])
@@ -70,6 +71,9 @@ def test_tcgen05_gemm_epilogues(dtype, shape, epi):
     want = ref_gemm(dtype, epi, a, w, bias, y_in)
     tol = 8e-3 if dtype == BF16 else 1.5e-3
     assert rel_err(got, want) < tol
+    # Single-CTA tiles give the same sums in the same order: the same bits.
+    one = runtime.gemm_check(dtype, 2, epi, a, w, bias, y_in)
+    assert np.array_equal(got, one)
     # The FFMA kernel on the same narrowed operands agrees as closely.
     simt = runtime.gemm_check(dtype, 1, epi, a, w, bias, y_in)
     assert rel_err(got, simt) < tol

@@ -133,8 +133,9 @@ struct Linear {
     void *w = nullptr;
     const float *bias = nullptr;
     int n = 0, k = 0;
-    CUtensorMap map{};  // W's TMA map (narrowed sets only), box rows = bn
+    CUtensorMap map{};  // W's TMA map (narrowed sets only), boxes of 128 rows
     int bn = 256;
+    bool pair = false;  // 256 x 256 tiles on CTA pairs (N a multiple of 256)
 };
 
 struct LayerWeights {
@@ -196,6 +197,8 @@ struct Session {
     bool upload_pending = false;
     // GEMM operand maps over x, xn, ctx, ffn (box rows 128)
     CUtensorMap map_x{}, map_xn{}, map_ctx{}, map_ffn{}, map_qkv{}, map_qkv64{};
+    // TMA store maps of the GEMM outputs x, qkv and ffn ([32 x 32] boxes)
+    CUtensorMap out_x{}, out_qkv{}, out_ffn{};
     // the written state
     bool written = false;
     int tokens = 0, batch = 0, n_vectors = 0, n_attn = 0, max_len = 0;
@@ -645,8 +648,9 @@ cudaError_t narrowed(Model *m, Dt dt) {
         e = narrow(dt, src, dst, (int64_t)L.n * L.k, s);
         if (e != cudaSuccess) return e;
         L.w = dst;
-        L.bn = L.n % 256 == 0 ? 256 : 128;
-        return make_operand_map(dt, dst, L.n, L.k, L.k, L.bn, &L.map);
+        L.pair = L.n % 256 == 0;
+        L.bn = L.pair ? 256 : 128;
+        return make_operand_map(dt, dst, L.n, L.k, L.k, 128, &L.map);
     };
     for (LayerWeights &L : ws.layers) {
         for (Linear *x : {&L.qkv, &L.out, &L.ffn_in, &L.ffn_out}) {
@@ -780,6 +784,9 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         if (e == cudaSuccess && m->modern) e = make_operand_map(dt, s->xn, rows, h, h, 128, &s->map_xn);
         if (e == cudaSuccess) e = make_operand_map(dt, s->qkv, rows, 3 * h, 3 * h, 128, &s->map_qkv);
         if (e == cudaSuccess) e = make_operand_map(dt, s->qkv, rows, 3 * h, 3 * h, 64, &s->map_qkv64);
+        if (e == cudaSuccess) e = make_store_map(dt, s->x, rows, h, h, &s->out_x);
+        if (e == cudaSuccess) e = make_store_map(dt, s->qkv, rows, 3 * h, 3 * h, &s->out_qkv);
+        if (e == cudaSuccess) e = make_store_map(dt, s->ffn, rows, I, I, &s->out_ffn);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return cuda_fail(err, e, "session_open");
@@ -956,7 +963,7 @@ template <class F> cudaError_t timed(Session *s, int kind, double flops, F launc
 // One GEMM of the layer loop: the tensor-core kernel on F16/BF16 sessions,
 // the FFMA kernel on F32 ones.
 cudaError_t linear_launch(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi,
-                          int M) {
+                          int M, const CUtensorMap *out_map) {
     if (s->dt == Dt::F32) {
         if (epi.kind == EPI_ROPE) {
             Epilogue e2 = epi;
@@ -971,11 +978,18 @@ cudaError_t linear_launch(Session *s, const CUtensorMap *amap, const void *a, co
     maps.a = *amap;
     maps.w = L.map;
     maps.bn = L.bn;
+    maps.pair = L.pair;
+    if (out_map) {
+        maps.out = *out_map;
+        maps.has_out = true;
+    }
     return gemm_tc(s->dt, maps, M, L.n, L.k, epi, s->ctx->sms, s->ctx->fault_dev, s->ctx->stream);
 }
 
-cudaError_t linear(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi, int M) {
-    return timed(s, 0, 2.0 * M * L.n * L.k, [&] { return linear_launch(s, amap, a, L, epi, M); });
+// out_map: the output's TMA store map, or null for direct stores.
+cudaError_t linear(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi, int M,
+                   const CUtensorMap *out_map = nullptr) {
+    return timed(s, 0, 2.0 * M * L.n * L.k, [&] { return linear_launch(s, amap, a, L, epi, M, out_map); });
 }
 
 cudaError_t encode(Session *s) {
@@ -1013,21 +1027,21 @@ cudaError_t encode(Session *s) {
             const LayerWeights &L = ws.layers[l];
             Epilogue q;
             q.kind = EPI_STORE, q.bias = L.qkv.bias, q.out = s->qkv, q.ldo = 3 * h;
-            if ((e = linear(s, &s->map_x, s->x, L.qkv, q, T)) != cudaSuccess) return e;
+            if ((e = linear(s, &s->map_x, s->x, L.qkv, q, T, &s->out_qkv)) != cudaSuccess) return e;
             if ((e = attention(-1)) != cudaSuccess) return e;
             Epilogue o;
             o.kind = EPI_RESIDUAL, o.bias = L.out.bias, o.out = s->x, o.ldo = h;
-            if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T)) != cudaSuccess) return e;
+            if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
             if ((e = layer_norm(dt, s->x, s->x, L.ln1_w, L.ln1_b, T, h, m->eps, st)) != cudaSuccess) return e;
             Epilogue f1;
             // FASTEST takes the tanh form, as the reference's FASTEST does;
             // EXACT and MODEL keep the erf form the CPU path computes.
             f1.kind = s->precision == TURBO_PRECISION_FASTEST ? EPI_GELU_TANH : EPI_GELU;
             f1.bias = L.ffn_in.bias, f1.out = s->ffn, f1.ldo = I;
-            if ((e = linear(s, &s->map_x, s->x, L.ffn_in, f1, T)) != cudaSuccess) return e;
+            if ((e = linear(s, &s->map_x, s->x, L.ffn_in, f1, T, &s->out_ffn)) != cudaSuccess) return e;
             Epilogue f2;
             f2.kind = EPI_RESIDUAL, f2.bias = L.ffn_out.bias, f2.out = s->x, f2.ldo = h;
-            if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T)) != cudaSuccess) return e;
+            if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) return e;
             if ((e = layer_norm(dt, s->x, s->x, L.ln2_w, L.ln2_b, T, h, m->eps, st)) != cudaSuccess) return e;
         }
         return cudaSuccess;
@@ -1054,14 +1068,14 @@ cudaError_t encode(Session *s) {
         if ((e = attention(global ? -1 : m->window)) != cudaSuccess) return e;
         Epilogue o;
         o.kind = EPI_RESIDUAL, o.out = s->x, o.ldo = h;
-        if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T)) != cudaSuccess) return e;
+        if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
         if ((e = layer_norm(dt, s->x, s->xn, L.ln2_w, nullptr, T, h, m->eps, st)) != cudaSuccess) return e;
         Epilogue g;
         g.kind = EPI_GATED, g.out = s->ffn, g.ldo = I, g.act = m->act;
         if ((e = linear(s, &s->map_xn, s->xn, L.ffn_in, g, T)) != cudaSuccess) return e;
         Epilogue f2;
         f2.kind = EPI_RESIDUAL, f2.out = s->x, f2.ldo = h;
-        if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T)) != cudaSuccess) return e;
+        if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) return e;
     }
     (void)es;
     return layer_norm(dt, s->x, s->x, m->final_w, nullptr, T, h, m->eps, st);

@@ -36,20 +36,25 @@ namespace {
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
 using namespace tc;
 
-template <int BN> struct Cfg {
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
+template <int BN, bool PAIR> struct Cfg {
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // W rows this CTA loads a stage
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : 5;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int MAX_BIAS = 4096;  // the bias vector, staged in shared memory once per CTA
+    // Output staging for TMA stores: two [32 x 32] 16-bit tiles per epilogue warp.
+    static constexpr int STORE_BYTES = 8 * 2 * 2048;
+    // ring | barriers (padded to 1 KB) | store staging | bias
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + STORE_BYTES + MAX_BIAS * 4 + 1024;
 };
 
 // Instruction descriptor of kind::f16: F32 accumulator, A and B the same
 // 16-bit type (fmt 0 F16, 1 BF16), both K-major, M = 128, N = BN.
-template <int BN> __host__ __device__ constexpr uint32_t instr_desc(uint32_t fmt) {
-    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+template <int TM, int BN> __host__ __device__ constexpr uint32_t instr_desc(uint32_t fmt) {
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
 }
 
 // 32 values of T from/to 16-byte-aligned memory.
@@ -80,11 +85,162 @@ template <class T, int NV> __device__ __forceinline__ void store_n(T *p, const f
     }
 }
 
-template <class T, int BN, int EPI_WG>
+// One output tile's epilogue for one warp: its 32 TMEM lanes (rows) and
+// COLS columns from tbase. `release` hands the accumulator back to the MMA
+// warp; it is called right after the last TMEM read, before the last
+// columns' math and stores.
+// Stores go straight from registers, or, with `out_map`, through the warp's
+// two [32 x 32] staging tiles in shared memory (64-byte swizzle) and a TMA
+// store issued by lane 0; `nstore` counts the warp's staged chunks.
+struct StoreStage {
+    bool tma;      // false: direct stores
+    uint8_t *buf;  // this warp's 4 KB
+    int row0;      // the warp's first row
+    uint32_t nstore;
+};
+
+template <class T, int COLS, class Release>
+__device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
+                                              bool row_ok, int col_base, int N, const uint4 *res, StoreStage &ss,
+                                              const CUtensorMap *out_map, Release release) {
+    if (e.kind == EPI_ROPE) {
+        // 64 columns at a time: whole heads of width 16, 32 or 64.
+#pragma unroll 1
+        for (int c = 0; c < COLS; c += 64) {
+            const int col = col_base + c;
+            float v[64];
+            __syncwarp();
+            tmem_ld32(tbase + c, v);
+            tmem_ld32(tbase + c + 32, v + 32);
+            if (c + 64 >= COLS) release();
+            if (col >= N) continue;
+            if (e.bias)
+#pragma unroll
+                for (int i = 0; i < 64; ++i) v[i] += (col + i < N) ? bias_s[col + i] : 0.0f;
+            if (row_ok && col < e.rope_cols) {
+                const int d = e.head_dim, half = d >> 1;
+                const float *cs = e.cos + (int64_t)e.tok_pos[row] * half;
+                const float *sn = e.sin + (int64_t)e.tok_pos[row] * half;
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const int seg = i - (i % d), k = i % d;
+                    if (k < half && col + seg < e.rope_cols) {
+                        const float x1 = v[i], x2 = v[i + half];
+                        v[i] = __fsub_rn(__fmul_rn(x1, cs[k]), __fmul_rn(x2, sn[k]));
+                        v[i + half] = __fadd_rn(__fmul_rn(x2, cs[k]), __fmul_rn(x1, sn[k]));
+                    }
+                }
+            }
+            if (row_ok) {
+                T *y = (T *)e.out + (int64_t)row * e.ldo + col;
+                store_n<T, 32>(y, v);
+                if (col + 32 < N) store_n<T, 32>(y + 32, v + 32);
+            }
+        }
+        return;
+    }
+    // Two 32-column chunks per TMEM round trip.
+#pragma unroll
+    for (int c2 = 0; c2 < COLS; c2 += 64) {
+        uint32_t raw[2][32];
+        __syncwarp();
+        tmem_ld32_async(tbase + c2, raw[0]);
+        if (c2 + 32 < COLS) tmem_ld32_async(tbase + c2 + 32, raw[1]);
+        tmem_wait_ld();
+        if (c2 + 64 >= COLS) release();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int c = c2 + hh * 32;
+            const int col = col_base + c;
+            if (c >= COLS || col >= N) continue;
+            if (!row_ok && (e.kind == EPI_GATED || !ss.tma)) continue;
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[hh][i]);
+            if (e.bias) {
+                const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float4 bb = b4[i];
+                    v[4 * i] += bb.x;
+                    v[4 * i + 1] += bb.y;
+                    v[4 * i + 2] += bb.z;
+                    v[4 * i + 3] += bb.w;
+                }
+            }
+            if (e.kind == EPI_GATED) {
+                float o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float g = v[2 * i];
+                    o[i] = (e.act == 2 ? silu(g) : gelu_erf(g)) * v[2 * i + 1];
+                }
+                store_n<T, 16>((T *)e.out + (int64_t)row * e.ldo + col / 2, o);
+                continue;
+            }
+            T *y = (T *)e.out + (int64_t)row * e.ldo + col;
+            if (e.kind == EPI_GELU) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+            } else if (e.kind == EPI_GELU_TANH) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+            } else if (e.kind == EPI_RESIDUAL && row_ok) {
+                // This chunk's residual, loaded before the accumulator was ready.
+                const uint4 *rq = res + (c / 32) * 4;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t w4[4] = {rq[i].x, rq[i].y, rq[i].z, rq[i].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = unpack2<T>(w4[j]);
+                        v[8 * i + 2 * j] += f.x;
+                        v[8 * i + 2 * j + 1] += f.y;
+                    }
+                }
+            }
+            if (!ss.tma) {
+                store_n<T, 32>(y, v);
+                continue;
+            }
+            // Lane l writes row l: 16-byte chunk q at q ^ ((l >> 1) & 3), the
+            // TMA 64-byte swizzle, which spreads each store over all banks.
+            const int lane = threadIdx.x & 31;
+            uint8_t *buf = ss.buf + (ss.nstore & 1) * 2048;
+            if (lane == 0) tma_store_wait_read<1>();  // the store two chunks back is done reading buf
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 u;
+                u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+                u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+                u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+                u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+                *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = u;
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(out_map, smem_u32(buf), col, ss.row0);
+                tma_store_commit();
+            }
+            ++ss.nstore;
+        }
+    }
+}
+
+// PAIR = false: one CTA computes a 128 x BN tile. PAIR = true: a cluster of
+// two CTAs computes a 256 x BN tile with tcgen05.mma.cta_group::2: each CTA
+// loads its own 128 rows of A and BN/2 rows of W (no multicast), the
+// leader (rank 0) issues the MMAs for both, and each CTA's TMEM holds its
+// 128 rows of the product.
+template <class T, int BN, int EPI_WG, bool PAIR>
 __global__ void __launch_bounds__(128 + 128 * EPI_WG, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
-               Epilogue e, int *fault) {
-    using C = Cfg<BN>;
+gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
+               const __grid_constant__ CUtensorMap tout, int use_tma_store, int M, int N, int K, Epilogue e,
+               int *fault) {
+    using C = Cfg<BN, PAIR>;
+    constexpr int TM = PAIR ? 2 * BM : BM;  // rows a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *bars = smem + C::STAGES * C::STAGE_BYTES;
@@ -92,8 +248,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     const uint32_t tfull0 = empty0 + 8 * C::STAGES, tempty0 = tfull0 + 16;
     uint32_t *tmem_slot = (uint32_t *)(bars + 16 * C::STAGES + 32);
     volatile int *abort_flag = (volatile int *)(bars + 16 * C::STAGES + 40);
+    uint8_t *staging = bars + 1024;
+    float *bias_s = (float *)(staging + C::STORE_BYTES);
+    for (int i = threadIdx.x; i < N && e.bias; i += blockDim.x) bias_s[i] = e.bias[i];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_rank() : 0;
+    const bool leader = rank == 0;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
@@ -101,22 +264,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, 4 * EPI_WG);
+            mbar_init(tempty0 + 8 * a, (PAIR ? 2 : 1) * 4 * EPI_WG);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (warp == 2) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"((uint32_t)C::TMEM_COLS));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"((uint32_t)C::TMEM_COLS));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"((uint32_t)C::TMEM_COLS));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before anyone signals them
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+    const int m_tiles = (M + TM - 1) / TM, n_tiles = (N + BN - 1) / BN;
     const int tiles = m_tiles * n_tiles, kblocks = (K + BK - 1) / BK;
 
     if (warp == 0) {
@@ -124,29 +294,41 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+            for (int tile = unit; tile < tiles && ok; tile += units) {
+                const int m0 = (tile / n_tiles) * TM + (int)rank * BM;
+                const int n0 = (tile % n_tiles) * BN + (int)rank * C::B_ROWS;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, fault)) {
                         ok = false;
                         break;
                     }
                     const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
-                    mbar_expect_tx(full0 + 8 * stage, C::STAGE_BYTES);
-                    tma_load_2d(sa, &ta, kb * BK, m0, full0 + 8 * stage);
-                    tma_load_2d(sa + C::A_BYTES, &tw, kb * BK, n0, full0 + 8 * stage);
+                    const uint32_t fb = full0 + 8 * stage;
+                    if constexpr (PAIR) {
+                        // Both CTAs' bytes complete on the leader's barrier.
+                        if (leader) mbar_expect_tx(fb, 2 * C::STAGE_BYTES);
+                        const uint32_t fb0 = mapa(fb, 0);
+                        tma_load_2d_pair(sa, &ta, kb * BK, m0, fb0);
+                        tma_load_2d_pair(sa + C::A_BYTES, &tw, kb * BK, n0, fb0);
+                    } else {
+                        mbar_expect_tx(fb, C::STAGE_BYTES);
+                        tma_load_2d(sa, &ta, kb * BK, m0, fb);
+                        tma_load_2d(sa + C::A_BYTES, &tw, kb * BK, n0, fb);
+                    }
                     if (++stage == C::STAGES) stage = 0, phase ^= 1;
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = instr_desc<BN>(Elem<T>::dt == Dt::BF16 ? 1u : 0u);
+        if (lane == 0 && leader) {
+            const uint32_t idesc = instr_desc<TM, BN>(Elem<T>::dt == Dt::BF16 ? 1u : 0u);
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, fault)) break;
+            for (int tile = unit; tile < tiles && ok; tile += units) {
+                const bool freed = PAIR ? mbar_wait_cluster(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, fault)
+                                        : mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, fault);
+                if (!freed) break;
                 tc_fence_after();
                 const uint32_t d = tmem + acc * BN;
                 for (int kb = 0; kb < kblocks; ++kb) {
@@ -158,121 +340,73 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                     const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
                     const uint64_t da = smem_desc(sa), db = smem_desc(sa + C::A_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
-                        umma_f16(d, da + (uint64_t)(kk * UMMA_K * 2 / 16), db + (uint64_t)(kk * UMMA_K * 2 / 16),
-                                 idesc, (kb | kk) ? 1u : 0u);
-                    umma_commit(empty0 + 8 * stage);
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                        const uint64_t off = (uint64_t)(kk * UMMA_K * 2 / 16);
+                        if constexpr (PAIR) umma_f16_pair(d, da + off, db + off, idesc, (kb | kk) ? 1u : 0u);
+                        else umma_f16(d, da + off, db + off, idesc, (kb | kk) ? 1u : 0u);
+                    }
+                    if constexpr (PAIR) umma_commit_pair(empty0 + 8 * stage);
+                    else umma_commit(empty0 + 8 * stage);
                     if (++stage == C::STAGES) stage = 0, phase ^= 1;
                 }
                 if (!ok) break;
-                umma_commit(tfull0 + 8 * acc);
+                if constexpr (PAIR) umma_commit_pair(tfull0 + 8 * acc);
+                else umma_commit(tfull0 + 8 * acc);
                 if (++acc == 2) acc = 0, acc_phase ^= 1;
             }
         }
     } else if (warp >= 4) {
         const int ew = warp - 4, quad = warp & 3, part = ew >> 2;
         constexpr int COLS = BN / EPI_WG;  // this warp's columns of a tile
+        const uint32_t tempty_leader = PAIR ? mapa(tempty0, 0) : tempty0;
+        const bool tma_out = use_tma_store && (e.kind == EPI_STORE || e.kind == EPI_GELU ||
+                                               e.kind == EPI_GELU_TANH || e.kind == EPI_RESIDUAL);
+        StoreStage ss{tma_out, staging + ew * 4096, 0, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
-            if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, fault)) break;
-            tc_fence_after();
+        for (int tile = unit; tile < tiles; tile += units) {
+            const int m0 = (tile / n_tiles) * TM + (int)rank * BM, n0 = (tile % n_tiles) * BN;
             const int row = m0 + quad * 32 + lane;
             const bool row_ok = row < M;
-            const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + part * COLS;
-            if (e.kind == EPI_ROPE) {
-                // 64 columns at a time: whole heads of width 16, 32 or 64.
-#pragma unroll 1
-                for (int c = 0; c < COLS; c += 64) {
-                    const int col = n0 + part * COLS + c;
-                    if (col >= N) break;
-                    float v[64];
-                    __syncwarp();
-                    tmem_ld32(tbase + c, v);
-                    if (col + 32 < N) tmem_ld32(tbase + c + 32, v + 32);
-                    else
+            const int col_base = n0 + part * COLS;
+            // The residual rows of this warp's columns, fetched while the
+            // mainloop still runs: one memory round trip a tile.
+            uint4 res[COLS / 32 * 4];
+            if (e.kind == EPI_RESIDUAL && row_ok) {
 #pragma unroll
-                        for (int i = 32; i < 64; ++i) v[i] = 0.0f;
-                    if (e.bias)
+                for (int c = 0; c < COLS / 32; ++c) {
+                    const int col = col_base + c * 32;
+                    const uint4 *src = reinterpret_cast<const uint4 *>((const T *)e.out + (int64_t)row * e.ldo + col);
 #pragma unroll
-                        for (int i = 0; i < 64; ++i) v[i] += (col + i < N) ? e.bias[col + i] : 0.0f;
-                    if (row_ok && col < e.rope_cols) {
-                        const int d = e.head_dim, half = d >> 1;
-                        const float *cs = e.cos + (int64_t)e.tok_pos[row] * half;
-                        const float *sn = e.sin + (int64_t)e.tok_pos[row] * half;
-#pragma unroll
-                        for (int i = 0; i < 64; ++i) {
-                            const int seg = i - (i % d), k = i % d;
-                            if (k < half && col + seg < e.rope_cols) {
-                                const float x1 = v[i], x2 = v[i + half];
-                                v[i] = __fsub_rn(__fmul_rn(x1, cs[k]), __fmul_rn(x2, sn[k]));
-                                v[i + half] = __fadd_rn(__fmul_rn(x2, cs[k]), __fmul_rn(x1, sn[k]));
-                            }
-                        }
-                    }
-                    if (row_ok) {
-                        T *y = (T *)e.out + (int64_t)row * e.ldo + col;
-                        store_n<T, 32>(y, v);
-                        if (col + 32 < N) store_n<T, 32>(y + 32, v + 32);
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < COLS; c += 32) {
-                    const int col = n0 + part * COLS + c;
-                    if (col >= N) break;
-                    float v[32];
-                    __syncwarp();
-                    tmem_ld32(tbase + c, v);
-                    if (e.bias) {
-                        const float4 *b4 = reinterpret_cast<const float4 *>(e.bias + col);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            float4 b = b4[i];
-                            v[4 * i] += b.x;
-                            v[4 * i + 1] += b.y;
-                            v[4 * i + 2] += b.z;
-                            v[4 * i + 3] += b.w;
-                        }
-                    }
-                    if (!row_ok) continue;
-                    if (e.kind == EPI_GATED) {
-                        float o[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float g = v[2 * i];
-                            o[i] = (e.act == 2 ? silu(g) : gelu_erf(g)) * v[2 * i + 1];
-                        }
-                        store_n<T, 16>((T *)e.out + (int64_t)row * e.ldo + col / 2, o);
-                        continue;
-                    }
-                    T *y = (T *)e.out + (int64_t)row * e.ldo + col;
-                    if (e.kind == EPI_GELU) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-                    } else if (e.kind == EPI_GELU_TANH) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
-                    } else if (e.kind == EPI_RESIDUAL) {
-                        float r[32];
-                        load32<T>(y, r);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] += r[i];
-                    }
-                    store_n<T, 32>(y, v);
+                    for (int i = 0; i < 4; ++i) res[c * 4 + i] = col < N ? src[i] : make_uint4(0, 0, 0, 0);
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
+            if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, fault)) break;
+            tc_fence_after();
+            const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + part * COLS;
+            const int a_now = acc;
+            ss.row0 = m0 + quad * 32;
+            epilogue_tile<T, COLS>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, [&]() {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (PAIR) mbar_arrive_cluster(tempty_leader + 8 * a_now);
+                    else mbar_arrive(tempty0 + 8 * a_now);
+                }
+            });
             if (++acc == 2) acc = 0, acc_phase ^= 1;
         }
+        if (ss.tma && lane == 0) tma_store_wait<0>();  // every store written before the CTA leaves
     }
-    __syncthreads();
+    tc_fence_before();
+    if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal it
+    else __syncthreads();
     if (warp == 2) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS));
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS));
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS));
     }
 }
 
@@ -288,22 +422,38 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <class T, int BN, int EPI_WG>
+template <class T, int BN, int EPI_WG, bool PAIR>
 cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
-    using C = Cfg<BN>;
-    auto kern = gemm_tc_kernel<T, BN, EPI_WG>;
+    using C = Cfg<BN, PAIR>;
+    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (err != cudaSuccess) return err;
-    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    const int grid = tiles < sms ? tiles : sms;
-    kern<<<grid, 128 + 128 * EPI_WG, C::SMEM, s>>>(maps.a, maps.w, M, N, K, e, fault);
-    return cudaGetLastError();
+    const int TM = PAIR ? 2 * BM : BM;
+    const int tiles = ((M + TM - 1) / TM) * ((N + BN - 1) / BN);
+    const int units = PAIR ? sms / 2 : sms;
+    const int grid_units = tiles < units ? tiles : units;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(PAIR ? 2 * grid_units : grid_units);
+    cfg.blockDim = dim3(128 + 128 * EPI_WG);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (PAIR) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, maps.a, maps.w, maps.out, maps.has_out ? 1 : 0, M, N, K, e, fault);
 }
 
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
-    if (maps.bn == 256) return launch<T, 256, 2>(maps, M, N, K, e, sms, fault, s);
-    return launch<T, 128, 2>(maps, M, N, K, e, sms, fault, s);
+    if (maps.pair) return launch<T, 256, 2, true>(maps, M, N, K, e, sms, fault, s);
+    if (maps.bn == 256) return launch<T, 256, 2, false>(maps, M, N, K, e, sms, fault, s);
+    return launch<T, 128, 2, false>(maps, M, N, K, e, sms, fault, s);
 }
 
 }  // namespace
@@ -324,11 +474,27 @@ cudaError_t make_operand_map(Dt dt, const void *ptr, uint64_t rows, uint64_t col
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t make_store_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems, CUtensorMap *out) {
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    if (dt == Dt::F32 || (ld_elems * 2) % 16 != 0 || ((uintptr_t)ptr & 15) != 0) return cudaErrorInvalidValue;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld_elems * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(out, dt == Dt::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilogue &epi, int sms, int *fault,
                     cudaStream_t s) {
     if (M == 0) return cudaSuccess;
     if (N % 32 != 0 || K % 8 != 0 || (maps.bn != 128 && maps.bn != 256)) return cudaErrorNotSupported;
     if (epi.kind == EPI_ROPE && (epi.head_dim > 64 || 64 % epi.head_dim != 0)) return cudaErrorNotSupported;
+    if (epi.bias && N > Cfg<256, false>::MAX_BIAS) return cudaErrorNotSupported;
+    if (maps.pair && maps.bn != 256) return cudaErrorNotSupported;
     if (dt == Dt::F16) return dispatch<__half>(maps, M, N, K, epi, sms, fault, s);
     if (dt == Dt::BF16) return dispatch<__nv_bfloat16>(maps, M, N, K, epi, sms, fault, s);
     return cudaErrorNotSupported;

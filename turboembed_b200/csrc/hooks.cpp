@@ -93,7 +93,7 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t vari
                                                    const float *sin_t, uint32_t positions, turbo_error *err) {
     Dt dt;
     if (!dt_of(dtype, &dt)) return hook_fail(err, TURBO_E_INVALID_ENUM, "dtype", cudaSuccess);
-    if (variant == 0 && dt == Dt::F32) return hook_fail(err, TURBO_E_UNSUPPORTED, "tcgen05 takes F16/BF16", cudaSuccess);
+    if (variant != 1 && dt == Dt::F32) return hook_fail(err, TURBO_E_UNSUPPORTED, "tcgen05 takes F16/BF16", cudaSuccess);
     Dev dv;
     cudaError_t e = cudaSuccess;
     const size_t out_cols = epi == EPI_GATED ? N / 2 : N;
@@ -127,11 +127,19 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t vari
     ep.tok_pos = dpos;
     ep.head_dim = (int)head_dim;
     ep.rope_cols = (int)(2 * (N / 3));
-    if (variant == 0) {
+    if (variant == 0 || variant == 2) {
+        // 0: the backend's choice (CTA pairs when N is a multiple of 256);
+        // 2: one CTA a 128 x BN tile.
         TcMaps maps;
         maps.bn = N % 256 == 0 ? 256 : 128;
+        maps.pair = variant == 0 && N % 256 == 0;
         e = make_operand_map(dt, da, M, K, K, 128, &maps.a);
-        if (e == cudaSuccess) e = make_operand_map(dt, dw, N, K, K, maps.bn, &maps.w);
+        if (e == cudaSuccess) e = make_operand_map(dt, dw, N, K, K, maps.pair ? 128 : maps.bn, &maps.w);
+        // Variant 0 stores through TMA as the backend does; 2 directly.
+        if (e == cudaSuccess && variant == 0) {
+            e = make_store_map(dt, dy, M, out_cols, out_cols, &maps.out);
+            maps.has_out = true;
+        }
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
         if (e == cudaSuccess) e = gemm_tc(dt, maps, (int)M, (int)N, (int)K, ep, sms, fault, 0);

@@ -87,10 +87,19 @@ cudaError_t gemm_simt(Dt dt, const void *a, int64_t lda, const void *w, int M, i
 // tcgen05 GEMM (F16/BF16 operands, F32 sums in TMEM) over TMA tensor maps
 // made by make_operand_map. Returns cudaErrorNotSupported for shapes it does
 // not take (K or N not a multiple of 8 / 32).
+// pair = true runs 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2):
+// then bn is 256 and W's map has boxes of 128 rows (each CTA loads half).
+// out (with has_out) is a map over the output made by make_store_map: the
+// store, GELU and residual epilogues then write through TMA stores.
 struct TcMaps {
-    CUtensorMap a, w;
+    CUtensorMap a, w, out;
     int bn = 256;
+    bool pair = false;
+    bool has_out = false;
 };
+// A TMA map for GEMM outputs: [32 x 32] boxes, 64-byte swizzle.
+cudaError_t make_store_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                           CUtensorMap *out);
 cudaError_t make_operand_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                              uint32_t box_rows, CUtensorMap *out);
 cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilogue &epi, int sms,

@@ -103,43 +103,65 @@ __global__ void __launch_bounds__(256) ln_vec_kernel(const T *__restrict__ src, 
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int chunks = h / V::N;
-    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < tokens; t += warps) {
-        const T *in = src + (int64_t)t * h;
-        float v[CPL][V::N];
-        Acc s = 0;
+    // The weights and biases of this lane's chunks, read once per warp.
+    float w[CPL][V::N], b[CPL][V::N];
 #pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-            const int c = lane + 32 * i;
-            if (c < chunks) {
-                V::load(in + c * V::N, v[i]);
+    for (int i = 0; i < CPL; ++i) {
+        const int c = lane + 32 * i;
 #pragma unroll
-                for (int j = 0; j < V::N; ++j) s += (Acc)v[i][j];
+        for (int j = 0; j < V::N; ++j) {
+            w[i][j] = c < chunks ? ln_w[c * V::N + j] : 0.0f;
+            b[i][j] = (c < chunks && ln_b) ? ln_b[c * V::N + j] : 0.0f;
+        }
+    }
+    // Two tokens an iteration, both rows' loads issued before either's sums,
+    // so each warp keeps twice the bytes in flight.
+    for (int t0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t0 < tokens; t0 += 2 * warps) {
+        const int tk[2] = {t0, t0 + warps};
+        float v[2][CPL][V::N];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (tk[u] >= tokens) continue;
+            const T *in = src + (int64_t)tk[u] * h;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                const int c = lane + 32 * i;
+                if (c < chunks) V::load(in + c * V::N, v[u][i]);
             }
         }
-        const Acc mean = warp_sum(s) / (Acc)h;
-        Acc q = 0;
 #pragma unroll
-        for (int i = 0; i < CPL; ++i)
-            if (lane + 32 * i < chunks)
+        for (int u = 0; u < 2; ++u) {
+            if (tk[u] >= tokens) continue;
+            Acc s = 0;
 #pragma unroll
-                for (int j = 0; j < V::N; ++j) {
-                    const Acc d = (Acc)v[i][j] - mean;
-                    q += d * d;
+            for (int i = 0; i < CPL; ++i)
+                if (lane + 32 * i < chunks)
+#pragma unroll
+                    for (int j = 0; j < V::N; ++j) s += (Acc)v[u][i][j];
+            const Acc mean = warp_sum(s) / (Acc)h;
+            Acc q = 0;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i)
+                if (lane + 32 * i < chunks)
+#pragma unroll
+                    for (int j = 0; j < V::N; ++j) {
+                        const Acc d = (Acc)v[u][i][j] - mean;
+                        q += d * d;
+                    }
+            const Acc inv = (Acc)1 / sqrt(warp_sum(q) / (Acc)h + (Acc)(float)eps);
+            T *out = dst + (int64_t)tk[u] * h;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                const int c = lane + 32 * i;
+                if (c < chunks) {
+                    float o[V::N];
+#pragma unroll
+                    for (int j = 0; j < V::N; ++j) {
+                        const float z = (float)(((Acc)v[u][i][j] - mean) * inv);
+                        o[j] = z * w[i][j] + b[i][j];
+                    }
+                    V::store(out + c * V::N, o);
                 }
-        const Acc inv = (Acc)1 / sqrt(warp_sum(q) / (Acc)h + (Acc)(float)eps);
-        T *out = dst + (int64_t)t * h;
-#pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-            const int c = lane + 32 * i;
-            if (c < chunks) {
-                float o[V::N];
-#pragma unroll
-                for (int j = 0; j < V::N; ++j) {
-                    const int col = c * V::N + j;
-                    const float z = (float)(((Acc)v[i][j] - mean) * inv);
-                    o[j] = z * ln_w[col] + (ln_b ? ln_b[col] : 0.0f);
-                }
-                V::store(out + c * V::N, o);
             }
         }
     }
@@ -263,6 +285,7 @@ cudaError_t ln_launch(const void *src, void *dst, const float *w, const float *b
     T *out = (T *)dst;
     if (cpl <= 1) ln_vec_kernel<T, 1><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
     else if (cpl <= 2) ln_vec_kernel<T, 2><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
+    else if (cpl <= 3) ln_vec_kernel<T, 3><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
     else if (cpl <= 4) ln_vec_kernel<T, 4><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
     else if (cpl <= 8) ln_vec_kernel<T, 8><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
     else return cudaErrorInvalidValue;
