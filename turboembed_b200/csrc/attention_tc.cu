@@ -9,23 +9,28 @@
 // the tcgen05 counterpart of the reference's FASTEST attention_fa_kernel
 // (core/cuda/kernels.cu:4142, mma.sync m16n8k16).
 //
-// One CTA per (row, head, 128-query tile), 160 threads, four CTAs per SM
-// (48 KB shared memory and 128 TMEM columns each), keys in chunks of 64:
+// Persistent CTAs, four per SM (48 KB shared memory, 128 TMEM columns each),
+// 160 threads, looping over work units (row, 128-query tile, head); keys in
+// chunks of 64:
 //   warp 4, lane 0   TMA loads ([rows x 64] boxes of the packed qkv buffer,
 //                    128-byte swizzle: Q 128 rows, K and V 64) and every MMA:
 //                    S = Q K^T (M 128, N 64, K 64) into TMEM columns 0..63,
 //                    O += P V (M 128, N 64, K 64) into columns 64..127, V
-//                    read MN-major.
+//                    read MN-major. The next unit's Q and first K/V chunk
+//                    are loaded while the current unit's last chunk is still
+//                    in the softmax.
 //   warps 0..3       the softmax: thread r owns query row r (TMEM lane r):
 //                    pass 1 reads S for the row max, pass 2 reads it again
 //                    and writes P = 2^(s log2e/sqrt(d) - m_ref) as F16/BF16
 //                    straight into the swizzled shared-memory A operand of
-//                    the P V product, summing the row.
-// O accumulates in TMEM across chunks. Its reference max m_ref moves only
-// when a chunk's max passes it by more than 8 (log2 units): then O (after
-// the previous P V is done) and the row sum are rescaled in place. P stays
-// below 2^8, and the result is exact either way since O and the row sum
-// share m_ref. Waits are bounded (2 s) and end in the fault word.
+//                    the P V product, summing the row. A chunk whose keys are
+//                    all live and in range takes a path without masks.
+// O accumulates in TMEM across a unit's chunks. Its reference max m_ref
+// moves only when a chunk's max passes it by more than 8 (log2 units): then
+// O (after the previous P V is done) and the row sum are rescaled in place.
+// P stays below 2^8, and the result is exact either way since O and the row
+// sum share m_ref. Barrier phases run on across units (chunk and unit
+// counters). Waits are bounded (2 s) and end in the fault word.
 #include "kernels.h"
 #include "tcgen05.cuh"
 
@@ -39,6 +44,7 @@ constexpr int Q_BYTES = QT * D * 2;   // 16 KB
 constexpr int KV_BYTES = KT * D * 2;  // 8 KB
 constexpr int P_BYTES = QT * KT * 2;  // 16 KB
 constexpr int SMEM = Q_BYTES + 2 * KV_BYTES + P_BYTES + 256 + 1024;
+constexpr int CTAS_PER_SM = 4;
 constexpr float RESCALE = 8.0f;  // log2 units
 
 __device__ __forceinline__ float ex2(float x) {
@@ -53,11 +59,21 @@ __host__ __device__ constexpr uint32_t idesc(uint32_t fmt, int n, bool b_mn_majo
            ((uint32_t)(128 >> 4) << 24);
 }
 
+// Keys [klo, khi) a query tile of a row reads.
+__device__ __forceinline__ void key_range(const AttnItem &it, int window, int &klo, int &khi) {
+    klo = 0;
+    khi = it.len;
+    if (window >= 0) {
+        klo = max(0, it.q0 - window);
+        khi = min(it.len, it.q0 + QT - 1 + window + 1);
+    }
+}
+
 template <class T>
-__global__ void __launch_bounds__(160, 4)
+__global__ void __launch_bounds__(160, CTAS_PER_SM)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv, T *__restrict__ ctx,
-               const uint8_t *__restrict__ live, const AttnItem *__restrict__ items, int h, int window,
-               float scale_log2, int *fault) {
+               const uint8_t *__restrict__ live, const AttnItem *__restrict__ items, int n_items, int heads, int h,
+               int window, float scale_log2, int *fault) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sQ = smem, *sP = smem + Q_BYTES, *sK = sP + P_BYTES, *sV = sK + KV_BYTES;
@@ -68,14 +84,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     volatile int *abort_flag = (volatile int *)(bars + 56);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const AttnItem it = items[blockIdx.x];
-    const int head = blockIdx.y;
-    int klo = 0, khi = it.len;
-    if (window >= 0) {
-        klo = max(0, it.q0 - window);
-        khi = min(it.len, it.q0 + QT - 1 + window + 1);
-    }
-    const int nch = (khi - klo + KT - 1) / KT;
+    const int units = n_items * heads;
 
     if (threadIdx.x == 0) {
         mbar_init(bar_q, 1);
@@ -99,18 +108,29 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     const uint32_t fmt = Elem<T>::dt == Dt::BF16 ? 1u : 0u;
 
     if (warp == 4) {
-        if (lane == 0 && nch > 0) {
-            const int xq = head * D, xk = h + head * D, xv = 2 * h + head * D;
-            const int row0 = it.start;
+        if (lane == 0) {
             const uint32_t ids = idesc(fmt, KT, false), idpv = idesc(fmt, D, true);
             const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sP);
-            mbar_expect_tx(bar_q, Q_BYTES);
-            tma_load_2d(aq, &tq, xq, row0 + it.q0, bar_q);
-            mbar_expect_tx(bar_k, KV_BYTES);
-            tma_load_2d(ak, &tkv, xk, row0 + klo, bar_k);
-            mbar_expect_tx(bar_v, KV_BYTES);
-            tma_load_2d(av, &tkv, xv, row0 + klo, bar_v);
-            bool ok = mbar_wait(bar_q, 0, abort_flag, fault) && mbar_wait(bar_k, 0, abort_flag, fault);
+            // Loads of a unit's Q, or of chunk j's K / V.
+            auto load_q = [&](int u) {
+                const AttnItem it = items[u / heads];
+                mbar_expect_tx(bar_q, Q_BYTES);
+                tma_load_2d(aq, &tq, (u % heads) * D, it.start + it.q0, bar_q);
+            };
+            auto load_k = [&](int u, int j) {
+                const AttnItem it = items[u / heads];
+                int klo, khi;
+                key_range(it, window, klo, khi);
+                mbar_expect_tx(bar_k, KV_BYTES);
+                tma_load_2d(ak, &tkv, h + (u % heads) * D, it.start + klo + j * KT, bar_k);
+            };
+            auto load_v = [&](int u, int j) {
+                const AttnItem it = items[u / heads];
+                int klo, khi;
+                key_range(it, window, klo, khi);
+                mbar_expect_tx(bar_v, KV_BYTES);
+                tma_load_2d(av, &tkv, 2 * h + (u % heads) * D, it.start + klo + j * KT, bar_v);
+            };
             auto issue_s = [&]() {
                 tc_fence_after();
 #pragma unroll
@@ -119,132 +139,171 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                              kk > 0 ? 1u : 0u);
                 umma_commit(bar_s);
             };
-            if (ok) issue_s();
-            for (int j = 0; j < nch && ok; ++j) {
-                const uint32_t par = j & 1;
-                // S_j done: K is free for the next chunk.
-                if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
-                if (j + 1 < nch) {
-                    mbar_expect_tx(bar_k, KV_BYTES);
-                    tma_load_2d(ak, &tkv, xk, row0 + klo + (j + 1) * KT, bar_k);
-                }
-                // P_j written (S_j read, O rescaled) by the softmax; V_j loaded.
-                if (!(ok = mbar_wait(bar_p, par, abort_flag, fault))) break;
-                if (!(ok = mbar_wait(bar_v, par, abort_flag, fault))) break;
-                tc_fence_after();
+            uint32_t g = 0, qc = 0;  // chunks and units done so far
+            bool ok = true;
+            int u = blockIdx.x;
+            if (u < units) {
+                load_q(u);
+                load_k(u, 0);
+                load_v(u, 0);
+            }
+            for (; u < units && ok; u += gridDim.x, ++qc) {
+                const AttnItem it = items[u / heads];
+                int klo, khi;
+                key_range(it, window, klo, khi);
+                const int nch = (khi - klo + KT - 1) / KT;
+                const int next = u + gridDim.x;
+                if (!(ok = mbar_wait(bar_q, qc & 1, abort_flag, fault))) break;
+                if (!(ok = mbar_wait(bar_k, g & 1, abort_flag, fault))) break;
+                issue_s();
+                for (int j = 0; j < nch && ok; ++j, ++g) {
+                    const uint32_t par = g & 1;
+                    // S done: K (and, after the last chunk, Q) are free.
+                    if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
+                    if (j + 1 < nch) load_k(u, j + 1);
+                    else if (next < units) {
+                        load_q(next);
+                        load_k(next, 0);
+                    }
+                    // P written (S read, O rescaled) by the softmax; V loaded.
+                    if (!(ok = mbar_wait(bar_p, par, abort_flag, fault))) break;
+                    if (!(ok = mbar_wait(bar_v, par, abort_flag, fault))) break;
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < KT / 16; ++kk)
-                    // A = P [128 q x 64 keys] K-major; B = V [64 keys x 64 d] MN-major, 16 keys a step.
-                    umma_f16(tmem + 64, smem_desc(ap) + (uint64_t)(kk * 2), smem_desc(av + kk * 16 * 128), idpv,
-                             (j | kk) ? 1u : 0u);
-                umma_commit(bar_o);
-                if (j + 1 < nch) {
-                    if (!(ok = mbar_wait(bar_k, (j + 1) & 1, abort_flag, fault))) break;
-                    issue_s();
-                }
-                // P V_j done: V and P are free.
-                if (!(ok = mbar_wait(bar_o, par, abort_flag, fault))) break;
-                if (j + 1 < nch) {
-                    mbar_expect_tx(bar_v, KV_BYTES);
-                    tma_load_2d(av, &tkv, xv, row0 + klo + (j + 1) * KT, bar_v);
+                    for (int kk = 0; kk < KT / 16; ++kk)
+                        // A = P [128 q x 64 keys] K-major; B = V [64 keys x 64 d] MN-major, 16 keys a step.
+                        umma_f16(tmem + 64, smem_desc(ap) + (uint64_t)(kk * 2), smem_desc(av + kk * 16 * 128), idpv,
+                                 (j | kk) ? 1u : 0u);
+                    umma_commit(bar_o);
+                    if (j + 1 < nch) {
+                        if (!(ok = mbar_wait(bar_k, (g + 1) & 1, abort_flag, fault))) break;
+                        issue_s();
+                    }
+                    // P V done: V and P are free.
+                    if (!(ok = mbar_wait(bar_o, par, abort_flag, fault))) break;
+                    if (j + 1 < nch) load_v(u, j + 1);
+                    else if (next < units) load_v(next, 0);
                 }
             }
         }
     } else {
         // Softmax: thread r = query row r = TMEM lane r.
         const int r = threadIdx.x;
-        const int qi = it.q0 + r;
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        float m_ref = -INFINITY, l = 0.0f;
+        uint32_t g = 0;
         bool ok = true;
-        for (int j = 0; j < nch && ok; ++j) {
-            const uint32_t par = j & 1;
-            const int k0 = klo + j * KT;
-            // The chunk's key flags: lane l of every warp loads 2 of them.
-            uint32_t km0, km1;
-            {
-                int key = k0 + lane;
-                km0 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
-                key += 32;
-                km1 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
-            }
-            if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
-            tc_fence_after();
-            // Pass 1: the row max of the chunk's valid scores.
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int half = 0; half < 2; ++half) {
-                float sv[32];
-                __syncwarp();
-                tmem_ld32(lane_base + half * 32, sv);
-                const uint32_t km = half ? km1 : km0;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    bool valid = (km >> i) & 1u;
-                    if (window >= 0) valid = valid && abs(qi - (k0 + half * 32 + i)) <= window;
-                    if (valid) mx = fmaxf(mx, sv[i] * scale_log2);
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const AttnItem it = items[u / heads];
+            const int head = u % heads;
+            int klo, khi;
+            key_range(it, window, klo, khi);
+            const int nch = (khi - klo + KT - 1) / KT;
+            const int qi = it.q0 + r;
+            float m_ref = -INFINITY, l = 0.0f;
+            for (int j = 0; j < nch && ok; ++j, ++g) {
+                const uint32_t par = g & 1;
+                const int k0 = klo + j * KT;
+                // The chunk's key flags: lane l of every warp loads 2 of them.
+                uint32_t km0, km1;
+                {
+                    int key = k0 + lane;
+                    km0 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
+                    key += 32;
+                    km1 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
                 }
-            }
-            // P smem and O are free once P V_{j-1} is done.
-            if (j > 0) {
-                if (!(ok = mbar_wait(bar_o, (j - 1) & 1, abort_flag, fault))) break;
+                const bool full = window < 0 && (km0 & km1) == 0xffffffffu;
+                if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
                 tc_fence_after();
-            }
-            // A row whose max passed m_ref by more than RESCALE moves m_ref;
-            // the warp rescales O in TMEM (warp-wide, factor 1 for the
-            // rows that keep theirs) when any of its rows moved.
-            const bool move = mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + RESCALE);
-            float f = 1.0f;
-            if (move) {
-                f = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mx);
-                l *= f;
-                m_ref = mx;
-            }
-            if (j > 0 && __any_sync(0xffffffffu, move)) {
-                __syncwarp();
-                float o[32];
+                // Pass 1: the row max of the chunk's valid raw scores (the
+                // scale is positive, so it is applied once after).
+                float mx = -INFINITY;
 #pragma unroll 1
                 for (int half = 0; half < 2; ++half) {
-                    tmem_ld32(lane_base + 64 + half * 32, o);
+                    float sv[32];
+                    __syncwarp();
+                    tmem_ld32(lane_base + half * 32, sv);
+                    if (full) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= f;
-                    tmem_st32(lane_base + 64 + half * 32, o);
+                        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
+                    } else {
+                        const uint32_t km = half ? km1 : km0;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            bool valid = (km >> i) & 1u;
+                            if (window >= 0) valid = valid && abs(qi - (k0 + half * 32 + i)) <= window;
+                            if (valid) mx = fmaxf(mx, sv[i]);
+                        }
+                    }
                 }
-            }
-            const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
-            // Pass 2: P = 2^(s c - mu) into the swizzled A operand.
-            float rs = 0.0f;
-            uint8_t *rowp = sP + r * 128;
+                mx = mx == -INFINITY ? mx : mx * scale_log2;
+                // P smem and O are free once the previous chunk's P V is done.
+                if (j > 0) {
+                    if (!(ok = mbar_wait(bar_o, (g - 1) & 1, abort_flag, fault))) break;
+                    tc_fence_after();
+                }
+                // A row whose max passed m_ref by more than RESCALE moves
+                // m_ref; the warp rescales O in TMEM (warp-wide, factor 1 for
+                // the rows that keep theirs) when any of its rows moved.
+                const bool move = mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + RESCALE);
+                float f = 1.0f;
+                if (move) {
+                    f = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mx);
+                    l *= f;
+                    m_ref = mx;
+                }
+                if (j > 0 && __any_sync(0xffffffffu, move)) {
+                    __syncwarp();
+                    float o[32];
 #pragma unroll 1
-            for (int half = 0; half < 2; ++half) {
-                float sv[32];
-                __syncwarp();
-                tmem_ld32(lane_base + half * 32, sv);
-                const uint32_t km = half ? km1 : km0;
+                    for (int half = 0; half < 2; ++half) {
+                        tmem_ld32(lane_base + 64 + half * 32, o);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    bool valid = (km >> i) & 1u;
-                    if (window >= 0) valid = valid && abs(qi - (k0 + half * 32 + i)) <= window;
-                    sv[i] = valid ? ex2(fmaf(sv[i], scale_log2, -mu)) : 0.0f;
-                    rs += sv[i];
+                        for (int i = 0; i < 32; ++i) o[i] *= f;
+                        tmem_st32(lane_base + 64 + half * 32, o);
+                    }
                 }
+                const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
+                // Pass 2: P = 2^(s c - mu) into the swizzled A operand.
+                float rs = 0.0f;
+                uint8_t *rowp = sP + r * 128;
+#pragma unroll 1
+                for (int half = 0; half < 2; ++half) {
+                    float sv[32];
+                    __syncwarp();
+                    tmem_ld32(lane_base + half * 32, sv);
+                    if (full) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint4 u;
-                    u.x = pack2<T>(sv[8 * q + 0], sv[8 * q + 1]);
-                    u.y = pack2<T>(sv[8 * q + 2], sv[8 * q + 3]);
-                    u.z = pack2<T>(sv[8 * q + 4], sv[8 * q + 5]);
-                    u.w = pack2<T>(sv[8 * q + 6], sv[8 * q + 7]);
-                    const int cc = half * 4 + q;
-                    *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = u;
+                        for (int i = 0; i < 32; ++i) {
+                            sv[i] = ex2(fmaf(sv[i], scale_log2, -mu));
+                            rs += sv[i];
+                        }
+                    } else {
+                        const uint32_t km = half ? km1 : km0;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            bool valid = (km >> i) & 1u;
+                            if (window >= 0) valid = valid && abs(qi - (k0 + half * 32 + i)) <= window;
+                            sv[i] = valid ? ex2(fmaf(sv[i], scale_log2, -mu)) : 0.0f;
+                            rs += sv[i];
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 w;
+                        w.x = pack2<T>(sv[8 * q + 0], sv[8 * q + 1]);
+                        w.y = pack2<T>(sv[8 * q + 2], sv[8 * q + 3]);
+                        w.z = pack2<T>(sv[8 * q + 4], sv[8 * q + 5]);
+                        w.w = pack2<T>(sv[8 * q + 6], sv[8 * q + 7]);
+                        const int cc = half * 4 + q;
+                        *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
+                    }
                 }
+                l += rs;
+                fence_async_smem();
+                tc_fence_before();
+                mbar_arrive(bar_p);
             }
-            l += rs;
-            fence_async_smem();
-            tc_fence_before();
-            mbar_arrive(bar_p);
-        }
-        if (ok && nch > 0 && mbar_wait(bar_o, (nch - 1) & 1, abort_flag, fault)) {
+            if (!ok || !(ok = mbar_wait(bar_o, (g - 1) & 1, abort_flag, fault))) break;
             tc_fence_after();
             __syncwarp();
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
@@ -256,15 +315,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 if (qi < it.len) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        uint4 u;
-                        u.x = pack2<T>(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
-                        u.y = pack2<T>(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
-                        u.z = pack2<T>(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
-                        u.w = pack2<T>(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
-                        reinterpret_cast<uint4 *>(out)[half * 4 + q] = u;
+                        uint4 w;
+                        w.x = pack2<T>(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
+                        w.y = pack2<T>(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
+                        w.z = pack2<T>(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
+                        w.w = pack2<T>(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
+                        reinterpret_cast<uint4 *>(out)[half * 4 + q] = w;
                     }
                 }
             }
+            // O is read: the next unit's first P V may overwrite it.
+            tc_fence_before();
         }
     }
     tc_fence_before();
@@ -277,12 +338,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 
 template <class T>
 cudaError_t launch(const CUtensorMap &mq, const CUtensorMap &mkv, void *ctx, const uint8_t *live,
-                   const AttnItem *items, int n_items, int heads, int h, int window, int *fault, cudaStream_t s) {
+                   const AttnItem *items, int n_items, int heads, int h, int window, int sms, int *fault,
+                   cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return e;
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
-    dim3 grid(n_items, heads);
-    attn_tc_kernel<T><<<grid, 160, SMEM, s>>>(mq, mkv, (T *)ctx, live, items, h, window, sl2, fault);
+    const int units = n_items * heads;
+    const int grid = units < sms * CTAS_PER_SM ? units : sms * CTAS_PER_SM;
+    attn_tc_kernel<T><<<grid, 160, SMEM, s>>>(mq, mkv, (T *)ctx, live, items, n_items, heads, h, window, sl2, fault);
     return cudaGetLastError();
 }
 
@@ -293,10 +356,14 @@ cudaError_t attention_tc(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_
                          int hidden, int window, int *fault, cudaStream_t s) {
     if (n_items == 0) return cudaSuccess;
     if (head_dim != D) return cudaErrorNotSupported;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (dt == Dt::F16)
-        return launch<__half>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, fault, s);
+        return launch<__half>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, sms, fault, s);
     if (dt == Dt::BF16)
-        return launch<__nv_bfloat16>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, fault, s);
+        return launch<__nv_bfloat16>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, sms,
+                                     fault, s);
     return cudaErrorNotSupported;
 }
 

@@ -7,6 +7,7 @@
 // variance summed in F64, (y - mean) * inv rounded to F32, then * w + b),
 // pooling mod.rs:426-484 (mean in F32 in column order, 1/n as F32, cut
 // before L2, L2 norm in F64 with a 1e-12 floor).
+#include <algorithm>
 #include <type_traits>
 
 #include "kernels.h"
@@ -93,29 +94,24 @@ template <class T> struct Vec {
 };
 
 // One warp per token, 16-byte accesses: lane l holds chunks l, l + 32, ..
-// of the row. Sums in F64 at F32 (the EXACT tier, as the reference's
-// LayerNorm sums), in F32 at F16/BF16.
+// of the row; two rows an iteration, both rows' loads issued first. The
+// weights and biases sit in shared memory (read once per block). Sums in F64
+// at F32 (the EXACT tier, as the reference's LayerNorm sums), in F32 at
+// F16/BF16.
 template <class T, int CPL>
 __global__ void __launch_bounds__(256) ln_vec_kernel(const T *__restrict__ src, T *dst, const float *__restrict__ ln_w,
                                                      const float *__restrict__ ln_b, int tokens, int h, double eps) {
     using V = Vec<T>;
     using Acc = typename std::conditional<sizeof(T) == 4, double, float>::type;
+    __shared__ __align__(16) float wb[2 * 1024];
+    for (int i = threadIdx.x; i < h; i += blockDim.x) {
+        wb[i] = ln_w[i];
+        wb[1024 + i] = ln_b ? ln_b[i] : 0.0f;
+    }
+    __syncthreads();
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int chunks = h / V::N;
-    // The weights and biases of this lane's chunks, read once per warp.
-    float w[CPL][V::N], b[CPL][V::N];
-#pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-        const int c = lane + 32 * i;
-#pragma unroll
-        for (int j = 0; j < V::N; ++j) {
-            w[i][j] = c < chunks ? ln_w[c * V::N + j] : 0.0f;
-            b[i][j] = (c < chunks && ln_b) ? ln_b[c * V::N + j] : 0.0f;
-        }
-    }
-    // Two tokens an iteration, both rows' loads issued before either's sums,
-    // so each warp keeps twice the bytes in flight.
     for (int t0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t0 < tokens; t0 += 2 * warps) {
         const int tk[2] = {t0, t0 + warps};
         float v[2][CPL][V::N];
@@ -157,8 +153,9 @@ __global__ void __launch_bounds__(256) ln_vec_kernel(const T *__restrict__ src, 
                     float o[V::N];
 #pragma unroll
                     for (int j = 0; j < V::N; ++j) {
+                        const int col = c * V::N + j;
                         const float z = (float)(((Acc)v[u][i][j] - mean) * inv);
-                        o[j] = z * w[i][j] + b[i][j];
+                        o[j] = z * wb[col] + wb[1024 + col];
                     }
                     V::store(out + c * V::N, o);
                 }
@@ -280,7 +277,9 @@ template <class T>
 cudaError_t ln_launch(const void *src, void *dst, const float *w, const float *b, int tokens, int h, double eps,
                       cudaStream_t s) {
     const int chunks = h / Vec<T>::N, cpl = (chunks + 31) / 32;
-    const int g = grid_for(tokens);
+    // Resident blocks only (3 of 256 threads an SM at 78 registers), each
+    // warp streaming rows.
+    const int g = std::min(148 * 3, (tokens + 15) / 16);
     const T *in = (const T *)src;
     T *out = (T *)dst;
     if (cpl <= 1) ln_vec_kernel<T, 1><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
