@@ -73,6 +73,33 @@ TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, u
                                              const float *qkv, const uint8_t *live, uint32_t heads,
                                              uint32_t head_dim, int32_t window, float *ctx_out, turbo_error *err);
 
+/* Attention that allocates nothing. This entry point has no counterpart in
+ * the reference. It is for callers that cannot call cudaMalloc (code living
+ * in another framework's memory pool or arena, serving loops that must not
+ * pay for an allocation, runtimes that forbid allocation after start-up):
+ * they pass their own device buffers and get the tensor-core attention
+ * alone. qkv is [tokens, 3 * heads * head_dim] (16-byte aligned), ctx
+ * [tokens, heads * head_dim], live [tokens] the mask entries, all device
+ * memory of the current device; lens [batch] (host) the rows' token counts,
+ * packed one after another; window < 0 for whole rows. F16 or BF16, head
+ * width 64. Asynchronous on `stream` (NULL: the default stream); when
+ * fault_host is not NULL the kernel's fault word (0, or 1 when a wait gave
+ * up) is copied there on the stream (pinned memory keeps the call
+ * asynchronous).
+ *
+ * Its scratch -- the work list and the fault word -- lives in one device
+ * array of TURBO_B200_NOALLOC_MAX_ITEMS 16-byte work units plus 256 bytes
+ * (about 1 MB), held by every GPU that loads the library until exit; a batch
+ * needing more query tiles of 128 than that is TURBO_E_CAPACITY. Every call
+ * shares the array and rewrites it (the fault word cleared first), so calls
+ * that overlap on the GPU race on it. The first call on a device looks up
+ * the array's address on that device; make it before any stream capture. */
+#define TURBO_B200_NOALLOC_MAX_ITEMS 65536u
+TB_EXPORT int32_t turbo_b200_attention_noalloc(uint32_t dtype, const void *qkv, void *ctx, const uint8_t *live,
+                                               const int32_t *lens, uint32_t batch, uint32_t heads,
+                                               uint32_t head_dim, int32_t window, void *stream,
+                                               int32_t *fault_host, turbo_error *err);
+
 /* Bench hooks (no counterpart needed in the reference, whose bench times the
  * public API): mark the last written batch as written again, so the next
  * session_run computes on the plan already in device memory; turn on event
