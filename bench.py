@@ -15,9 +15,12 @@ encoder over one batch.
   e2e    the same metric through the C table with host buffers: each step is
          embed_write (host rows, packing, H2D) + session_run + buffer_read
          (D2H of the vectors), wall-clock.
-Under torchrun (N > 1) each rank runs its own rows on its own GPU (weak
-scaling: rows shard by sequence with no collective on the data path);
-timings are reduced with MAX over ranks through torch.distributed.
+Under torchrun (N > 1) one seeded global batch of 256 N rows is sharded by
+tokens (longest-processing-time, turboembed_b200/shard.py) and each rank runs
+its rows on its own GPU (weak scaling: no collective on the data path);
+timings are reduced with MAX over ranks through torch.distributed. After the
+timed steps the pooled vectors are all-gathered once into one device buffer
+on every rank (NCCL over NVLink) and checked (`allgather` in the JSON line).
 """
 import argparse
 import json
@@ -34,7 +37,7 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from turboembed_b200 import abi, models, runtime  # noqa: E402
+from turboembed_b200 import abi, models, runtime, shard  # noqa: E402
 
 METRIC = "embedded tokens/sec/GPU (BERT-base F16, seq 512) and % of tensor-core peak"
 WORKLOAD = ("BERT-base (BASELINE config 2): 12L h768 12 heads FFN3072 GELU, batch 256/GPU, L~U[64,512], "
@@ -210,8 +213,13 @@ def main():
     ctx = backend.context(local)
     desc = models.synthetic("bert-base", 1)
     model = ctx.load(desc)
-    sess = model.session(BATCH, SEQ, abi.TURBO_PRECISION_FASTEST)
-    ids, mask, lens = models.rows_bert(1000 + rank, BATCH, 64, 512, SEQ)
+    # One seeded global batch of BATCH rows per GPU, sharded by tokens
+    # (longest-processing-time): weak scaling, no collective on the data path.
+    ids_all, mask_all, lens_all = models.rows_bert(1000, BATCH * world, 64, 512, SEQ)
+    mine = shard.shard_rows(lens_all, world)[rank]
+    ids, mask, lens = ids_all[mine], mask_all[mine], lens_all[mine]
+    counts = [len(p) for p in shard.shard_rows(lens_all, world)]
+    sess = model.session(max(counts), SEQ, abi.TURBO_PRECISION_FASTEST)
     live = int(mask.sum())
 
     def times():
@@ -272,6 +280,22 @@ def main():
     h2d = int(run.h2d_bytes)
     d2h = int(vec.nbytes)
 
+    # The optional all-gather of the pooled vectors into one device buffer
+    # on every rank (NCCL over NVLink), once, outside the timed steps.
+    gather = None
+    if dist is not None:
+        import torch
+        lib.turbo_b200_buffer_copy.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p]
+        local_vec = torch.empty((len(mine), HIDDEN), dtype=torch.float32, device=f"cuda:{local}")
+        assert lib.turbo_b200_buffer_copy(run.output, local_vec.data_ptr(), local_vec.numel() * 4, None) == 0
+        torch.cuda.synchronize(local)
+        t0 = time.perf_counter()
+        allv = shard.gather_vectors(local_vec, counts)
+        torch.cuda.synchronize(local)
+        gather = {"ms": 1000 * (time.perf_counter() - t0), "rows": int(allv.shape[0]),
+                  "bytes": int(allv.numel() * 4), "matches_local": bool(torch.equal(
+                      allv[sum(counts[:rank]):sum(counts[:rank]) + counts[rank]], local_vec))}
+
     out = None
     if rank == 0:
         cpu = None
@@ -299,6 +323,8 @@ def main():
         }
         if cpu is not None:
             out["cpu_baseline"] = cpu
+        if gather is not None:
+            out["allgather"] = gather
         print(json.dumps(out), flush=True)
     sess.release()
     model.release()

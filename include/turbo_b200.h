@@ -108,6 +108,10 @@ TB_EXPORT int32_t turbo_b200_attention_noalloc(uint32_t dtype, const void *qkv, 
  * when profiling, the summed GEMM and attention launch times, the GEMM
  * launch count and their algorithmic FLOPs (2 M N K each). */
 TB_EXPORT int32_t turbo_b200_session_rerun(void *session);
+/* Copy the first `bytes` of a buffer (a session's output) to device (or
+ * host) memory the caller owns, on `stream`, and wait: how the multi-GPU
+ * bench hands pooled vectors to an NCCL all-gather. */
+TB_EXPORT int32_t turbo_b200_buffer_copy(void *buffer, void *dst, uint64_t bytes, void *stream);
 TB_EXPORT int32_t turbo_b200_session_profile(void *session, uint32_t on);
 TB_EXPORT int32_t turbo_b200_session_times(void *session, float *run_ms, float *gemm_ms, float *attn_ms,
                                            uint32_t *gemm_launches, double *gemm_flops);

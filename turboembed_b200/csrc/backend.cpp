@@ -1219,6 +1219,15 @@ TB_EXPORT const char *turbo_cuda_arch_label(void) { return "b200"; }
 
 TB_EXPORT const turbo_backend *turbo_b200_backend(void) { return &turbo_cuda_backend; }
 
+TB_EXPORT int32_t turbo_b200_buffer_copy(void *buffer, void *dst, uint64_t bytes, void *stream) {
+    auto *b = (Buffer *)buffer;
+    if (!b || !dst || bytes > b->bytes) return TURBO_E_INVALID_ARGUMENT;
+    DeviceScope ds(b->ctx->device);
+    cudaError_t e = cudaMemcpyAsync(dst, b->ptr, bytes, cudaMemcpyDefault, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    return e == cudaSuccess ? TURBO_OK : TURBO_E_RUNTIME;
+}
+
 TB_EXPORT int32_t turbo_b200_session_rerun(void *session) {
     auto *s = (Session *)session;
     if (!s || !s->rerun_ok) return TURBO_E_INVALID_STATE;
