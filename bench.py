@@ -1,28 +1,32 @@
-"""Benchmark of the B200 backend on BASELINE.json's headline workload.
+"""Benchmark of the B200 backend on BASELINE.json's workloads.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--config c1|c2|c2x|c3|c4|c5]
 
-Workload (the metric's config): a BERT-base encoder
-(12 layers, hidden 768, 12 heads, FFN 3072 GELU, post-LN, vocab 30522,
-random N(0, 0.02) weights from seed 1), batch 256 rows per GPU with lengths
-U[64, 512], ids U[1000, 30521] between 101 and 102, CLS pooling + L2, run at
-FASTEST (F16 operands, F32 sums), varlen-packed. A step is one pass of the
-encoder over one batch.
+The default (c2) is the headline metric's config:
+a BERT-base encoder (12 layers, hidden 768, 12 heads, FFN 3072 GELU,
+post-LN, vocab 30522, random N(0, 0.02) weights from seed 1), batch 256 rows
+per GPU with lengths U[64, 512], ids U[1000, 30521] between 101 and 102,
+CLS pooling + L2, run at FASTEST (F16 operands, F32 sums), varlen-packed.
+The other configs are BASELINE.json's other workloads (WORKLOADS below);
+each prints the same JSON line for its own workload. A step is one pass of
+the encoder (and, for c3, the rerank head) over one batch.
 
   value  live tokens/s of the whole job, inputs already resident in HBM:
          each step re-runs the written batch (turbo_b200_session_rerun) and
          is timed by CUDA events on the backend's own stream; max over ranks.
   e2e    the same metric through the C table with host buffers: each step is
          embed_write (host rows, packing, H2D) + session_run + buffer_read
-         (D2H of the vectors), wall-clock.
-Under torchrun (N > 1) one seeded global batch of 256 N rows is sharded by
-tokens (longest-processing-time, turboembed_b200/shard.py) and each rank runs
-its rows on its own GPU (weak scaling: no collective on the data path);
-timings are reduced with MAX over ranks through torch.distributed. After the
-timed steps the pooled vectors are all-gathered once into one device buffer
-on every rank (NCCL over NVLink) and checked (`allgather` in the JSON line).
+         (D2H of the vectors, or of the scores for c3), wall-clock.
+Under torchrun (N > 1) one seeded global batch of N times the per-GPU rows is
+sharded by cost (longest-processing-time, turboembed_b200/shard.py) and each
+rank runs its rows on its own GPU (weak scaling: no collective on the data
+path); timings are reduced with MAX over ranks through torch.distributed.
+After the timed steps the pooled vectors are all-gathered once into one
+device buffer on every rank (NCCL over NVLink) and checked (`allgather`).
 """
 import argparse
+import ctypes as C
 import json
 import os
 import statistics
@@ -40,23 +44,109 @@ sys.path.insert(0, str(ROOT))
 from turboembed_b200 import abi, models, runtime, shard  # noqa: E402
 
 METRIC = "embedded tokens/sec/GPU (BERT-base F16, seq 512) and % of tensor-core peak"
-WORKLOAD = ("BERT-base (BASELINE config 2): 12L h768 12 heads FFN3072 GELU, batch 256/GPU, L~U[64,512], "
-            "CLS + L2, FASTEST (F16 operands, F32 sums), varlen-packed")
-BATCH, SEQ, LAYERS, HIDDEN, FFN = 256, 512, 12, 768, 3072
+FFMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal F32 FMA peak (148 SMs x 128 lanes at 1965 MHz)
 
 
 def env_rank():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
-def flops_per_step(lens):
-    """Algorithmic FLOPs of one step (GEMMs + attention, per SURVEY's 8(d)):
-    per layer 2 L (h 3h + h h + h F + F h) + 4 L^2 h for each row of L tokens."""
-    lens = np.asarray(lens, np.float64)
-    mac = HIDDEN * 3 * HIDDEN + HIDDEN * HIDDEN + 2 * HIDDEN * FFN
-    gemm = LAYERS * 2.0 * lens.sum() * mac
-    attn = LAYERS * 4.0 * (lens ** 2).sum() * HIDDEN
-    return gemm, attn
+def _no_types(t):
+    ids, mask, lens = t
+    return ids, mask, None, lens
+
+
+class Workload:
+    """One BASELINE.json config: model, rows, session options and FLOP count.
+
+    rows(seed, n) -> (ids, mask, types or None, lens); cpu_rows / ref_rows
+    give the bounded CPU samples (a row count of the same distribution, or
+    a function of a seed)."""
+
+    def __init__(self, key, text, model, seed, wdtype, precision, dtype, per_gpu, seq, rows, pooling, normalize,
+                 task=abi.TURBO_TASK_EMBED, ranges=None, head=False, cpu_rows=None, ref_rows=None):
+        self.key, self.text, self.model, self.seed, self.wdtype = key, text, model, seed, wdtype
+        self.precision, self.dtype, self.per_gpu, self.seq, self.rows = precision, dtype, per_gpu, seq, rows
+        self.pooling, self.normalize, self.task, self.ranges, self.head = pooling, normalize, task, ranges, head
+        self.cpu_rows, self.ref_rows = cpu_rows, ref_rows
+        cfg = models.CONFIGS[model]
+        self.layers, self.hidden, self.ffn = cfg["layers"], cfg["hidden"], cfg["intermediate"]
+        self.modern = cfg["family"] == abi.TURBO_FAMILY_MODERNBERT
+        self.window = cfg.get("window", 0) // 2
+        self.global_every = cfg.get("global_every", 0)
+
+    def desc(self):
+        return models.synthetic(self.model, self.seed, dtype=self.wdtype)
+
+    def flops(self, lens):
+        """Algorithmic FLOPs of one pass: 2 M N K for every GEMM and 4 h per
+        attended (query, key) pair (QK^T and PV), summed over the layers;
+        local layers count only the keys inside the window."""
+        lens = np.asarray(lens, np.int64)
+        h, F, L = self.hidden, self.ffn, self.layers
+        per_tok = 4 * h * h + (3 * h * F if self.modern else 2 * h * F)
+        gemm = 2.0 * L * float(lens.sum()) * per_tok
+        full = float((lens.astype(np.float64) ** 2).sum())
+        if not self.modern:
+            return gemm, 4.0 * h * L * full
+        n_global = sum(1 for l in range(L) if self.global_every == 0 or l % self.global_every == 0)
+        local, w = 0.0, self.window
+        for n in lens:
+            i = np.arange(n)
+            local += float((np.minimum(i + w, n - 1) - np.maximum(i - w, 0) + 1).sum())
+        return gemm, 4.0 * h * (n_global * full + (L - n_global) * local)
+
+    def row_weight(self):
+        """Attention's cost per L^2 relative to a token's GEMM cost, for
+        sharding rows of unequal length (attention runs at about a quarter
+        of the GEMMs' rate)."""
+        per_tok = 4 * self.hidden ** 2 + (3 if self.modern else 2) * self.hidden * self.ffn
+        return 4.0 * 4 * self.hidden / (2 * per_tok)
+
+
+WORKLOADS = {
+    "c1": Workload("c1", "all-MiniLM-L6-v2 shape (BASELINE config 1): 6L h384 12 heads FFN1536, batch 32/GPU, "
+                         "L~U[16,128], mean + L2, EXACT (F32)", "minilm", 0, abi.TURBO_DTYPE_F32,
+                   abi.TURBO_PRECISION_EXACT, "f32", 32, 128,
+                   lambda seed, n: _no_types(models.rows_bert(seed, n, 16, 128, 128)), abi.TURBO_POOLING_MEAN,
+                   abi.TURBO_NORMALIZE_L2, cpu_rows=128, ref_rows=16),
+    "c2": Workload("c2", "BERT-base (BASELINE config 2): 12L h768 12 heads FFN3072 GELU, batch 256/GPU, "
+                         "L~U[64,512], CLS + L2, FASTEST (F16 operands, F32 sums), varlen-packed", "bert-base", 1,
+                   abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 256, 512,
+                   lambda seed, n: _no_types(models.rows_bert(seed, n, 64, 512, 512)), abi.TURBO_POOLING_CLS,
+                   abi.TURBO_NORMALIZE_L2, cpu_rows=6, ref_rows=2),
+    "c2x": Workload("c2x", "BERT-base (BASELINE config 2) at EXACT (F32): 12L h768, batch 256/GPU, L~U[64,512], "
+                           "CLS + L2, varlen-packed", "bert-base", 1, abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_EXACT,
+                    "f32", 256, 512, lambda seed, n: _no_types(models.rows_bert(seed, n, 64, 512, 512)),
+                    abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_L2, cpu_rows=6, ref_rows=2),
+    "c3": Workload("c3", "cross-encoder rerank (BASELINE config 3): BERT-base body + 768->1 head on CLS, "
+                         "1 query x 1024 passages/GPU, [101] q [102] p [102], BF16 (MODEL)", "bert-base", 2,
+                   abi.TURBO_DTYPE_BF16, abi.TURBO_PRECISION_MODEL, "bf16", 1024, 512,
+                   lambda seed, n: models.rows_rerank(seed, n), abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_NONE,
+                   task=abi.TURBO_TASK_RERANK, head=True, cpu_rows=6, ref_rows=2),
+    "c4": Workload("c4", "ModernBERT-base (BASELINE config 4): 22L h768 GeGLU 1152, global every 3rd layer, "
+                         "local window 128, batch 8/GPU, L~U[1024,8192] unpadded, mean + L2, FASTEST (F16)",
+                   "modernbert-base", 3, abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 8, 8192,
+                   lambda seed, n: _no_types(models.rows_long(seed, n, 1024, 8192, 8192, 100, 50367)),
+                   abi.TURBO_POOLING_MEAN, abi.TURBO_NORMALIZE_L2,
+                   cpu_rows=lambda seed: _no_types(models.rows_long(seed, 1, 1024, 1024, 1024, 100, 50367)),
+                   ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 256, 256, 256, 100, 50367))),
+    "c5": Workload("c5", "XLM-R-large / bge-m3 shape (BASELINE config 5): 24L h1024 16 heads FFN4096, 16 documents"
+                         "/GPU (128 over 8 GPUs) of 8192 tokens, range pooling U[32,256] + L2, BF16 (MODEL)",
+                   "xlmr-large", 4, abi.TURBO_DTYPE_BF16, abi.TURBO_PRECISION_MODEL, "bf16", 16, 8192,
+                   lambda seed, n: _no_types(models.rows_long(seed, n, 8192, 8192, 8192, 5, 250001)),
+                   abi.TURBO_POOLING_MEAN, abi.TURBO_NORMALIZE_L2,
+                   ranges=lambda seed, lens: models.ranges_tiling(seed, lens, 32, 256),
+                   cpu_rows=lambda seed: _no_types(models.rows_long(seed, 1, 512, 512, 512, 5, 250001)),
+                   ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 128, 128, 128, 5, 250001))),
+}
+
+
+def head_weights(wl):
+    """The rerank head of config 3: a hidden -> 1 linear on the CLS vector,
+    N(0, 0.02) from the config's seed + 1000, bias 0."""
+    rng = np.random.default_rng(wl.seed + 1000)
+    return (rng.standard_normal(wl.hidden, dtype=np.float32) * np.float32(0.02)).astype(np.float32), np.float32(0.0)
 
 
 class Clocks:
@@ -110,53 +200,76 @@ def peaks():
     return 1400.0, 1590.0, "fallback"
 
 
-def traffic_from_profile():
+def traffic_from_profile(key):
     """DRAM bytes per launch of the dominant kernel, from the committed ncu
-    summary (profiles/gemm_tc_bert_base.md, line `traffic_bytes_per_launch:`)."""
+    summary of the default workload (profiles/gemm_tc_bert_base.md, line
+    `traffic_bytes_per_launch:`); None for the other workloads."""
     p = ROOT / "profiles" / "gemm_tc_bert_base.md"
-    if p.exists():
+    if key == "c2" and p.exists():
         for line in p.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
                 return float(line.split(":", 1)[1].strip())
     return None
 
 
-def cpu_baseline(desc, seconds_hint=10.0):
-    """The CPU oracle (a restatement of the reference CPU encoder) on a
-    bounded sample of the same workload, all host threads."""
+def sample_rows(wl, spec, seed):
+    return spec(seed) if callable(spec) else wl.rows(seed, spec)
+
+
+def oracle_pass(wl, desc, rows, cores):
+    """One pass of the CPU oracle (a restatement of the reference CPU encoder)
+    over rows, with the workload's pooling (and ranges, and head)."""
     from oracle import oracle
-    ids, mask, lens = models.rows_bert(4242, 6, 64, 512, SEQ)
+    ids, mask, types, lens = rows
+    rg = wl.ranges(99, lens) if wl.ranges else None
+    out = oracle.encode(desc, ids, mask, types, pooling=wl.pooling, normalize=wl.normalize, ranges=rg,
+                        threads=cores)
+    if wl.head:
+        w, b = head_weights(wl)
+        out = oracle.rerank_head(out, None, None, w, b)
+    return out
+
+
+def cpu_baseline(wl, desc):
+    """The CPU oracle on a bounded sample of the same workload, all host
+    threads."""
     cores = os.cpu_count() or 1
+    rows = sample_rows(wl, wl.cpu_rows, 4242)
+    lens = rows[3]
     t0 = time.perf_counter()
-    oracle.encode(desc, ids, mask, pooling=abi.TURBO_POOLING_CLS, threads=cores)
+    oracle_pass(wl, desc, rows, cores)
     dt = time.perf_counter() - t0
-    return {"value": float(lens.sum() / dt), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{len(lens)} rows of the config-2 distribution ({int(lens.sum())} live tokens), F32, "
-                      f"full 12-layer BERT-base, {dt:.1f} s"}
+    return {"value": float(np.sum(lens) / dt), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{len(lens)} rows of the {wl.key} distribution ({int(np.sum(lens))} live tokens), F32, "
+                      f"all {wl.layers} layers, {dt:.1f} s"}
 
 
-def run_reference(args):
+def metric_of(wl):
+    return METRIC if wl.key == "c2" else f"embedded tokens/sec/GPU ({wl.key}: {wl.model}, {wl.dtype})"
+
+
+def run_reference(args, wl):
     rank, world, _ = env_rank()
     if rank != 0:
         return
-    from oracle import oracle
-    desc = models.synthetic("bert-base", 1)
+    desc = wl.desc()
     cores = os.cpu_count() or 1
     times, toks = [], []
     for step in range(args.warmup + args.steps):
-        ids, mask, lens = models.rows_bert(7000 + step, 2, 64, 512, SEQ)
+        rows = sample_rows(wl, wl.ref_rows, 7000 + step)
         t0 = time.perf_counter()
-        oracle.encode(desc, ids, mask, pooling=abi.TURBO_POOLING_CLS, threads=cores)
+        oracle_pass(wl, desc, rows, cores)
         if step >= args.warmup:
             times.append(time.perf_counter() - t0)
-            toks.append(int(lens.sum()))
+            toks.append(int(np.sum(rows[3])))
     value = sum(toks) / sum(times)
-    sample = (f"each step 2 rows of the config-2 distribution through the full 12-layer BERT-base in F32 "
+    sample = (f"each step {len(rows[3])} row(s) of the {wl.key} distribution through all {wl.layers} layers in F32 "
               f"(the reference CPU encoder's algorithm, oracle/; the Rust original is not buildable here)")
-    print(json.dumps({"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
-                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                      "data": "synthetic", "config": {"workload": WORKLOAD, "seq_len": SEQ},
+    print(json.dumps({"impl": "reference", "metric": metric_of(wl), "value": value, "unit": "tokens/s",
+                      "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": wl.text, "config": wl.key, "seq_len": wl.seq},
                       "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                                        "sample": sample},
                       "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
@@ -169,10 +282,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    wl = WORKLOADS[args.config]
     if args.impl == "reference":
-        return run_reference(args)
+        return run_reference(args, wl)
     rank, world, local = env_rank()
     dist = None
     if world > 1:
@@ -183,144 +298,179 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
 
-    def max_over_ranks(x):
+    def reduce(x, op):
         if dist is None:
             return x
         import torch
         t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=op)
         return float(t.item())
 
+    def max_over_ranks(x):
+        return reduce(x, dist.ReduceOp.MAX if dist else None)
+
     def sum_over_ranks(x):
-        if dist is None:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return reduce(x, dist.ReduceOp.SUM if dist else None)
 
     def barrier():
         if dist is not None:
             dist.barrier(device_ids=[local])
 
     lib = runtime.library()
-    import ctypes as C
     lib.turbo_b200_session_rerun.argtypes = [C.c_void_p]
     lib.turbo_b200_session_profile.argtypes = [C.c_void_p, C.c_uint32]
     lib.turbo_b200_session_times.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float),
-                                             C.POINTER(C.c_float), C.POINTER(C.c_uint32), C.POINTER(C.c_double)]
+                                             C.POINTER(C.c_float), C.POINTER(C.c_uint32), C.POINTER(C.c_double),
+                                             C.POINTER(C.c_float)]
+    lib.turbo_b200_kernel_launches.restype = C.c_uint64
     backend = runtime.Backend()
     ctx = backend.context(local)
-    desc = models.synthetic("bert-base", 1)
+    desc = wl.desc()
     model = ctx.load(desc)
-    # One seeded global batch of BATCH rows per GPU, sharded by tokens
+    # One seeded global batch of per_gpu rows per GPU, sharded by cost
     # (longest-processing-time): weak scaling, no collective on the data path.
-    ids_all, mask_all, lens_all = models.rows_bert(1000, BATCH * world, 64, 512, SEQ)
-    mine = shard.shard_rows(lens_all, world)[rank]
+    ids_all, mask_all, types_all, lens_all = wl.rows(1000, wl.per_gpu * world)
+    parts = shard.shard_rows(lens_all, world, wl.row_weight())
+    mine = parts[rank]
+    counts = [len(p) for p in parts]
     ids, mask, lens = ids_all[mine], mask_all[mine], lens_all[mine]
-    counts = [len(p) for p in shard.shard_rows(lens_all, world)]
-    sess = model.session(max(counts), SEQ, abi.TURBO_PRECISION_FASTEST)
+    types = None if types_all is None else types_all[mine]
+    ranges = wl.ranges(2000 + rank, lens) if wl.ranges else None
+    max_ranges = 0 if ranges is None else len(ranges)
+    sess = model.session(max(counts), wl.seq, wl.precision, task=wl.task, max_ranges=max_ranges)
     live = int(mask.sum())
+    if wl.head:
+        hw, hb = head_weights(wl)
+        sess.set_head(hw, hb)
+
+    def write():
+        if ranges is not None:
+            sess.write_ranges(ids, mask, ranges, types=types, normalize=wl.normalize)
+        else:
+            sess.write(ids, mask, types, pooling=wl.pooling, normalize=wl.normalize)
+
+    def step():
+        run = sess.run()
+        if wl.head:
+            sess.head_scores()
+        return run
 
     def times():
-        r, g, a, n, f = C.c_float(), C.c_float(), C.c_float(), C.c_uint32(), C.c_double()
-        rc = lib.turbo_b200_session_times(sess.h, C.byref(r), C.byref(g), C.byref(a), C.byref(n), C.byref(f))
+        r, g, a, n, f, o = C.c_float(), C.c_float(), C.c_float(), C.c_uint32(), C.c_double(), C.c_float()
+        rc = lib.turbo_b200_session_times(sess.h, C.byref(r), C.byref(g), C.byref(a), C.byref(n), C.byref(f),
+                                          C.byref(o))
         assert rc == 0
-        return r.value, g.value, a.value, n.value, f.value
+        return r.value, g.value, a.value, n.value, f.value, o.value
 
-    sess.write(ids, mask, pooling=abi.TURBO_POOLING_CLS)
-    sess.run()
-    per_step_launches = 1 + LAYERS * 7 + 1
+    write()
+    step()
     for _ in range(args.warmup):
         lib.turbo_b200_session_rerun(sess.h)
-        sess.run()
+        step()
     barrier()
     dev_ms = []
+    launches0 = lib.turbo_b200_kernel_launches()
     with Clocks(local) as clk:
         t0 = time.perf_counter()
         for _ in range(args.steps):
             assert lib.turbo_b200_session_rerun(sess.h) == 0
-            sess.run()
+            step()
             dev_ms.append(times()[0])
         wall = time.perf_counter() - t0
+    launches = int(lib.turbo_b200_kernel_launches() - launches0)
     barrier()
     total_ms = max_over_ranks(sum(dev_ms))
     wall = max_over_ranks(wall)
     tokens_all = sum_over_ranks(float(live))
     value = tokens_all * args.steps / (total_ms / 1000.0)
 
-    # The dominant kernel's live timing: event pairs around every GEMM.
+    # The dominant kernel's live timing: event pairs around every launch.
     lib.turbo_b200_session_profile(sess.h, 1)
-    g_ms = a_ms = g_flops = 0.0
+    g_ms = a_ms = g_flops = o_ms = p_run = 0.0
     g_n = 0
     for _ in range(3):
         lib.turbo_b200_session_rerun(sess.h)
         sess.run()
-        _, g, a, n, f = times()
-        g_ms, a_ms, g_n, g_flops = g_ms + g, a_ms + a, g_n + n, g_flops + f
+        rr, g, a, n, f, o = times()
+        g_ms, a_ms, g_n, g_flops, o_ms, p_run = g_ms + g, a_ms + a, g_n + n, g_flops + f, o_ms + o, p_run + rr
     lib.turbo_b200_session_profile(sess.h, 0)
     sustained, burst, peak_kind = peaks()
     gemm_tflops = g_flops / (g_ms / 1000.0) / 1e12
-    gemm_flops_step, attn_flops_step = flops_per_step(lens)
+    gemm_flops_step, attn_flops_step = wl.flops(lens)
     step_ms = total_ms / args.steps
+    f32 = wl.dtype == "f32"
+    peak = FFMA_PEAK_TFLOPS if f32 else sustained
 
     # End to end through the C table with host buffers.
     e2e_t = []
     barrier()
-    for step in range(args.warmup + args.steps):
+    for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        sess.write(ids, mask, pooling=abi.TURBO_POOLING_CLS)
+        write()
         run = sess.run()
-        vec = sess.read()
-        if step >= args.warmup:
+        res = sess.head_scores() if wl.head else sess.read()
+        if i >= args.warmup:
             e2e_t.append(time.perf_counter() - t0)
     barrier()
     e2e_total = max_over_ranks(sum(e2e_t))
     e2e_value = tokens_all * args.steps / e2e_total
     h2d = int(run.h2d_bytes)
-    d2h = int(vec.nbytes)
+    d2h = int(res.nbytes)
 
     # The optional all-gather of the pooled vectors into one device buffer
     # on every rank (NCCL over NVLink), once, outside the timed steps.
+    n_vec = len(ranges) if ranges is not None else len(mine)
     gather = None
     if dist is not None:
         import torch
+        cnt = torch.tensor([n_vec], dtype=torch.int64, device=f"cuda:{local}")
+        every = [torch.zeros_like(cnt) for _ in range(world)]
+        dist.all_gather(every, cnt)
+        vec_counts = [int(t.item()) for t in every]
         lib.turbo_b200_buffer_copy.argtypes = [C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p]
-        local_vec = torch.empty((len(mine), HIDDEN), dtype=torch.float32, device=f"cuda:{local}")
+        local_vec = torch.empty((n_vec, wl.hidden), dtype=torch.float32, device=f"cuda:{local}")
         assert lib.turbo_b200_buffer_copy(run.output, local_vec.data_ptr(), local_vec.numel() * 4, None) == 0
         torch.cuda.synchronize(local)
         t0 = time.perf_counter()
-        allv = shard.gather_vectors(local_vec, counts)
+        allv = shard.gather_vectors(local_vec, vec_counts)
         torch.cuda.synchronize(local)
+        off = sum(vec_counts[:rank])
         gather = {"ms": 1000 * (time.perf_counter() - t0), "rows": int(allv.shape[0]),
-                  "bytes": int(allv.numel() * 4), "matches_local": bool(torch.equal(
-                      allv[sum(counts[:rank]):sum(counts[:rank]) + counts[rank]], local_vec))}
+                  "bytes": int(allv.numel() * 4),
+                  "matches_local": bool(torch.equal(allv[off:off + vec_counts[rank]], local_vec))}
 
-    out = None
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(desc)
-        clocks = clk.summary()
+            cpu = cpu_baseline(wl, desc)
+        kernel = "gemm_simt (FFMA GEMM" if f32 else "gemm_tc (tcgen05 GEMM"
         out = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric_of(wl), "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "model": "bert-base (random init, seed 1)", "global_batch": BATCH * world,
-                       "seq_len": SEQ, "parallelism": f"dp{world}", "live_tokens_per_gpu": live,
-                       "l2": "no flush: every step streams > 126 MB (170 MB of F16 weights + activations)"},
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+            "config": {"workload": wl.text, "config": wl.key,
+                       "model": f"{wl.model} (random init, seed {wl.seed})", "global_batch": wl.per_gpu * world,
+                       "seq_len": wl.seq, "parallelism": f"dp{world}", "live_tokens_per_gpu": live,
+                       "vectors_per_gpu": n_vec,
+                       "l2": "no flush: every step streams more than the 126 MB L2 (weights + activations)"},
             "per_gpu_tokens_per_s": value / world,
             "wall_tokens_per_s": tokens_all * args.steps / wall,
-            "tensor_frac_whole_step": (gemm_flops_step + attn_flops_step) / (step_ms / 1000) / 1e12 / sustained,
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc (tcgen05 GEMM, all 48 launches of a step)",
-                         "achieved": gemm_tflops, "peak": sustained, "unit": "TFLOP/s",
-                         "frac": gemm_tflops / sustained, "peak_kind": f"{peak_kind} bf16 sustained",
-                         "traffic": traffic_from_profile(), "gemm_ms_per_step": g_ms / 3,
-                         "attention_ms_per_step": a_ms / 3, "launches_per_step": g_n // 3},
+            "tensor_frac_whole_step": (gemm_flops_step + attn_flops_step) / (step_ms / 1000) / 1e12 / peak,
+            "roofline": {"bound": "fp32-ffma" if f32 else "tensor",
+                         "kernel": f"{kernel}, all {g_n // 3} launches of a step)",
+                         "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s", "frac": gemm_tflops / peak,
+                         "peak_kind": "nominal F32 FMA (148 SMs x 128 x 2 x 1.965 GHz)" if f32
+                         else f"{peak_kind} bf16 sustained",
+                         "traffic": traffic_from_profile(wl.key), "gemm_ms_per_step": g_ms / 3,
+                         "attention_ms_per_step": a_ms / 3, "other_kernels_ms_per_step": o_ms / 3,
+                         "between_kernels_ms_per_step": (p_run - g_ms - a_ms - o_ms) / 3,
+                         "launches_per_step": g_n // 3},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": per_step_launches * args.steps,
-            "clocks": clocks,
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
         }
+        if wl.head:
+            out["pairs_per_s"] = wl.per_gpu * world * args.steps / (total_ms / 1000.0)
         if cpu is not None:
             out["cpu_baseline"] = cpu
         if gather is not None:

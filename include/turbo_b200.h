@@ -49,6 +49,10 @@ TB_EXPORT void turbo_cuda_fail_allocation(int32_t after);
 /* The label benchmarks are filed under (core/cuda/backend.cpp:3830). */
 TB_EXPORT const char *turbo_cuda_arch_label(void);
 
+/* How many kernels this library has launched in this process (counted on
+ * the host at each successful launch; no counterpart in the reference). */
+TB_EXPORT uint64_t turbo_b200_kernel_launches(void);
+
 /* One GEMM y = epi(a w^T + bias) on the device, operands given as host F32
  * and narrowed to dtype (TURBO_DTYPE_F16 / BF16 / F32) first, run through
  * `variant` 0 (the tcgen05 kernel as the backend runs it: CTA pairs when N
@@ -72,6 +76,19 @@ TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t variant, uint32
 TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, uint32_t batch, const int32_t *lens,
                                              const float *qkv, const uint8_t *live, uint32_t heads,
                                              uint32_t head_dim, int32_t window, float *ctx_out, turbo_error *err);
+
+/* The cross-encoder head on the device (SURVEY-listed next step after the
+ * reference's host head, core/src/session/rerank.rs:170-188): set_head
+ * uploads a pooler (W_p [h, h] row-major and b_p [h], or NULL for none) and
+ * a one-logit classifier (w_c [h], b_c) to the session once; head_scores
+ * turns the first n vectors of the session's last run -- CLS pooling,
+ * NORMALIZE_NONE, output_dim = hidden, as the core's rerank writes them --
+ * into n scores b_c + w_c . f32(tanh(W_p x + b_p)) with F64 sums, and copies
+ * the n floats to host memory. The max over a pair's passage windows stays
+ * with the caller (the core). */
+TB_EXPORT int32_t turbo_b200_session_set_head(void *session, const float *pooler_w, const float *pooler_b,
+                                              const float *cls_w, float cls_b, turbo_error *err);
+TB_EXPORT int32_t turbo_b200_session_head_scores(void *session, uint32_t n, float *scores, turbo_error *err);
 
 /* Attention that allocates nothing. This entry point has no counterpart in
  * the reference. It is for callers that cannot call cudaMalloc (code living
@@ -104,9 +121,12 @@ TB_EXPORT int32_t turbo_b200_attention_noalloc(uint32_t dtype, const void *qkv, 
  * public API): mark the last written batch as written again, so the next
  * session_run computes on the plan already in device memory; turn on event
  * pairs around every GEMM and attention launch; and read the device time of
- * the last run (events on the context's stream around its launches) and,
+ * the last run (events on the context's stream around its launches, the
+ * end event moved past the head when turbo_b200_session_head_scores ran
+ * after the run) and,
  * when profiling, the summed GEMM and attention launch times, the GEMM
- * launch count and their algorithmic FLOPs (2 M N K each). */
+ * launch count and their algorithmic FLOPs (2 M N K each), and the summed
+ * times of the other launches (gather, LayerNorm). */
 TB_EXPORT int32_t turbo_b200_session_rerun(void *session);
 /* Copy the first `bytes` of a buffer (a session's output) to device (or
  * host) memory the caller owns, on `stream`, and wait: how the multi-GPU
@@ -114,7 +134,7 @@ TB_EXPORT int32_t turbo_b200_session_rerun(void *session);
 TB_EXPORT int32_t turbo_b200_buffer_copy(void *buffer, void *dst, uint64_t bytes, void *stream);
 TB_EXPORT int32_t turbo_b200_session_profile(void *session, uint32_t on);
 TB_EXPORT int32_t turbo_b200_session_times(void *session, float *run_ms, float *gemm_ms, float *attn_ms,
-                                           uint32_t *gemm_launches, double *gemm_flops);
+                                           uint32_t *gemm_launches, double *gemm_flops, float *other_ms);
 
 #ifdef __cplusplus
 }

@@ -97,6 +97,28 @@ def test_rerank_scores(ctx, precision):
 
 
 @pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_rerank_scores_with_the_device_head(ctx, precision):
+    a, meta = load_golden("tiny_bert")
+    m = ctx.load(models.bert_desc(a, meta))
+    s = m.session(8, 32, precision, task=abi.TURBO_TASK_RERANK)
+    ids, types, mask, pair, z = rerank_rows()
+    s.set_head(z["cls_w"], z["cls_b"], z["pooler_w"], z["pooler_b"])
+    s.write(ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
+    s.run()
+    sc = s.head_scores()
+    host = oracle.rerank_head(s.read(), z["pooler_w"], z["pooler_b"], z["cls_w"], z["cls_b"])
+    assert np.abs(sc - host).max() < 1e-6  # the same F64 head on the same vectors
+    scores = np.full(4, -np.inf)
+    for i, p in enumerate(pair):
+        scores[p] = max(scores[p], sc[i])
+    ref = z["scores"].ravel()
+    bound = 1e-4 if precision == EXACT else 1e-2 * np.abs(ref).max()
+    assert np.abs(scores - ref).max() < bound
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
 @pytest.mark.parametrize("pooling", [abi.TURBO_POOLING_MEAN, abi.TURBO_POOLING_CLS, abi.TURBO_POOLING_LAST])
 def test_poolings_and_cut_vs_oracle(ctx, precision, pooling):
     d = models.synthetic("minilm", 0, layers=2)

@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(F32_WARPS * 32)
 attn_simt_kernel(const T *__restrict__ qkv, T *__restrict__ ctx, const uint8_t *__restrict__ live,
                  const AttnItem *__restrict__ items, int d, int h, int window, int lp) {
     extern __shared__ float sm[];
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnItem it = items[blockIdx.x];
     const int head = blockIdx.y;
@@ -131,6 +133,8 @@ attn_mma_kernel(const T *__restrict__ qkv, T *__restrict__ ctx, const uint8_t *_
     __shared__ __align__(128) T Qs[BQ * LDS];
     __shared__ __align__(128) T Ks[2][BKEY * LDS];
     __shared__ __align__(128) T Vs[2][BKEY * LDS];
+    pdl_wait();
+    pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const AttnItem it = items[blockIdx.x];
@@ -285,12 +289,11 @@ cudaError_t launch_mma(const void *qkv, void *ctx, const uint8_t *live, const At
     dim3 grid(n_items, heads);
     const float sl2 = (1.0f / sqrtf((float)d)) * 1.4426950408889634f;
     switch (d) {
-    case 16: attn_mma_kernel<T, 16><<<grid, 128, 0, s>>>((const T *)qkv, (T *)ctx, live, items, h, window, sl2); break;
-    case 32: attn_mma_kernel<T, 32><<<grid, 128, 0, s>>>((const T *)qkv, (T *)ctx, live, items, h, window, sl2); break;
-    case 64: attn_mma_kernel<T, 64><<<grid, 128, 0, s>>>((const T *)qkv, (T *)ctx, live, items, h, window, sl2); break;
+    case 16: return launch_pdl(attn_mma_kernel<T, 16>, grid, 128, 0, s, (const T *)qkv, (T *)ctx, live, items, h, window, sl2);
+    case 32: return launch_pdl(attn_mma_kernel<T, 32>, grid, 128, 0, s, (const T *)qkv, (T *)ctx, live, items, h, window, sl2);
+    case 64: return launch_pdl(attn_mma_kernel<T, 64>, grid, 128, 0, s, (const T *)qkv, (T *)ctx, live, items, h, window, sl2);
     default: return cudaErrorNotSupported;
     }
-    return cudaGetLastError();
 }
 
 
@@ -305,9 +308,8 @@ cudaError_t launch_simt(const void *qkv, void *ctx, const uint8_t *tok_live, con
         if (e != cudaSuccess) return e;
     }
     dim3 grid(n_items, heads);
-    attn_simt_kernel<T><<<grid, F32_WARPS * 32, smem, s>>>((const T *)qkv, (T *)ctx, tok_live, items, head_dim, hidden,
-                                                           window, lp);
-    return cudaGetLastError();
+    return launch_pdl(attn_simt_kernel<T>, grid, F32_WARPS * 32, smem, s, (const T *)qkv, (T *)ctx, tok_live, items,
+                      head_dim, hidden, window, lp);
 }
 
 }  // namespace

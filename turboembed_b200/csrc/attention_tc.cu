@@ -106,6 +106,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t fmt = Elem<T>::dt == Dt::BF16 ? 1u : 0u;
+    pdl_wait();  // qkv and the plan are an earlier kernel's and copy's
+    pdl_trigger();
 
     if (warp == 4) {
         if (lane == 0) {
@@ -345,8 +347,8 @@ cudaError_t launch(const CUtensorMap &mq, const CUtensorMap &mkv, void *ctx, con
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
     const int units = n_items * heads;
     const int grid = units < sms * CTAS_PER_SM ? units : sms * CTAS_PER_SM;
-    attn_tc_kernel<T><<<grid, 160, SMEM, s>>>(mq, mkv, (T *)ctx, live, items, n_items, heads, h, window, sl2, fault);
-    return cudaGetLastError();
+    return launch_pdl(attn_tc_kernel<T>, grid, 160, SMEM, s, mq, mkv, (T *)ctx, live, items, n_items, heads, h, window,
+                      sl2, fault);
 }
 
 }  // namespace

@@ -214,10 +214,15 @@ struct Session {
     std::vector<double> prof_flops;
     int prof_n = 0;
     bool rerun_ok = false;
+    // The cross-encoder head on the device (set by turbo_b200_session_set_head).
+    float *head_wt = nullptr, *head_bp = nullptr, *head_wc = nullptr, *head_scores = nullptr;
+    float head_bc = 0.0f;
 
     ~Session() {
         DeviceScope ds(ctx->device);
-        for (void *p : {x, xn, qkv, ctxb, ffn, (void *)plan_dev}) cudaFree(p);
+        for (void *p : {x, xn, qkv, ctxb, ffn, (void *)plan_dev, (void *)head_wt, (void *)head_bp, (void *)head_wc,
+                        (void *)head_scores})
+            cudaFree(p);
         if (plan_host) cudaFreeHost(plan_host);
         if (uploaded) cudaEventDestroy(uploaded);
         if (run0) cudaEventDestroy(run0);
@@ -1021,7 +1026,10 @@ cudaError_t encode(Session *s) {
         return timed(s, 1, 0.0, [&] { return attention_raw(window); });
     };
     if (!m->modern) {
-        e = embed_layer_norm(dt, s->x, pk, m->word, m->pos, m->type, m->pos_offset, m->emb_ln_w, m->emb_ln_b, h, m->eps, st);
+        e = timed(s, 2, 0.0, [&] {
+            return embed_layer_norm(dt, s->x, pk, m->word, m->pos, m->type, m->pos_offset, m->emb_ln_w, m->emb_ln_b, h,
+                                    m->eps, st);
+        });
         if (e != cudaSuccess) return e;
         for (int l = 0; l < m->layers; ++l) {
             const LayerWeights &L = ws.layers[l];
@@ -1032,7 +1040,9 @@ cudaError_t encode(Session *s) {
             Epilogue o;
             o.kind = EPI_RESIDUAL, o.bias = L.out.bias, o.out = s->x, o.ldo = h;
             if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
-            if ((e = layer_norm(dt, s->x, s->x, L.ln1_w, L.ln1_b, T, h, m->eps, st)) != cudaSuccess) return e;
+            if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln1_w, L.ln1_b, T, h, m->eps, st); })) !=
+                cudaSuccess)
+                return e;
             Epilogue f1;
             // FASTEST takes the tanh form, as the reference's FASTEST does;
             // EXACT and MODEL keep the erf form the CPU path computes.
@@ -1042,7 +1052,9 @@ cudaError_t encode(Session *s) {
             Epilogue f2;
             f2.kind = EPI_RESIDUAL, f2.bias = L.ffn_out.bias, f2.out = s->x, f2.ldo = h;
             if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) return e;
-            if ((e = layer_norm(dt, s->x, s->x, L.ln2_w, L.ln2_b, T, h, m->eps, st)) != cudaSuccess) return e;
+            if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln2_w, L.ln2_b, T, h, m->eps, st); })) !=
+                cudaSuccess)
+                return e;
         }
         return cudaSuccess;
     }
@@ -1217,7 +1229,62 @@ TB_EXPORT void turbo_cuda_fail_allocation(int32_t after) { g_fail_alloc_after.st
 
 TB_EXPORT const char *turbo_cuda_arch_label(void) { return "b200"; }
 
+TB_EXPORT uint64_t turbo_b200_kernel_launches(void) { return launch_counter().load(); }
+
 TB_EXPORT const turbo_backend *turbo_b200_backend(void) { return &turbo_cuda_backend; }
+
+TB_EXPORT int32_t turbo_b200_session_set_head(void *session, const float *pooler_w, const float *pooler_b,
+                                              const float *cls_w, float cls_b, turbo_error *err) {
+    return guarded(err, [&]() -> int32_t {
+        auto *s = (Session *)session;
+        if (!s || !cls_w) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "a session and a classifier are required");
+        const int h = s->m->hidden;
+        DeviceScope ds(s->ctx->device);
+        for (float **p : {&s->head_wt, &s->head_bp, &s->head_wc, &s->head_scores}) {
+            cudaFree(*p);
+            *p = nullptr;
+        }
+        std::vector<float> wt;
+        if (pooler_w) {
+            wt.resize((size_t)h * h);
+            for (int o = 0; o < h; ++o)
+                for (int k = 0; k < h; ++k) wt[(size_t)k * h + o] = pooler_w[(size_t)o * h + k];
+            CK(dmalloc((void **)&s->head_wt, wt.size() * 4), "set_head");
+            CK(dmalloc((void **)&s->head_bp, (size_t)h * 4), "set_head");
+            CK(cudaMemcpy(s->head_wt, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice), "set_head");
+            CK(cudaMemcpy(s->head_bp, pooler_b, (size_t)h * 4, cudaMemcpyHostToDevice), "set_head");
+        }
+        CK(dmalloc((void **)&s->head_wc, (size_t)h * 4), "set_head");
+        CK(cudaMemcpy(s->head_wc, cls_w, (size_t)h * 4, cudaMemcpyHostToDevice), "set_head");
+        CK(dmalloc((void **)&s->head_scores, (size_t)s->cap_vectors * 4), "set_head");
+        s->head_bc = cls_b;
+        ok(err);
+        return TURBO_OK;
+    });
+}
+
+TB_EXPORT int32_t turbo_b200_session_head_scores(void *session, uint32_t n, float *scores, turbo_error *err) {
+    return guarded(err, [&]() -> int32_t {
+        auto *s = (Session *)session;
+        if (!s || !s->head_wc) return fail(err, TURBO_E_INVALID_STATE, 0, "no head set on the session");
+        if (n > (uint32_t)s->cap_vectors || n > (uint32_t)s->n_vectors)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "%u scores, the last run pooled %d vectors", n, s->n_vectors);
+        if (s->output_dim != (uint32_t)s->m->hidden)
+            return fail(err, TURBO_E_INVALID_STATE, 0, "the head reads whole vectors: write with output_dim = hidden");
+        DeviceScope ds(s->ctx->device);
+        std::lock_guard<std::mutex> g(s->ctx->mu);
+        CK(rerank_head((const float *)s->out->ptr, (int)n, s->m->hidden, s->head_wt, s->head_bp, s->head_wc, s->head_bc,
+                       s->head_scores, s->ctx->stream),
+           "head");
+        // The session's device span (turbo_b200_session_times) now ends
+        // after the head: run and head are one step of a rerank.
+        cudaEventRecord(s->run1, s->ctx->stream);
+        CK(cudaMemcpyAsync(scores, s->head_scores, (size_t)n * 4, cudaMemcpyDeviceToHost, s->ctx->stream), "head");
+        CK(cudaStreamSynchronize(s->ctx->stream), "head");
+        ok(err);
+        return TURBO_OK;
+    });
+}
 
 TB_EXPORT int32_t turbo_b200_buffer_copy(void *buffer, void *dst, uint64_t bytes, void *stream) {
     auto *b = (Buffer *)buffer;
@@ -1251,13 +1318,13 @@ TB_EXPORT int32_t turbo_b200_session_profile(void *session, uint32_t on) {
 }
 
 TB_EXPORT int32_t turbo_b200_session_times(void *session, float *run_ms, float *gemm_ms, float *attn_ms,
-                                           uint32_t *gemm_launches, double *gemm_flops) {
+                                           uint32_t *gemm_launches, double *gemm_flops, float *other_ms) {
     auto *s = (Session *)session;
     DeviceScope ds(s->ctx->device);
     float ms = 0.0f;
     if (cudaEventElapsedTime(&ms, s->run0, s->run1) != cudaSuccess) return TURBO_E_RUNTIME;
     *run_ms = ms;
-    *gemm_ms = *attn_ms = 0.0f;
+    *gemm_ms = *attn_ms = *other_ms = 0.0f;
     *gemm_launches = 0;
     *gemm_flops = 0.0;
     for (int i = 0; i < s->prof_n; ++i) {
@@ -1267,8 +1334,10 @@ TB_EXPORT int32_t turbo_b200_session_times(void *session, float *run_ms, float *
             *gemm_ms += t;
             *gemm_launches += 1;
             *gemm_flops += s->prof_flops[i];
-        } else {
+        } else if (s->prof_kind[i] == 1) {
             *attn_ms += t;
+        } else {
+            *other_ms += t;
         }
     }
     return TURBO_OK;

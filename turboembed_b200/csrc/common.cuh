@@ -7,7 +7,57 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <cstdlib>
+#include <utility>
+
 namespace tb {
+
+// Programmatic dependent launch. Every kernel of a run is launched with
+// programmatic stream serialization: it may start while the kernel before it
+// finishes, so it runs its prologue, then waits (pdl_wait) before reading
+// anything an earlier kernel wrote, and lets the next kernel start launching
+// (pdl_trigger). Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Whether launches use programmatic stream serialization: on unless the
+// environment sets TB_PDL=0 (an A/B switch, read once).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char *v = getenv("TB_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// Every kernel this library launches, counted on the host as it is launched
+// (read by turbo_b200_kernel_launches).
+inline std::atomic<unsigned long long> &launch_counter() {
+    static std::atomic<unsigned long long> n{0};
+    return n;
+}
+
+inline cudaError_t counted(cudaError_t e) {
+    if (e == cudaSuccess) launch_counter().fetch_add(1, std::memory_order_relaxed);
+    return e;
+}
+
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return counted(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
 
 // The element type a buffer holds. F32 is the EXACT tier's; F16 and BF16
 // the FASTEST and MODEL tiers'.

@@ -31,6 +31,8 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T *__restrict__ a,
                                                         const T *__restrict__ w, int M, int N, int K, Epilogue e) {
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[BK][BN + 4];
+    pdl_wait();
+    pdl_trigger();
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     float acc[8][8];
@@ -97,11 +99,11 @@ cudaError_t gemm_simt(Dt dt, const void *a, int64_t lda, const void *w, int M, i
     if (epi.kind == EPI_ROPE) return cudaErrorNotSupported;
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
     switch (dt) {
-    case Dt::F32: gemm_simt_kernel<float><<<grid, 256, 0, s>>>((const float *)a, lda, (const float *)w, M, N, K, epi); break;
-    case Dt::F16: gemm_simt_kernel<__half><<<grid, 256, 0, s>>>((const __half *)a, lda, (const __half *)w, M, N, K, epi); break;
-    case Dt::BF16: gemm_simt_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16 *)a, lda, (const __nv_bfloat16 *)w, M, N, K, epi); break;
+    case Dt::F32: return launch_pdl(gemm_simt_kernel<float>, grid, 256, 0, s, (const float *)a, lda, (const float *)w, M, N, K, epi);
+    case Dt::F16: return launch_pdl(gemm_simt_kernel<__half>, grid, 256, 0, s, (const __half *)a, lda, (const __half *)w, M, N, K, epi);
+    case Dt::BF16: return launch_pdl(gemm_simt_kernel<__nv_bfloat16>, grid, 256, 0, s, (const __nv_bfloat16 *)a, lda, (const __nv_bfloat16 *)w, M, N, K, epi);
     }
-    return cudaGetLastError();
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace tb

@@ -285,6 +285,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // A and the residual are an earlier kernel's
+    pdl_trigger();
 
     const int m_tiles = (M + TM - 1) / TM, n_tiles = (N + BN - 1) / BN;
     const int tiles = m_tiles * n_tiles, kblocks = (K + BK - 1) / BK;
@@ -437,16 +439,20 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
     cfg.blockDim = dim3(128 + 128 * EPI_WG);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (!pdl_enabled()) attr[0].val.programmaticStreamSerializationAllowed = 0;
     if (PAIR) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
     }
-    return cudaLaunchKernelEx(&cfg, kern, maps.a, maps.w, maps.out, maps.has_out ? 1 : 0, M, N, K, e, fault);
+    return counted(cudaLaunchKernelEx(&cfg, kern, maps.a, maps.w, maps.out, maps.has_out ? 1 : 0, M, N, K, e, fault));
 }
 
 template <class T>

@@ -73,6 +73,14 @@ cudaError_t layer_norm(Dt dt, const void *src, void *dst, const float *ln_w, con
                        int hidden, double eps, cudaStream_t s);
 cudaError_t pool_vectors(Dt dt, const void *x, const uint8_t *tok_live, const PoolItem *items, int count,
                          int hidden, int output_dim, int normalize_l2, float *out, cudaStream_t s);
+// The cross-encoder head on pooled CLS vectors x [n, h] F32 (the session's
+// output): score[i] = b_c + sum_o w_c[o] * f32(tanh(b_p[o] + sum_k W_p[o][k]
+// x[i][k])), the sums in F64 (core/src/session/rerank.rs:170-188); wt_p is
+// W_p transposed, [k][o]. Without a pooler (wt_p null) score[i] = b_c +
+// w_c . x_i.
+cudaError_t rerank_head(const float *x, int n, int h, const float *wt_p, const float *b_p, const float *w_c, float b_c,
+                        float *scores, cudaStream_t s);
+
 // In place on qkv [tokens, 3 * hidden]: Q and K of each head rotated pair
 // (i, i + d/2) by the token's position.
 cudaError_t rope_qk(Dt dt, void *qkv, const int32_t *tok_pos, const float *cos, const float *sin, int tokens,

@@ -23,6 +23,8 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(T *__restrict__ x, Packed
                                                        const float *__restrict__ pos, const float *__restrict__ type,
                                                        int pos_offset, const float *__restrict__ ln_w,
                                                        const float *__restrict__ ln_b, int h, double eps) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < p.tokens; t += warps) {
@@ -109,6 +111,8 @@ __global__ void __launch_bounds__(256) ln_vec_kernel(const T *__restrict__ src, 
         wb[1024 + i] = ln_b ? ln_b[i] : 0.0f;
     }
     __syncthreads();
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int chunks = h / V::N;
@@ -172,6 +176,8 @@ __global__ void __launch_bounds__(256) pool_kernel(const T *__restrict__ x, cons
                                                    const PoolItem *__restrict__ items, int h, int od, int l2,
                                                    float *__restrict__ out) {
     constexpr int PER = 4;  // columns per thread: output_dim up to 1024
+    pdl_wait();
+    pdl_trigger();
     const PoolItem it = items[blockIdx.x];
     float acc[PER];
 #pragma unroll
@@ -223,6 +229,8 @@ __global__ void __launch_bounds__(256) pool_kernel(const T *__restrict__ x, cons
 template <class T>
 __global__ void rope_kernel(T *qkv, const int32_t *__restrict__ tok_pos, const float *__restrict__ cos_t,
                             const float *__restrict__ sin_t, int tokens, int h, int d) {
+    pdl_wait();
+    pdl_trigger();
     const int half = d / 2;
     const int per_token = h;  // 2 parts x h/2 pairs
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -236,6 +244,38 @@ __global__ void rope_kernel(T *qkv, const int32_t *__restrict__ tok_pos, const f
     const float x1 = ld(base + k), x2 = ld(base + k + half);
     st(base + k, __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn)));
     st(base + k + half, __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn)));
+}
+
+// One block per pooled vector: thread o owns pooler outputs o, o + 256, ..
+__global__ void __launch_bounds__(256) rerank_head_kernel(const float *__restrict__ x, int h,
+                                                          const float *__restrict__ wt_p, const float *__restrict__ b_p,
+                                                          const float *__restrict__ w_c, float b_c,
+                                                          float *__restrict__ scores) {
+    __shared__ float xs[1024];
+    __shared__ double part[8];
+    pdl_wait();
+    pdl_trigger();
+    const float *xi = x + (int64_t)blockIdx.x * h;
+    for (int k = threadIdx.x; k < h; k += blockDim.x) xs[k] = xi[k];
+    __syncthreads();
+    double dot = 0.0;
+    for (int o = threadIdx.x; o < h; o += blockDim.x) {
+        float pooled = xs[o];
+        if (wt_p) {
+            double a = (double)b_p[o];
+            for (int k = 0; k < h; ++k) a += (double)wt_p[(int64_t)k * h + o] * (double)xs[k];
+            pooled = (float)tanh(a);
+        }
+        dot += (double)w_c[o] * (double)pooled;
+    }
+    dot = warp_sum(dot);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = dot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double v = (double)b_c;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += part[w];
+        scores[blockIdx.x] = (float)v;
+    }
 }
 
 template <class T> __global__ void narrow_kernel(const float *__restrict__ src, T *__restrict__ dst, int64_t n) {
@@ -266,11 +306,11 @@ cudaError_t embed_layer_norm(Dt dt, void *x, const Packed &p, const float *word,
     if (p.tokens == 0) return cudaSuccess;
     int g = grid_for(p.tokens);
     switch (dt) {
-    case Dt::F32: embed_ln_kernel<float><<<g, 256, 0, s>>>((float *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps); break;
-    case Dt::F16: embed_ln_kernel<__half><<<g, 256, 0, s>>>((__half *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps); break;
-    case Dt::BF16: embed_ln_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((__nv_bfloat16 *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps); break;
+    case Dt::F32: return launch_pdl(embed_ln_kernel<float>, g, 256, 0, s, (float *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+    case Dt::F16: return launch_pdl(embed_ln_kernel<__half>, g, 256, 0, s, (__half *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+    case Dt::BF16: return launch_pdl(embed_ln_kernel<__nv_bfloat16>, g, 256, 0, s, (__nv_bfloat16 *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
     }
-    return cudaGetLastError();
+    return cudaErrorInvalidValue;
 }
 
 template <class T>
@@ -282,13 +322,12 @@ cudaError_t ln_launch(const void *src, void *dst, const float *w, const float *b
     const int g = std::min(148 * 3, (tokens + 15) / 16);
     const T *in = (const T *)src;
     T *out = (T *)dst;
-    if (cpl <= 1) ln_vec_kernel<T, 1><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
-    else if (cpl <= 2) ln_vec_kernel<T, 2><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
-    else if (cpl <= 3) ln_vec_kernel<T, 3><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
-    else if (cpl <= 4) ln_vec_kernel<T, 4><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
-    else if (cpl <= 8) ln_vec_kernel<T, 8><<<g, 256, 0, s>>>(in, out, w, b, tokens, h, eps);
-    else return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (cpl <= 1) return launch_pdl(ln_vec_kernel<T, 1>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
+    if (cpl <= 2) return launch_pdl(ln_vec_kernel<T, 2>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
+    if (cpl <= 3) return launch_pdl(ln_vec_kernel<T, 3>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
+    if (cpl <= 4) return launch_pdl(ln_vec_kernel<T, 4>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
+    if (cpl <= 8) return launch_pdl(ln_vec_kernel<T, 8>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t layer_norm(Dt dt, const void *src, void *dst, const float *ln_w, const float *ln_b, int tokens, int hidden,
@@ -308,11 +347,18 @@ cudaError_t pool_vectors(Dt dt, const void *x, const uint8_t *tok_live, const Po
     if (output_dim > 1024 || output_dim > hidden) return cudaErrorInvalidValue;
     if (count == 0) return cudaSuccess;
     switch (dt) {
-    case Dt::F32: pool_kernel<float><<<count, 256, 0, s>>>((const float *)x, tok_live, items, hidden, output_dim, normalize_l2, out); break;
-    case Dt::F16: pool_kernel<__half><<<count, 256, 0, s>>>((const __half *)x, tok_live, items, hidden, output_dim, normalize_l2, out); break;
-    case Dt::BF16: pool_kernel<__nv_bfloat16><<<count, 256, 0, s>>>((const __nv_bfloat16 *)x, tok_live, items, hidden, output_dim, normalize_l2, out); break;
+    case Dt::F32: return launch_pdl(pool_kernel<float>, count, 256, 0, s, (const float *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+    case Dt::F16: return launch_pdl(pool_kernel<__half>, count, 256, 0, s, (const __half *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+    case Dt::BF16: return launch_pdl(pool_kernel<__nv_bfloat16>, count, 256, 0, s, (const __nv_bfloat16 *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
     }
-    return cudaGetLastError();
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t rerank_head(const float *x, int n, int h, const float *wt_p, const float *b_p, const float *w_c, float b_c,
+                        float *scores, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    if (h > 1024) return cudaErrorInvalidValue;
+    return launch_pdl(rerank_head_kernel, n, 256, 0, s, x, h, wt_p, b_p, w_c, b_c, scores);
 }
 
 cudaError_t rope_qk(Dt dt, void *qkv, const int32_t *tok_pos, const float *cos, const float *sin, int tokens, int hidden,
@@ -321,11 +367,11 @@ cudaError_t rope_qk(Dt dt, void *qkv, const int32_t *tok_pos, const float *cos, 
     int64_t n = (int64_t)tokens * hidden;
     int g = (int)((n + 255) / 256);
     switch (dt) {
-    case Dt::F32: rope_kernel<float><<<g, 256, 0, s>>>((float *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim); break;
-    case Dt::F16: rope_kernel<__half><<<g, 256, 0, s>>>((__half *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim); break;
-    case Dt::BF16: rope_kernel<__nv_bfloat16><<<g, 256, 0, s>>>((__nv_bfloat16 *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim); break;
+    case Dt::F32: return launch_pdl(rope_kernel<float>, g, 256, 0, s, (float *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim);
+    case Dt::F16: return launch_pdl(rope_kernel<__half>, g, 256, 0, s, (__half *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim);
+    case Dt::BF16: return launch_pdl(rope_kernel<__nv_bfloat16>, g, 256, 0, s, (__nv_bfloat16 *)qkv, tok_pos, cos, sin, tokens, hidden, head_dim);
     }
-    return cudaGetLastError();
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace tb

@@ -220,6 +220,27 @@ class Session:
         _check(self.t.buffer_read(self.last_run.output, _ptr(dst), n * 4, C.byref(err)), err, "buffer_read")
         return dst.reshape(self._count, self._out_dim)
 
+    def set_head(self, cls_w, cls_b, pooler_w=None, pooler_b=None):
+        """turbo_b200_session_set_head: the cross-encoder head on the device."""
+        lib = library()
+        f = lib.turbo_b200_session_set_head
+        f.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.POINTER(abi.turbo_error)]
+        self._head = [None if a is None else np.ascontiguousarray(a, np.float32) for a in (pooler_w, pooler_b, cls_w)]
+        err = abi.new_error()
+        _check(f(self.h, _ptr(self._head[0]), _ptr(self._head[1]), _ptr(self._head[2]), float(np.asarray(cls_b).ravel()[0]),
+                 C.byref(err)), err, "set_head")
+
+    def head_scores(self, n=None):
+        """The head's score of each of the last run's first n vectors."""
+        lib = library()
+        f = lib.turbo_b200_session_head_scores
+        f.argtypes = [C.c_void_p, C.c_uint32, C.c_void_p, C.POINTER(abi.turbo_error)]
+        n = self._count if n is None else n
+        out = np.zeros(n, np.float32)
+        err = abi.new_error()
+        _check(f(self.h, n, _ptr(out), C.byref(err)), err, "head_scores")
+        return out
+
     def embed(self, ids, mask, types=None, **kw):
         self.write(ids, mask, types, **kw)
         self.run()
