@@ -133,6 +133,12 @@ TB_EXPORT int32_t turbo_b200_session_rerun(void *session);
  * bench hands pooled vectors to an NCCL all-gather. */
 TB_EXPORT int32_t turbo_b200_buffer_copy(void *buffer, void *dst, uint64_t bytes, void *stream);
 TB_EXPORT int32_t turbo_b200_session_profile(void *session, uint32_t on);
+/* With profiling on, each timed launch of the last run in launch order:
+ * its kind (0 GEMM, 1 attention, 2 gather / LayerNorm), device time and
+ * algorithmic FLOPs (GEMMs only). Returns how many were written (at most
+ * cap), or -1. */
+TB_EXPORT int32_t turbo_b200_session_launch_times(void *session, uint32_t cap, int32_t *kinds, float *ms,
+                                                  double *flops);
 TB_EXPORT int32_t turbo_b200_session_times(void *session, float *run_ms, float *gemm_ms, float *attn_ms,
                                            uint32_t *gemm_launches, double *gemm_flops, float *other_ms);
 

@@ -93,6 +93,9 @@ def test_tcgen05_gemm_rope(dtype, head_dim, h):
     want = ref_gemm(dtype, 4, a, w, None, None, head_dim, pos, cos, sin)
     tol = 8e-3 if dtype == BF16 else 1.5e-3
     assert rel_err(got, want) < tol
+    # TMA-staged stores (variant 0) and direct stores (2) write the same bits.
+    one = runtime.gemm_check(dtype, 2, 4, a, w, None, None, head_dim, pos, cos, sin)
+    assert np.array_equal(got, one)
     simt = runtime.gemm_check(dtype, 1, 4, a, w, None, None, head_dim, pos, cos, sin)
     assert rel_err(got, simt) < tol
 

@@ -79,9 +79,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     uint8_t *sQ = smem, *sP = smem + Q_BYTES, *sK = sP + P_BYTES, *sV = sK + KV_BYTES;
     uint8_t *bars = sV + KV_BYTES;
     const uint32_t bar_q = smem_u32(bars), bar_k = bar_q + 8, bar_v = bar_q + 16, bar_s = bar_q + 24;
-    const uint32_t bar_p = bar_q + 32, bar_o = bar_q + 40;
-    uint32_t *tmem_slot = (uint32_t *)(bars + 48);
-    volatile int *abort_flag = (volatile int *)(bars + 56);
+    const uint32_t bar_p = bar_q + 32, bar_o = bar_q + 40, bar_sf = bar_q + 48;
+    uint32_t *tmem_slot = (uint32_t *)(bars + 64);
+    volatile int *abort_flag = (volatile int *)(bars + 72);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = n_items * heads;
@@ -93,6 +93,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         mbar_init(bar_s, 1);
         mbar_init(bar_p, 128);
         mbar_init(bar_o, 1);
+        mbar_init(bar_sf, 128);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
@@ -141,7 +142,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                              kk > 0 ? 1u : 0u);
                 umma_commit(bar_s);
             };
-            uint32_t g = 0, qc = 0;  // chunks and units done so far
+            // g: chunks of this CTA so far (every barrier but bar_q completes
+            // once a chunk); qc: units so far.
+            uint32_t g = 0, qc = 0;
             bool ok = true;
             int u = blockIdx.x;
             if (u < units) {
@@ -156,6 +159,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 const int nch = (khi - klo + KT - 1) / KT;
                 const int next = u + gridDim.x;
                 if (!(ok = mbar_wait(bar_q, qc & 1, abort_flag, fault))) break;
+                // The softmax has S of the previous chunk in registers.
+                if (g > 0 && !(ok = mbar_wait(bar_sf, (g - 1) & 1, abort_flag, fault))) break;
                 if (!(ok = mbar_wait(bar_k, g & 1, abort_flag, fault))) break;
                 issue_s();
                 for (int j = 0; j < nch && ok; ++j, ++g) {
@@ -167,7 +172,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                         load_q(next);
                         load_k(next, 0);
                     }
-                    // P written (S read, O rescaled) by the softmax; V loaded.
+                    // The next S as soon as the softmax holds this one: it
+                    // runs while the softmax works on this chunk.
+                    if (j + 1 < nch) {
+                        if (!(ok = mbar_wait(bar_sf, par, abort_flag, fault))) break;
+                        if (!(ok = mbar_wait(bar_k, (g + 1) & 1, abort_flag, fault))) break;
+                        issue_s();
+                    }
+                    // P written (O rescaled) by the softmax; V loaded.
                     if (!(ok = mbar_wait(bar_p, par, abort_flag, fault))) break;
                     if (!(ok = mbar_wait(bar_v, par, abort_flag, fault))) break;
                     tc_fence_after();
@@ -177,10 +189,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                         umma_f16(tmem + 64, smem_desc(ap) + (uint64_t)(kk * 2), smem_desc(av + kk * 16 * 128), idpv,
                                  (j | kk) ? 1u : 0u);
                     umma_commit(bar_o);
-                    if (j + 1 < nch) {
-                        if (!(ok = mbar_wait(bar_k, (g + 1) & 1, abort_flag, fault))) break;
-                        issue_s();
-                    }
                     // P V done: V and P are free.
                     if (!(ok = mbar_wait(bar_o, par, abort_flag, fault))) break;
                     if (j + 1 < nch) load_v(u, j + 1);
@@ -216,25 +224,34 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 const bool full = window < 0 && (km0 & km1) == 0xffffffffu;
                 if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
                 tc_fence_after();
-                // Pass 1: the row max of the chunk's valid raw scores (the
-                // scale is positive, so it is applied once after).
-                float mx = -INFINITY;
-#pragma unroll 1
-                for (int half = 0; half < 2; ++half) {
-                    float sv[32];
+                // The chunk's 64 raw scores into registers; then S is free
+                // for the next chunk's Q K^T.
+                float sv[64];
+                {
+                    uint32_t raw[64];
                     __syncwarp();
-                    tmem_ld32(lane_base + half * 32, sv);
-                    if (full) {
+                    tmem_ld32_async(lane_base, raw);
+                    tmem_ld32_async(lane_base + 32, raw + 32);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
-                    } else {
-                        const uint32_t km = half ? km1 : km0;
+                    for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
+                }
+                tc_fence_before();
+                mbar_arrive(bar_sf);
+                // Invalid keys (masked, past the row, outside the window)
+                // become -inf; the row max of the valid raw scores (the scale
+                // is positive, so it is applied once after).
+                float mx = -INFINITY;
+                if (full) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            bool valid = (km >> i) & 1u;
-                            if (window >= 0) valid = valid && abs(qi - (k0 + half * 32 + i)) <= window;
-                            if (valid) mx = fmaxf(mx, sv[i]);
-                        }
+                    for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        bool valid = (((i < 32) ? km0 : km1) >> (i & 31)) & 1u;
+                        if (window >= 0) valid = valid && abs(qi - (k0 + i)) <= window;
+                        sv[i] = valid ? sv[i] : -INFINITY;
+                        mx = fmaxf(mx, sv[i]);
                     }
                 }
                 mx = mx == -INFINITY ? mx : mx * scale_log2;
@@ -255,50 +272,33 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 }
                 if (j > 0 && __any_sync(0xffffffffu, move)) {
                     __syncwarp();
-                    float o[32];
 #pragma unroll 1
-                    for (int half = 0; half < 2; ++half) {
-                        tmem_ld32(lane_base + 64 + half * 32, o);
+                    for (int q = 0; q < 4; ++q) {
+                        float o[16];
+                        tmem_ld16(lane_base + 64 + q * 16, o);
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= f;
-                        tmem_st32(lane_base + 64 + half * 32, o);
+                        for (int i = 0; i < 16; ++i) o[i] *= f;
+                        tmem_st16(lane_base + 64 + q * 16, o);
                     }
                 }
                 const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
-                // Pass 2: P = 2^(s c - mu) into the swizzled A operand.
+                // P = 2^(s c - mu) (0 for invalid keys: 2^-inf) into the
+                // swizzled A operand of P V, summing the row.
                 float rs = 0.0f;
                 uint8_t *rowp = sP + r * 128;
-#pragma unroll 1
-                for (int half = 0; half < 2; ++half) {
-                    float sv[32];
-                    __syncwarp();
-                    tmem_ld32(lane_base + half * 32, sv);
-                    if (full) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            sv[i] = ex2(fmaf(sv[i], scale_log2, -mu));
-                            rs += sv[i];
-                        }
-                    } else {
-                        const uint32_t km = half ? km1 : km0;
+                for (int i = 0; i < 64; ++i) {
+                    sv[i] = ex2(fmaf(sv[i], scale_log2, -mu));
+                    rs += sv[i];
+                }
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            bool valid = (km >> i) & 1u;
-                            if (window >= 0) valid = valid && abs(qi - (k0 + half * 32 + i)) <= window;
-                            sv[i] = valid ? ex2(fmaf(sv[i], scale_log2, -mu)) : 0.0f;
-                            rs += sv[i];
-                        }
-                    }
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint4 w;
-                        w.x = pack2<T>(sv[8 * q + 0], sv[8 * q + 1]);
-                        w.y = pack2<T>(sv[8 * q + 2], sv[8 * q + 3]);
-                        w.z = pack2<T>(sv[8 * q + 4], sv[8 * q + 5]);
-                        w.w = pack2<T>(sv[8 * q + 6], sv[8 * q + 7]);
-                        const int cc = half * 4 + q;
-                        *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
-                    }
+                for (int cc = 0; cc < 8; ++cc) {
+                    uint4 w;
+                    w.x = pack2<T>(sv[8 * cc + 0], sv[8 * cc + 1]);
+                    w.y = pack2<T>(sv[8 * cc + 2], sv[8 * cc + 3]);
+                    w.z = pack2<T>(sv[8 * cc + 4], sv[8 * cc + 5]);
+                    w.w = pack2<T>(sv[8 * cc + 6], sv[8 * cc + 7]);
+                    *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
                 }
                 l += rs;
                 fence_async_smem();

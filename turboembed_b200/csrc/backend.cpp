@@ -1059,7 +1059,9 @@ cudaError_t encode(Session *s) {
         return cudaSuccess;
     }
     // ModernBERT (core/src/cpu/encoder/rotary/mod.rs:87-175): pre-norm.
-    e = embed_layer_norm(dt, s->x, pk, m->word, nullptr, nullptr, 0, m->emb_ln_w, nullptr, h, m->eps, st);
+    e = timed(s, 2, 0.0, [&] {
+        return embed_layer_norm(dt, s->x, pk, m->word, nullptr, nullptr, 0, m->emb_ln_w, nullptr, h, m->eps, st);
+    });
     if (e != cudaSuccess) return e;
     const size_t half_tab = (size_t)m->positions * m->rope_pairs;
     for (int l = 0; l < m->layers; ++l) {
@@ -1069,28 +1071,32 @@ cudaError_t encode(Session *s) {
         const void *src = s->x;
         const CUtensorMap *src_map = &s->map_x;
         if (l > 0) {
-            if ((e = layer_norm(dt, s->x, s->xn, L.ln1_w, nullptr, T, h, m->eps, st)) != cudaSuccess) return e;
+            if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->xn, L.ln1_w, nullptr, T, h, m->eps, st); })) !=
+                cudaSuccess)
+                return e;
             src = s->xn;
             src_map = &s->map_xn;
         }
         Epilogue q;
         q.kind = EPI_ROPE, q.out = s->qkv, q.ldo = 3 * h, q.cos = cos_t, q.sin = sin_t, q.tok_pos = pk.tok_pos;
         q.head_dim = dh, q.rope_cols = 2 * h;
-        if ((e = linear(s, src_map, src, L.qkv, q, T)) != cudaSuccess) return e;
+        if ((e = linear(s, src_map, src, L.qkv, q, T, &s->out_qkv)) != cudaSuccess) return e;
         if ((e = attention(global ? -1 : m->window)) != cudaSuccess) return e;
         Epilogue o;
         o.kind = EPI_RESIDUAL, o.out = s->x, o.ldo = h;
         if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
-        if ((e = layer_norm(dt, s->x, s->xn, L.ln2_w, nullptr, T, h, m->eps, st)) != cudaSuccess) return e;
+        if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->xn, L.ln2_w, nullptr, T, h, m->eps, st); })) !=
+            cudaSuccess)
+            return e;
         Epilogue g;
         g.kind = EPI_GATED, g.out = s->ffn, g.ldo = I, g.act = m->act;
-        if ((e = linear(s, &s->map_xn, s->xn, L.ffn_in, g, T)) != cudaSuccess) return e;
+        if ((e = linear(s, &s->map_xn, s->xn, L.ffn_in, g, T, &s->out_ffn)) != cudaSuccess) return e;
         Epilogue f2;
         f2.kind = EPI_RESIDUAL, f2.out = s->x, f2.ldo = h;
         if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) return e;
     }
     (void)es;
-    return layer_norm(dt, s->x, s->x, m->final_w, nullptr, T, h, m->eps, st);
+    return timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, m->final_w, nullptr, T, h, m->eps, st); });
 }
 
 int32_t tb_session_run(void *p, turbo_backend_run *out, turbo_error *err) {
@@ -1315,6 +1321,20 @@ TB_EXPORT int32_t turbo_b200_session_profile(void *session, uint32_t on) {
         s->prof_flops.assign(pairs, 0.0);
     }
     return TURBO_OK;
+}
+
+TB_EXPORT int32_t turbo_b200_session_launch_times(void *session, uint32_t cap, int32_t *kinds, float *ms,
+                                                  double *flops) {
+    auto *s = (Session *)session;
+    if (!s) return -1;
+    DeviceScope ds(s->ctx->device);
+    const int n = s->prof_n < (int)cap ? s->prof_n : (int)cap;
+    for (int i = 0; i < n; ++i) {
+        if (cudaEventElapsedTime(&ms[i], s->prof_ev[2 * i], s->prof_ev[2 * i + 1]) != cudaSuccess) return -1;
+        kinds[i] = s->prof_kind[i];
+        flops[i] = s->prof_flops[i];
+    }
+    return n;
 }
 
 TB_EXPORT int32_t turbo_b200_session_times(void *session, float *run_ms, float *gemm_ms, float *attn_ms,

@@ -99,43 +99,103 @@ struct StoreStage {
     uint32_t nstore;
 };
 
+// Stage 32 values of this lane's row in the warp's swizzled [32 x 32] tile
+// and store the tile with TMA at (col, ss.row0). Warp-collective.
+// Lane l writes row l: 16-byte chunk q at q ^ ((l >> 1) & 3), the TMA
+// 64-byte swizzle, which spreads each store over all banks.
+template <class T>
+__device__ __forceinline__ void stage_store32(const float *v, int col, StoreStage &ss, const CUtensorMap *out_map) {
+    const int lane = threadIdx.x & 31;
+    uint8_t *buf = ss.buf + (ss.nstore & 1) * 2048;
+    if (lane == 0) tma_store_wait_read<1>();  // the store two chunks back is done reading buf
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint4 u;
+        u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+        u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+        u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+        u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+        *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = u;
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(out_map, smem_u32(buf), col, ss.row0);
+        tma_store_commit();
+    }
+    ++ss.nstore;
+}
+
+// The RoPE epilogue (QKV of rotary models): 64 columns at a time, whole
+// heads of width HD; within each head of the first rope_cols columns,
+// (x1, x2) = (v[k], v[k + HD/2]) -> (x1 cos - x2 sin, x2 cos + x1 sin) with
+// the row's position's table entry k, each product rounded before the
+// subtraction (no contraction), as the CPU path computes it.
+template <class T, int COLS, int HD, class Release>
+__device__ __forceinline__ void rope_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row, bool row_ok,
+                                          int col_base, int N, StoreStage &ss, const CUtensorMap *out_map,
+                                          Release release) {
+    constexpr int HALF = HD / 2;
+#pragma unroll 1
+    for (int c = 0; c < COLS; c += 64) {
+        const int col = col_base + c;
+        uint32_t raw[64];
+        __syncwarp();
+        tmem_ld32_async(tbase + c, raw);
+        tmem_ld32_async(tbase + c + 32, raw + 32);
+        tmem_wait_ld();
+        if (c + 64 >= COLS) release();
+        if (col >= N) continue;
+        float v[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(raw[i]);
+        if (e.bias)
+#pragma unroll
+            for (int i = 0; i < 64; ++i) v[i] += (col + i < N) ? bias_s[col + i] : 0.0f;
+        if (row_ok && col < e.rope_cols) {
+            // The row's table entries, four at a time (HALF is a multiple of 4).
+            const float4 *cs = reinterpret_cast<const float4 *>(e.cos + (int64_t)e.tok_pos[row] * HALF);
+            const float4 *sn = reinterpret_cast<const float4 *>(e.sin + (int64_t)e.tok_pos[row] * HALF);
+#pragma unroll
+            for (int k4 = 0; k4 < HALF / 4; ++k4) {
+                const float4 c4 = cs[k4], s4 = sn[k4];
+                const float ck[4] = {c4.x, c4.y, c4.z, c4.w}, sk[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int k = 4 * k4 + t;
+#pragma unroll
+                    for (int sg = 0; sg < 64; sg += HD) {
+                        if (col + sg < e.rope_cols) {
+                            const float x1 = v[sg + k], x2 = v[sg + k + HALF];
+                            v[sg + k] = __fsub_rn(__fmul_rn(x1, ck[t]), __fmul_rn(x2, sk[t]));
+                            v[sg + k + HALF] = __fadd_rn(__fmul_rn(x2, ck[t]), __fmul_rn(x1, sk[t]));
+                        }
+                    }
+                }
+            }
+        }
+        if (ss.tma) {
+            stage_store32<T>(v, col, ss, out_map);
+            if (col + 32 < N) stage_store32<T>(v + 32, col + 32, ss, out_map);
+        } else if (row_ok) {
+            T *y = (T *)e.out + (int64_t)row * e.ldo + col;
+            store_n<T, 32>(y, v);
+            if (col + 32 < N) store_n<T, 32>(y + 32, v + 32);
+        }
+    }
+}
+
 template <class T, int COLS, class Release>
 __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
                                               bool row_ok, int col_base, int N, const uint4 *res, StoreStage &ss,
                                               const CUtensorMap *out_map, Release release) {
     if (e.kind == EPI_ROPE) {
-        // 64 columns at a time: whole heads of width 16, 32 or 64.
-#pragma unroll 1
-        for (int c = 0; c < COLS; c += 64) {
-            const int col = col_base + c;
-            float v[64];
-            __syncwarp();
-            tmem_ld32(tbase + c, v);
-            tmem_ld32(tbase + c + 32, v + 32);
-            if (c + 64 >= COLS) release();
-            if (col >= N) continue;
-            if (e.bias)
-#pragma unroll
-                for (int i = 0; i < 64; ++i) v[i] += (col + i < N) ? bias_s[col + i] : 0.0f;
-            if (row_ok && col < e.rope_cols) {
-                const int d = e.head_dim, half = d >> 1;
-                const float *cs = e.cos + (int64_t)e.tok_pos[row] * half;
-                const float *sn = e.sin + (int64_t)e.tok_pos[row] * half;
-#pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const int seg = i - (i % d), k = i % d;
-                    if (k < half && col + seg < e.rope_cols) {
-                        const float x1 = v[i], x2 = v[i + half];
-                        v[i] = __fsub_rn(__fmul_rn(x1, cs[k]), __fmul_rn(x2, sn[k]));
-                        v[i + half] = __fadd_rn(__fmul_rn(x2, cs[k]), __fmul_rn(x1, sn[k]));
-                    }
-                }
-            }
-            if (row_ok) {
-                T *y = (T *)e.out + (int64_t)row * e.ldo + col;
-                store_n<T, 32>(y, v);
-                if (col + 32 < N) store_n<T, 32>(y + 32, v + 32);
-            }
+        switch (e.head_dim) {
+        case 64: rope_tile<T, COLS, 64>(e, bias_s, tbase, row, row_ok, col_base, N, ss, out_map, release); break;
+        case 32: rope_tile<T, COLS, 32>(e, bias_s, tbase, row, row_ok, col_base, N, ss, out_map, release); break;
+        case 16: rope_tile<T, COLS, 16>(e, bias_s, tbase, row, row_ok, col_base, N, ss, out_map, release); break;
+        default: rope_tile<T, COLS, 8>(e, bias_s, tbase, row, row_ok, col_base, N, ss, out_map, release); break;
         }
         return;
     }
@@ -148,6 +208,25 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
         if (c2 + 32 < COLS) tmem_ld32_async(tbase + c2 + 32, raw[1]);
         tmem_wait_ld();
         if (c2 + 64 >= COLS) release();
+        if (e.kind == EPI_GATED && ss.tma) {
+            // 64 interleaved (gate, up) columns -> 32 outputs, one staged tile.
+            const int col = col_base + c2;
+            if (col >= N) continue;
+            float o[32];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float g = __uint_as_float(raw[hh][2 * i]), u = __uint_as_float(raw[hh][2 * i + 1]);
+                    if (e.bias) {
+                        g += bias_s[col + hh * 32 + 2 * i];
+                        u += bias_s[col + hh * 32 + 2 * i + 1];
+                    }
+                    o[hh * 16 + i] = (e.act == 2 ? silu(g) : gelu_erf(g)) * u;
+                }
+            stage_store32<T>(o, col / 2, ss, out_map);
+            continue;
+        }
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int c = c2 + hh * 32;
@@ -203,28 +282,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                 store_n<T, 32>(y, v);
                 continue;
             }
-            // Lane l writes row l: 16-byte chunk q at q ^ ((l >> 1) & 3), the
-            // TMA 64-byte swizzle, which spreads each store over all banks.
-            const int lane = threadIdx.x & 31;
-            uint8_t *buf = ss.buf + (ss.nstore & 1) * 2048;
-            if (lane == 0) tma_store_wait_read<1>();  // the store two chunks back is done reading buf
-            __syncwarp();
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 u;
-                u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
-                u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
-                u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
-                u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
-                *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = u;
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                tma_store_2d(out_map, smem_u32(buf), col, ss.row0);
-                tma_store_commit();
-            }
-            ++ss.nstore;
+            stage_store32<T>(v, col, ss, out_map);
         }
     }
 }
@@ -361,8 +419,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         const int ew = warp - 4, quad = warp & 3, part = ew >> 2;
         constexpr int COLS = BN / EPI_WG;  // this warp's columns of a tile
         const uint32_t tempty_leader = PAIR ? mapa(tempty0, 0) : tempty0;
-        const bool tma_out = use_tma_store && (e.kind == EPI_STORE || e.kind == EPI_GELU ||
-                                               e.kind == EPI_GELU_TANH || e.kind == EPI_RESIDUAL);
+        // Gated tiles store 32 outputs per 64 columns: whole tiles need N % 64 == 0.
+        const bool tma_out = use_tma_store && (e.kind != EPI_GATED || N % 64 == 0);
         StoreStage ss{tma_out, staging + ew * 4096, 0, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
