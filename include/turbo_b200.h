@@ -72,7 +72,9 @@ TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t variant, uint32
 /* Attention over `batch` rows packed one after another (row b has lens[b]
  * tokens), qkv [tokens, 3 * hidden] host F32 narrowed to dtype, live [tokens]
  * the mask entries, window < 0 for whole rows. variant 0 is the F16/BF16
- * tensor-core kernel, 1 the F32 kernel. ctx_out [tokens, hidden]. */
+ * mma.sync kernel, 1 the SIMT kernel (any dtype), 2 the tcgen05 kernel with
+ * one 128-query tile a CTA, 3 the tcgen05 kernel with two (whole rows only),
+ * the last two for head width 64. ctx_out [tokens, hidden]. */
 TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, uint32_t batch, const int32_t *lens,
                                              const float *qkv, const uint8_t *live, uint32_t heads,
                                              uint32_t head_dim, int32_t window, float *ctx_out, turbo_error *err);

@@ -167,20 +167,28 @@ TC_CASES = [([128], 2, 64, -1), ([300, 5, 129], 12, 64, -1), ([500, 130], 2, 64,
 
 @pytest.mark.parametrize("dtype", [F16, BF16])
 @pytest.mark.parametrize("case", TC_CASES)
-def test_tcgen05_attention(dtype, case):
+@pytest.mark.parametrize("holes", [True, False])
+@pytest.mark.parametrize("variant", [2, 3])
+def test_tcgen05_attention(dtype, case, holes, variant):
+    # Rows with masked keys inside read the live flags; rows without take
+    # their key masks from the row's end alone. Variant 3 (two query tiles a
+    # CTA) serves whole rows only.
     lens, heads, d, window = case
+    if variant == 3 and window >= 0:
+        pytest.skip("sliding windows run on the one-tile kernel")
     T = sum(lens)
     rng = np.random.default_rng(T + d + 5)
     qkv = narrow(rng.standard_normal((T, 3 * heads * d)).astype(np.float32) * 2, dtype)
-    live = (rng.random(T) > 0.15).astype(np.uint8)
-    got = runtime.attention_check(dtype, 2, lens, qkv, live, heads, d, window)
+    live = (rng.random(T) > 0.15).astype(np.uint8) if holes else np.ones(T, np.uint8)
+    got = runtime.attention_check(dtype, variant, lens, qkv, live, heads, d, window)
     want = ref_attention(qkv, lens, live, heads, d, window)
     # Output rounding to BF16 (8 significant bits) or F16 (11) bounds the error relative to its scale.
     assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
 
 
 @pytest.mark.parametrize("dtype", [F16, BF16])
-def test_tcgen05_attention_rescales_when_the_max_grows(dtype):
+@pytest.mark.parametrize("variant", [2, 3])
+def test_tcgen05_attention_rescales_when_the_max_grows(dtype, variant):
     # Key magnitudes ramp up along the row, so later 64-key chunks raise
     # the running max far past the first: O in tensor memory is rescaled.
     lens, heads, d = [400, 70], 2, 64
@@ -191,7 +199,7 @@ def test_tcgen05_attention_rescales_when_the_max_grows(dtype):
     qkv[:, heads * d:2 * heads * d] *= ramp[:, None]
     qkv = narrow(qkv, dtype)
     live = np.ones(T, np.uint8)
-    got = runtime.attention_check(dtype, 2, lens, qkv, live, heads, d, -1)
+    got = runtime.attention_check(dtype, variant, lens, qkv, live, heads, d, -1)
     want = ref_attention(qkv, lens, live, heads, d, -1)
     # Output rounding to BF16 (8 significant bits) or F16 (11) bounds the error relative to its scale.
     assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)

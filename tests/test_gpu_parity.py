@@ -195,6 +195,21 @@ def test_modernbert_long_rows_local_and_global_layers(ctx, precision):
     m.release()
 
 
+@pytest.mark.parametrize("precision", [FASTEST])
+def test_modernbert_rows_past_1024_take_the_two_tile_kernel(ctx, precision):
+    # Rows of 1,024 tokens and more on average run the global layers on the
+    # two-tile attention kernel, the local ones on the one-tile kernel.
+    d = models.synthetic("modernbert-base", 5, layers=3)
+    ids, mask, lens = models.rows_long(6, 2, 1100, 1400, 1400, 100, 50367)
+    m = ctx.load(d)
+    s = m.session(2, 1400, precision)
+    got = s.embed(ids, mask)
+    want = oracle.encode(d, ids, mask)
+    check(got, want, precision, "modernbert 3 layers, long rows")
+    s.release()
+    m.release()
+
+
 def test_warm_run_allocates_nothing_and_repeats_its_bits(ctx):
     a, meta = load_golden("tiny_bert")
     m = ctx.load(models.bert_desc(a, meta))

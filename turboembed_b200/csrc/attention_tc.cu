@@ -9,23 +9,34 @@
 // the tcgen05 counterpart of the reference's FASTEST attention_fa_kernel
 // (core/cuda/kernels.cu:4142, mma.sync m16n8k16).
 //
-// Persistent CTAs, four per SM (48 KB shared memory, 128 TMEM columns each),
-// 160 threads, looping over work units (row, 128-query tile, head); keys in
-// chunks of 64:
-//   warp 4, lane 0   TMA loads ([rows x 64] boxes of the packed qkv buffer,
-//                    128-byte swizzle: Q 128 rows, K and V 64) and every MMA:
-//                    S = Q K^T (M 128, N 64, K 64) into TMEM columns 0..63,
-//                    O += P V (M 128, N 64, K 64) into columns 64..127, V
-//                    read MN-major. The next unit's Q and first K/V chunk
-//                    are loaded while the current unit's last chunk is still
-//                    in the softmax.
-//   warps 0..3       the softmax: thread r owns query row r (TMEM lane r):
-//                    pass 1 reads S for the row max, pass 2 reads it again
-//                    and writes P = 2^(s log2e/sqrt(d) - m_ref) as F16/BF16
-//                    straight into the swizzled shared-memory A operand of
-//                    the P V product, summing the row. A chunk whose keys are
-//                    all live and in range takes a path without masks.
-// O accumulates in TMEM across a unit's chunks. Its reference max m_ref
+// Two kernels share the softmax (softmax_tile below); keys come in chunks of
+// 64, S = Q K^T is M 128 x N 64 x K 64 and O += P V is M 128 x N 64 x K 64
+// with V read MN-major, all operands [rows x 64] TMA boxes of the packed qkv
+// buffer with the 128-byte swizzle.
+//
+// attn_tc2_kernel (full attention, the encoder's global layers): persistent
+// CTAs, two per SM (about 98 KB shared memory, 256 TMEM columns each), 320
+// threads, looping over units (row, 256-query pair of tiles, head). Both
+// tiles read the same keys, so K and V are loaded once for the two, into two
+// buffers each, the next chunk's while this one is in use:
+//   warps 0..3, 4..7  two softmax warpgroups, one per 128-query tile
+//                     (S in TMEM columns 0..63 / 64..127, O in 128..191 /
+//                     192..255, P in its own shared-memory tile);
+//   warp 8, lane 0    every MMA: S of a tile's next chunk as soon as its
+//                     softmax holds the current S in registers and the K
+//                     chunk is in, P V as soon as P is written;
+//   warp 9, lane 0    every TMA load (Q of both tiles, K and V chunks) into
+//                     buffers the MMAs have released (tcgen05.commit).
+// attn_tc_kernel (sliding-window layers, and the allocation-free entry
+// point): persistent CTAs, four per SM (48 KB, 128 TMEM columns), 160
+// threads, units (row, 128-query tile, head), one K and one V buffer; warp 4
+// lane 0 issues both the loads and the MMAs.
+//
+// The softmax: thread r owns query row r (TMEM lane r). It loads a chunk's
+// 64 scores into registers (releasing S for the next chunk's Q K^T), masks
+// invalid keys, takes the row max, and writes P = 2^(s log2e/sqrt(d) - m_ref)
+// as F16/BF16 into the swizzled shared-memory A operand of P V, summing the
+// row. O accumulates in TMEM across a unit's chunks. Its reference max m_ref
 // moves only when a chunk's max passes it by more than 8 (log2 units): then
 // O (after the previous P V is done) and the row sum are rescaled in place.
 // P stays below 2^8, and the result is exact either way since O and the row
@@ -45,6 +56,9 @@ constexpr int KV_BYTES = KT * D * 2;  // 8 KB
 constexpr int P_BYTES = QT * KT * 2;  // 16 KB
 constexpr int SMEM = Q_BYTES + 2 * KV_BYTES + P_BYTES + 256 + 1024;
 constexpr int CTAS_PER_SM = 4;
+constexpr int KB2 = 3;  // attn_tc2's K buffers (V has 2)
+constexpr int SMEM2 = 2 * Q_BYTES + 2 * P_BYTES + (KB2 + 2) * KV_BYTES + 256 + 1024;
+constexpr int CTAS_PER_SM2 = 2;
 constexpr float RESCALE = 8.0f;  // log2 units
 
 __device__ __forceinline__ float ex2(float x) {
@@ -53,21 +67,242 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Packed pairs of F32 (Blackwell's two-wide FP32 operations): each half is
+// rounded exactly as the scalar operation would round it.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for a pair on the FMA pipe instead of the MUFU (ex2.approx): Cody and
+// Waite's range reduction x = j + f, j = round(x), |f| <= 1/2 (adding and
+// subtracting 1.5 * 2^23 rounds x to an integer), then 2^f from a degree-4
+// polynomial fitted here for relative error on [-1/2, 1/2] (a Lawson-weighted
+// least-squares fit: max relative error 2.7e-6 in F32 Horner form, far below
+// the F16 / BF16 rounding of P), and j added to the exponent bits. Below
+// -126 (and at -inf, a masked key) the result is 0, as ex2.approx.ftz's is;
+// the arithmetic there runs on out-of-range values and is discarded.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float &y1) {
+    const uint64_t xx = pk2(x0, x1);
+    const uint64_t r = add2(xx, pk2(12582912.0f, 12582912.0f));
+    const uint64_t t = add2(r, pk2(-12582912.0f, -12582912.0f));
+    const uint64_t f = fma2(t, pk2(-1.0f, -1.0f), xx);
+    uint64_t p = fma2(pk2(0.009570101276040077f, 0.009570101276040077f), f,
+                      pk2(0.05591786280274391f, 0.05591786280274391f));
+    p = fma2(p, f, pk2(0.240247443318367f, 0.240247443318367f));
+    p = fma2(p, f, pk2(0.6931217908859253f, 0.6931217908859253f));
+    p = fma2(p, f, pk2(0.9999992847442627f, 0.9999992847442627f));
+    float p0, p1, r0, r1;
+    upk2(p, p0, p1);
+    upk2(r, r0, r1);
+    // r's low mantissa bits hold j (two's complement); << 23 moves j into
+    // the exponent field and drops the rest of r's bits.
+    y0 = x0 >= -126.0f ? __int_as_float(__float_as_int(p0) + (__float_as_int(r0) << 23)) : 0.0f;
+    y1 = x1 >= -126.0f ? __int_as_float(__float_as_int(p1) + (__float_as_int(r1) << 23)) : 0.0f;
+}
+// Which pairs of a 64-key chunk take the polynomial: one in four, so the
+// MUFU and the FMA pipe share the exponentials.
+__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (pair & 3) == 3; }
+
 // Instruction descriptors of kind::f16 with F32 accumulators, M = 128.
 __host__ __device__ constexpr uint32_t idesc(uint32_t fmt, int n, bool b_mn_major) {
     return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
            ((uint32_t)(128 >> 4) << 24);
 }
 
-// Keys [klo, khi) a query tile of a row reads.
-__device__ __forceinline__ void key_range(const AttnItem &it, int window, int &klo, int &khi) {
+// Keys [klo, khi) the query tile at q0 of a row of len tokens reads.
+__device__ __forceinline__ void key_range(int len, int q0, int window, int &klo, int &khi) {
     klo = 0;
-    khi = it.len;
+    khi = len;
     if (window >= 0) {
-        klo = max(0, it.q0 - window);
-        khi = min(it.len, it.q0 + QT - 1 + window + 1);
+        klo = max(0, q0 - window);
+        khi = min(len, q0 + QT - 1 + window + 1);
     }
 }
+
+// The four barriers between one softmax warpgroup and the MMA issuer: S
+// done (commit), S held in registers (128 arrivals), P written (128
+// arrivals), P V done (commit).
+struct SoftBars {
+    uint32_t s, sf, p, o;
+};
+
+// One softmax warpgroup's pass over one 128-query tile at q0 of item `it`:
+// chunks of keys [klo, khi); `g` counts this warpgroup's chunks (barrier
+// phases) and advances by the tile's chunk count. lane_base addresses this
+// warp's TMEM lanes at the tile's S columns; O sits o_off columns further.
+// r is the thread's query row in the tile; rowp its 128-byte row of the
+// tile's P operand. Returns false when the kernel must stop.
+template <class T>
+__device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo, int khi, int window, int head,
+                                             T *__restrict__ ctx, int h, const uint8_t *__restrict__ live,
+                                             float scale_log2, uint32_t lane_base, uint32_t o_off, uint8_t *rowp, int r,
+                                             const SoftBars &b, uint32_t &g, volatile int *abort_flag, int *fault) {
+    const int lane = threadIdx.x & 31;
+    const int nch = (khi - klo + KT - 1) / KT;
+    const int qi = q0 + r;
+    float m_ref = -INFINITY, l = 0.0f;
+    for (int j = 0; j < nch; ++j, ++g) {
+        const uint32_t par = g & 1;
+        const int k0 = klo + j * KT;
+        // The chunk's key flags: from the row's end alone when the row has
+        // no holes, else lane l of every warp loads 2 of them.
+        uint32_t km0, km1;
+        if (!it.holes) {
+            const int n0 = khi - k0, n1 = n0 - 32;
+            km0 = n0 >= 32 ? 0xffffffffu : (n0 <= 0 ? 0u : (1u << n0) - 1u);
+            km1 = n1 >= 32 ? 0xffffffffu : (n1 <= 0 ? 0u : (1u << n1) - 1u);
+        } else {
+            int key = k0 + lane;
+            km0 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
+            key += 32;
+            km1 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
+        }
+        const bool full = window < 0 && (km0 & km1) == 0xffffffffu;
+        if (!mbar_wait(b.s, par, abort_flag, fault)) return false;
+        tc_fence_after();
+        // The chunk's 64 raw scores into registers; then S is free for the
+        // next chunk's Q K^T.
+        float sv[64];
+        {
+            uint32_t raw[64];
+            __syncwarp();
+            tmem_ld32_async(lane_base, raw);
+            tmem_ld32_async(lane_base + 32, raw + 32);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(b.sf);
+        // Invalid keys (masked, past the row, outside the window) become
+        // -inf; the row max of the valid raw scores (the scale is positive,
+        // so it is applied once after).
+        if (!full) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                bool valid = (((i < 32) ? km0 : km1) >> (i & 31)) & 1u;
+                if (window >= 0) valid = valid && abs(qi - (k0 + i)) <= window;
+                sv[i] = valid ? sv[i] : -INFINITY;
+            }
+        }
+        // Four independent three-input maxima, then a tree: half the
+        // instructions of a two-input chain and short dependencies.
+        float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int i = 4; i < 60; i += 8)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) m4[k] = max3(m4[k], sv[i + k], sv[i + 4 + k]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) m4[k] = fmaxf(m4[k], sv[60 + k]);
+        float mx = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
+        mx = mx == -INFINITY ? mx : mx * scale_log2;
+        // P smem and O are free once the previous chunk's P V is done.
+        if (j > 0) {
+            if (!mbar_wait(b.o, (g - 1) & 1, abort_flag, fault)) return false;
+            tc_fence_after();
+        }
+        // A row whose max passed m_ref by more than RESCALE moves m_ref; the
+        // warp rescales O in TMEM (warp-wide, factor 1 for the rows that
+        // keep theirs) when any of its rows moved.
+        const bool move = mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + RESCALE);
+        float f = 1.0f;
+        if (move) {
+            f = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mx);
+            l *= f;
+            m_ref = mx;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, move)) {
+            __syncwarp();
+#pragma unroll 1
+            for (int q = 0; q < 4; ++q) {
+                float o[16];
+                tmem_ld16(lane_base + o_off + q * 16, o);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] *= f;
+                tmem_st16(lane_base + o_off + q * 16, o);
+            }
+        }
+        const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
+        // P = 2^(s c - mu) (0 for invalid keys: 2^-inf) into the swizzled A
+        // operand of P V, summing the row in packed pairs.
+        const uint64_t c2 = pk2(scale_log2, scale_log2), nmu = pk2(-mu, -mu);
+        uint64_t s4[4] = {0, 0, 0, 0};  // 0 bits = +0.0f
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+            float x0, x1;
+            upk2(fma2(pk2(sv[i], sv[i + 1]), c2, nmu), x0, x1);
+            if (poly_pair(i / 2)) {
+                exp2_poly2(x0, x1, sv[i], sv[i + 1]);
+            } else {
+                sv[i] = ex2(x0);
+                sv[i + 1] = ex2(x1);
+            }
+            s4[(i / 2) & 3] = add2(s4[(i / 2) & 3], pk2(sv[i], sv[i + 1]));
+        }
+        float rs, rs1;
+        upk2(add2(add2(s4[0], s4[1]), add2(s4[2], s4[3])), rs, rs1);
+        rs += rs1;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            uint4 w;
+            w.x = pack2<T>(sv[8 * cc + 0], sv[8 * cc + 1]);
+            w.y = pack2<T>(sv[8 * cc + 2], sv[8 * cc + 3]);
+            w.z = pack2<T>(sv[8 * cc + 4], sv[8 * cc + 5]);
+            w.w = pack2<T>(sv[8 * cc + 6], sv[8 * cc + 7]);
+            *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
+        }
+        l += rs;
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(b.p);
+    }
+    if (!mbar_wait(b.o, (g - 1) & 1, abort_flag, fault)) return false;
+    tc_fence_after();
+    __syncwarp();
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    T *out = ctx + ((int64_t)it.start + qi) * h + head * D;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        float o[32];
+        tmem_ld32(lane_base + o_off + half * 32, o);
+        if (qi < it.len) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 w;
+                w.x = pack2<T>(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
+                w.y = pack2<T>(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
+                w.z = pack2<T>(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
+                w.w = pack2<T>(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
+                reinterpret_cast<uint4 *>(out)[half * 4 + q] = w;
+            }
+        }
+    }
+    // O is read: the next unit's first P V may overwrite it.
+    tc_fence_before();
+    return true;
+}
+
+// ---- one 128-query tile a CTA, four CTAs an SM (sliding-window layers) ----
 
 template <class T>
 __global__ void __launch_bounds__(160, CTAS_PER_SM)
@@ -114,25 +349,28 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         if (lane == 0) {
             const uint32_t ids = idesc(fmt, KT, false), idpv = idesc(fmt, D, true);
             const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sP);
-            // Loads of a unit's Q, or of chunk j's K / V.
-            auto load_q = [&](int u) {
+            // A unit's TMA coordinates, read once: first key row, query row,
+            // head column, chunk count.
+            struct Unit {
+                int row0, qrow, col, nch;
+            };
+            auto unit_of = [&](int u) {
                 const AttnItem it = items[u / heads];
+                int klo, khi;
+                key_range(it.len, it.q0, window, klo, khi);
+                return Unit{it.start + klo, it.start + it.q0, (u % heads) * D, (khi - klo + KT - 1) / KT};
+            };
+            auto load_q = [&](const Unit &n) {
                 mbar_expect_tx(bar_q, Q_BYTES);
-                tma_load_2d(aq, &tq, (u % heads) * D, it.start + it.q0, bar_q);
+                tma_load_2d(aq, &tq, n.col, n.qrow, bar_q);
             };
-            auto load_k = [&](int u, int j) {
-                const AttnItem it = items[u / heads];
-                int klo, khi;
-                key_range(it, window, klo, khi);
+            auto load_k = [&](const Unit &n, int j) {
                 mbar_expect_tx(bar_k, KV_BYTES);
-                tma_load_2d(ak, &tkv, h + (u % heads) * D, it.start + klo + j * KT, bar_k);
+                tma_load_2d(ak, &tkv, h + n.col, n.row0 + j * KT, bar_k);
             };
-            auto load_v = [&](int u, int j) {
-                const AttnItem it = items[u / heads];
-                int klo, khi;
-                key_range(it, window, klo, khi);
+            auto load_v = [&](const Unit &n, int j) {
                 mbar_expect_tx(bar_v, KV_BYTES);
-                tma_load_2d(av, &tkv, 2 * h + (u % heads) * D, it.start + klo + j * KT, bar_v);
+                tma_load_2d(av, &tkv, 2 * h + n.col, n.row0 + j * KT, bar_v);
             };
             auto issue_s = [&]() {
                 tc_fence_after();
@@ -142,39 +380,35 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                              kk > 0 ? 1u : 0u);
                 umma_commit(bar_s);
             };
-            // g: chunks of this CTA so far (every barrier but bar_q completes
-            // once a chunk); qc: units so far.
-            uint32_t g = 0, qc = 0;
+            uint32_t g = 0, qc = 0;  // chunks and units done so far
             bool ok = true;
             int u = blockIdx.x;
+            Unit cur = u < units ? unit_of(u) : Unit{0, 0, 0, 0};
             if (u < units) {
-                load_q(u);
-                load_k(u, 0);
-                load_v(u, 0);
+                load_q(cur);
+                load_k(cur, 0);
+                load_v(cur, 0);
             }
             for (; u < units && ok; u += gridDim.x, ++qc) {
-                const AttnItem it = items[u / heads];
-                int klo, khi;
-                key_range(it, window, klo, khi);
-                const int nch = (khi - klo + KT - 1) / KT;
                 const int next = u + gridDim.x;
+                const Unit nxt = next < units ? unit_of(next) : Unit{0, 0, 0, 0};
                 if (!(ok = mbar_wait(bar_q, qc & 1, abort_flag, fault))) break;
                 // The softmax has S of the previous chunk in registers.
                 if (g > 0 && !(ok = mbar_wait(bar_sf, (g - 1) & 1, abort_flag, fault))) break;
                 if (!(ok = mbar_wait(bar_k, g & 1, abort_flag, fault))) break;
                 issue_s();
-                for (int j = 0; j < nch && ok; ++j, ++g) {
+                for (int j = 0; j < cur.nch && ok; ++j, ++g) {
                     const uint32_t par = g & 1;
                     // S done: K (and, after the last chunk, Q) are free.
                     if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
-                    if (j + 1 < nch) load_k(u, j + 1);
+                    if (j + 1 < cur.nch) load_k(cur, j + 1);
                     else if (next < units) {
-                        load_q(next);
-                        load_k(next, 0);
+                        load_q(nxt);
+                        load_k(nxt, 0);
                     }
                     // The next S as soon as the softmax holds this one: it
                     // runs while the softmax works on this chunk.
-                    if (j + 1 < nch) {
+                    if (j + 1 < cur.nch) {
                         if (!(ok = mbar_wait(bar_sf, par, abort_flag, fault))) break;
                         if (!(ok = mbar_wait(bar_k, (g + 1) & 1, abort_flag, fault))) break;
                         issue_s();
@@ -191,143 +425,25 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                     umma_commit(bar_o);
                     // P V done: V and P are free.
                     if (!(ok = mbar_wait(bar_o, par, abort_flag, fault))) break;
-                    if (j + 1 < nch) load_v(u, j + 1);
-                    else if (next < units) load_v(next, 0);
+                    if (j + 1 < cur.nch) load_v(cur, j + 1);
+                    else if (next < units) load_v(nxt, 0);
                 }
+                cur = nxt;
             }
         }
     } else {
         // Softmax: thread r = query row r = TMEM lane r.
         const int r = threadIdx.x;
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const SoftBars sb{bar_s, bar_sf, bar_p, bar_o};
         uint32_t g = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
             const AttnItem it = items[u / heads];
-            const int head = u % heads;
             int klo, khi;
-            key_range(it, window, klo, khi);
-            const int nch = (khi - klo + KT - 1) / KT;
-            const int qi = it.q0 + r;
-            float m_ref = -INFINITY, l = 0.0f;
-            for (int j = 0; j < nch && ok; ++j, ++g) {
-                const uint32_t par = g & 1;
-                const int k0 = klo + j * KT;
-                // The chunk's key flags: lane l of every warp loads 2 of them.
-                uint32_t km0, km1;
-                {
-                    int key = k0 + lane;
-                    km0 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
-                    key += 32;
-                    km1 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
-                }
-                const bool full = window < 0 && (km0 & km1) == 0xffffffffu;
-                if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
-                tc_fence_after();
-                // The chunk's 64 raw scores into registers; then S is free
-                // for the next chunk's Q K^T.
-                float sv[64];
-                {
-                    uint32_t raw[64];
-                    __syncwarp();
-                    tmem_ld32_async(lane_base, raw);
-                    tmem_ld32_async(lane_base + 32, raw + 32);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
-                }
-                tc_fence_before();
-                mbar_arrive(bar_sf);
-                // Invalid keys (masked, past the row, outside the window)
-                // become -inf; the row max of the valid raw scores (the scale
-                // is positive, so it is applied once after).
-                float mx = -INFINITY;
-                if (full) {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        bool valid = (((i < 32) ? km0 : km1) >> (i & 31)) & 1u;
-                        if (window >= 0) valid = valid && abs(qi - (k0 + i)) <= window;
-                        sv[i] = valid ? sv[i] : -INFINITY;
-                        mx = fmaxf(mx, sv[i]);
-                    }
-                }
-                mx = mx == -INFINITY ? mx : mx * scale_log2;
-                // P smem and O are free once the previous chunk's P V is done.
-                if (j > 0) {
-                    if (!(ok = mbar_wait(bar_o, (g - 1) & 1, abort_flag, fault))) break;
-                    tc_fence_after();
-                }
-                // A row whose max passed m_ref by more than RESCALE moves
-                // m_ref; the warp rescales O in TMEM (warp-wide, factor 1 for
-                // the rows that keep theirs) when any of its rows moved.
-                const bool move = mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + RESCALE);
-                float f = 1.0f;
-                if (move) {
-                    f = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mx);
-                    l *= f;
-                    m_ref = mx;
-                }
-                if (j > 0 && __any_sync(0xffffffffu, move)) {
-                    __syncwarp();
-#pragma unroll 1
-                    for (int q = 0; q < 4; ++q) {
-                        float o[16];
-                        tmem_ld16(lane_base + 64 + q * 16, o);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) o[i] *= f;
-                        tmem_st16(lane_base + 64 + q * 16, o);
-                    }
-                }
-                const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
-                // P = 2^(s c - mu) (0 for invalid keys: 2^-inf) into the
-                // swizzled A operand of P V, summing the row.
-                float rs = 0.0f;
-                uint8_t *rowp = sP + r * 128;
-#pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    sv[i] = ex2(fmaf(sv[i], scale_log2, -mu));
-                    rs += sv[i];
-                }
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    uint4 w;
-                    w.x = pack2<T>(sv[8 * cc + 0], sv[8 * cc + 1]);
-                    w.y = pack2<T>(sv[8 * cc + 2], sv[8 * cc + 3]);
-                    w.z = pack2<T>(sv[8 * cc + 4], sv[8 * cc + 5]);
-                    w.w = pack2<T>(sv[8 * cc + 6], sv[8 * cc + 7]);
-                    *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
-                }
-                l += rs;
-                fence_async_smem();
-                tc_fence_before();
-                mbar_arrive(bar_p);
-            }
-            if (!ok || !(ok = mbar_wait(bar_o, (g - 1) & 1, abort_flag, fault))) break;
-            tc_fence_after();
-            __syncwarp();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            T *out = ctx + ((int64_t)it.start + qi) * h + head * D;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float o[32];
-                tmem_ld32(lane_base + 64 + half * 32, o);
-                if (qi < it.len) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint4 w;
-                        w.x = pack2<T>(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
-                        w.y = pack2<T>(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
-                        w.z = pack2<T>(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
-                        w.w = pack2<T>(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
-                        reinterpret_cast<uint4 *>(out)[half * 4 + q] = w;
-                    }
-                }
-            }
-            // O is read: the next unit's first P V may overwrite it.
-            tc_fence_before();
+            key_range(it.len, it.q0, window, klo, khi);
+            if (!softmax_tile<T>(it, it.q0, klo, khi, window, u % heads, ctx, h, live, scale_log2, lane_base, 64,
+                                 sP + r * 128, r, sb, g, abort_flag, fault))
+                break;
         }
     }
     tc_fence_before();
@@ -338,17 +454,236 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     }
 }
 
+// ---- two 128-query tiles a CTA, two CTAs an SM (full attention) ----
+
+template <class T>
+__global__ void __launch_bounds__(320, CTAS_PER_SM2)
+attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv, T *__restrict__ ctx,
+                const uint8_t *__restrict__ live, const AttnItem *__restrict__ items, int n_items, int heads, int h,
+                float scale_log2, int *fault) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sQ = smem, *sP = sQ + 2 * Q_BYTES, *sK = sP + 2 * P_BYTES, *sV = sK + KB2 * KV_BYTES;
+    uint8_t *bars = sV + 2 * KV_BYTES;
+    // Barriers: Q in, Q free, K in [3], K free [3], V in [2], V free [2],
+    // then per tile t the four SoftBars.
+    const uint32_t b0 = smem_u32(bars);
+    const uint32_t bar_q = b0, bar_qf = b0 + 8, bar_k = b0 + 16, bar_kf = b0 + 40, bar_v = b0 + 64, bar_vf = b0 + 80;
+    auto tile_bars = [&](int t) {
+        const uint32_t x = b0 + 96 + 32 * t;
+        return SoftBars{x, x + 8, x + 16, x + 24};
+    };
+    uint32_t *tmem_slot = (uint32_t *)(bars + 160);
+    volatile int *abort_flag = (volatile int *)(bars + 168);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int units = n_items * heads;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar_q, 1);
+        mbar_init(bar_qf, 1);
+        for (int i = 0; i < KB2; ++i) {
+            mbar_init(bar_k + 8 * i, 1);
+            mbar_init(bar_kf + 8 * i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar_v + 8 * i, 1);
+            mbar_init(bar_vf + 8 * i, 1);
+            const SoftBars tb = tile_bars(i);
+            mbar_init(tb.s, 1);
+            mbar_init(tb.sf, 128);
+            mbar_init(tb.p, 128);
+            mbar_init(tb.o, 1);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp == 8) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(256u));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t fmt = Elem<T>::dt == Dt::BF16 ? 1u : 0u;
+    pdl_wait();  // qkv and the plan are an earlier kernel's and copy's
+    pdl_trigger();
+
+    if (warp == 9) {
+        if (lane == 0) {
+            // Loads. Chunk c (counted over this CTA's units) uses K buffer
+            // c % 3, free once the S of chunk c - 3 are done, and V buffer
+            // c & 1, free once the P V of chunk c - 2 are; the K stream runs
+            // one chunk ahead of the V stream (S comes before P V).
+            struct Unit {
+                int start, q0, len, col, nch;
+            };
+            auto unit_of = [&](int u) {
+                const AttnItem it = items[u / heads];
+                return Unit{it.start, it.q0, it.len, (u % heads) * D, (it.len + KT - 1) / KT};
+            };
+            uint32_t kc = 0, vc = 0, qn = 0;  // K loads, V loads, units
+            bool ok = true;
+            auto load_k = [&](const Unit &n, int j) {
+                const uint32_t b = kc % KB2;
+                if (kc >= KB2 && !(ok = mbar_wait(bar_kf + 8 * b, ((kc - KB2) / KB2) & 1, abort_flag, fault))) return;
+                mbar_expect_tx(bar_k + 8 * b, KV_BYTES);
+                tma_load_2d(smem_u32(sK + b * KV_BYTES), &tkv, h + n.col, n.start + j * KT, bar_k + 8 * b);
+                ++kc;
+            };
+            auto load_v = [&](const Unit &n, int j) {
+                const uint32_t b = vc & 1;
+                if (vc >= 2 && !(ok = mbar_wait(bar_vf + 8 * b, ((vc - 2) >> 1) & 1, abort_flag, fault))) return;
+                mbar_expect_tx(bar_v + 8 * b, KV_BYTES);
+                tma_load_2d(smem_u32(sV + b * KV_BYTES), &tkv, 2 * h + n.col, n.start + j * KT, bar_v + 8 * b);
+                ++vc;
+            };
+            int u = blockIdx.x;
+            Unit cur = u < units ? unit_of(u) : Unit{0, 0, 0, 0, 0};
+            if (u < units) load_k(cur, 0);
+            for (; u < units && ok; u += gridDim.x, ++qn) {
+                const int next = u + gridDim.x;
+                const Unit nxt = next < units ? unit_of(next) : Unit{0, 0, 0, 0, 0};
+                const bool two = cur.q0 + QT < cur.len;
+                if (qn > 0 && !(ok = mbar_wait(bar_qf, (qn - 1) & 1, abort_flag, fault))) break;
+                mbar_expect_tx(bar_q, (two ? 2 : 1) * Q_BYTES);
+                tma_load_2d(smem_u32(sQ), &tq, cur.col, cur.start + cur.q0, bar_q);
+                if (two) tma_load_2d(smem_u32(sQ + Q_BYTES), &tq, cur.col, cur.start + cur.q0 + QT, bar_q);
+                for (int j = 0; j < cur.nch && ok; ++j) {
+                    if (j + 1 < cur.nch) load_k(cur, j + 1);
+                    else if (next < units) load_k(nxt, 0);
+                    if (ok) load_v(cur, j);
+                }
+                cur = nxt;
+            }
+        }
+    } else if (warp == 8) {
+        if (lane == 0) {
+            // MMAs. Per chunk: S of both tiles' next chunk as soon as each
+            // softmax holds its current S and the next K is in (then a
+            // commit releases K's buffer), P V of each tile as soon as its P
+            // is written (then V's buffer). A unit's Q buffer is released
+            // after its last S.
+            const uint32_t ids = idesc(fmt, KT, false), idpv = idesc(fmt, D, true);
+            const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sP);
+            const SoftBars tb0 = tile_bars(0), tb1 = tile_bars(1);
+            uint32_t c = 0, qn = 0, g0 = 0, g1 = 0;  // chunks; units; each tile's chunks
+            bool ok = true;
+            auto issue_s = [&](int t, uint32_t kb) {
+                const uint32_t q = aq + t * Q_BYTES, k = ak + kb * KV_BYTES;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma_f16(tmem + t * 64, smem_desc(q) + (uint64_t)(kk * 2), smem_desc(k) + (uint64_t)(kk * 2), ids,
+                             kk > 0 ? 1u : 0u);
+                umma_commit(t ? tb1.s : tb0.s);
+            };
+            auto issue_pv = [&](int t, uint32_t vb, bool acc) {
+                const uint32_t p = ap + t * P_BYTES, v = av + vb * KV_BYTES;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < KT / 16; ++kk)
+                    umma_f16(tmem + 128 + t * 64, smem_desc(p) + (uint64_t)(kk * 2), smem_desc(v + kk * 16 * 128), idpv,
+                             (acc || kk) ? 1u : 0u);
+                umma_commit(t ? tb1.o : tb0.o);
+            };
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++qn) {
+                const AttnItem it = items[u / heads];
+                const bool two = it.q0 + QT < it.len;
+                const int nch = (it.len + KT - 1) / KT;
+                // The unit's first S: Q and K in, each softmax done with its
+                // previous S.
+                if (!(ok = mbar_wait(bar_q, qn & 1, abort_flag, fault))) break;
+                if (!(ok = mbar_wait(bar_k + 8 * (c % KB2), (c / KB2) & 1, abort_flag, fault))) break;
+                if (g0 > 0 && !(ok = mbar_wait(tb0.sf, (g0 - 1) & 1, abort_flag, fault))) break;
+                issue_s(0, c % KB2);
+                if (two) {
+                    if (g1 > 0 && !(ok = mbar_wait(tb1.sf, (g1 - 1) & 1, abort_flag, fault))) break;
+                    issue_s(1, c % KB2);
+                }
+                umma_commit(bar_kf + 8 * (c % KB2));
+                for (int j = 0; j < nch && ok; ++j, ++c, ++g0, g1 += two ? 1 : 0) {
+                    if (j + 1 < nch) {
+                        const uint32_t kb = (c + 1) % KB2;
+                        if (!(ok = mbar_wait(bar_k + 8 * kb, ((c + 1) / KB2) & 1, abort_flag, fault))) break;
+                        if (!(ok = mbar_wait(tb0.sf, g0 & 1, abort_flag, fault))) break;
+                        issue_s(0, kb);
+                        if (two) {
+                            if (!(ok = mbar_wait(tb1.sf, g1 & 1, abort_flag, fault))) break;
+                            issue_s(1, kb);
+                        }
+                        umma_commit(bar_kf + 8 * kb);
+                    } else {
+                        umma_commit(bar_qf);
+                    }
+                    const uint32_t vb = c & 1;
+                    if (!(ok = mbar_wait(bar_v + 8 * vb, (c >> 1) & 1, abort_flag, fault))) break;
+                    if (!(ok = mbar_wait(tb0.p, g0 & 1, abort_flag, fault))) break;
+                    issue_pv(0, vb, j > 0);
+                    if (two) {
+                        if (!(ok = mbar_wait(tb1.p, g1 & 1, abort_flag, fault))) break;
+                        issue_pv(1, vb, j > 0);
+                    }
+                    umma_commit(bar_vf + 8 * vb);
+                }
+            }
+        }
+    } else {
+        // Softmax warpgroup t = warp / 4 owns tile t; thread r = query row r
+        // of the tile = TMEM lane r.
+        const int t = warp >> 2, r = threadIdx.x & 127;
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(t * 64);
+        const SoftBars sb = tile_bars(t);
+        uint32_t g = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
+            const AttnItem it = items[u / heads];
+            const int q0 = it.q0 + t * QT;
+            if (q0 >= it.len) continue;  // a unit with one tile
+            if (!softmax_tile<T>(it, q0, 0, it.len, -1, u % heads, ctx, h, live, scale_log2, lane_base, 128,
+                                 sP + t * P_BYTES + r * 128, r, sb, g, abort_flag, fault))
+                break;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u));
+    }
+}
+
+constexpr float SCALE_LOG2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+
 template <class T>
 cudaError_t launch(const CUtensorMap &mq, const CUtensorMap &mkv, void *ctx, const uint8_t *live,
                    const AttnItem *items, int n_items, int heads, int h, int window, int sms, int *fault,
                    cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return e;
-    const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
     const int units = n_items * heads;
     const int grid = units < sms * CTAS_PER_SM ? units : sms * CTAS_PER_SM;
     return launch_pdl(attn_tc_kernel<T>, grid, 160, SMEM, s, mq, mkv, (T *)ctx, live, items, n_items, heads, h, window,
-                      sl2, fault);
+                      SCALE_LOG2, fault);
+}
+
+template <class T>
+cudaError_t launch2(const CUtensorMap &mq, const CUtensorMap &mkv, void *ctx, const uint8_t *live,
+                    const AttnItem *items, int n_items, int heads, int h, int sms, int *fault, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2);
+    if (e != cudaSuccess) return e;
+    const int units = n_items * heads;
+    const int grid = units < sms * CTAS_PER_SM2 ? units : sms * CTAS_PER_SM2;
+    return launch_pdl(attn_tc2_kernel<T>, grid, 320, SMEM2, s, mq, mkv, (T *)ctx, live, items, n_items, heads, h,
+                      SCALE_LOG2, fault);
+}
+
+int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
 }
 
 }  // namespace
@@ -358,14 +693,24 @@ cudaError_t attention_tc(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_
                          int hidden, int window, int *fault, cudaStream_t s) {
     if (n_items == 0) return cudaSuccess;
     if (head_dim != D) return cudaErrorNotSupported;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = sm_count();
     if (dt == Dt::F16)
         return launch<__half>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, sms, fault, s);
     if (dt == Dt::BF16)
         return launch<__nv_bfloat16>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, sms,
                                      fault, s);
+    return cudaErrorNotSupported;
+}
+
+cudaError_t attention_tc2(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_map, void *ctx,
+                          const uint8_t *tok_live, const AttnItem *items, int n_items, int heads, int head_dim,
+                          int hidden, int *fault, cudaStream_t s) {
+    if (n_items == 0) return cudaSuccess;
+    if (head_dim != D) return cudaErrorNotSupported;
+    const int sms = sm_count();
+    if (dt == Dt::F16) return launch2<__half>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, sms, fault, s);
+    if (dt == Dt::BF16)
+        return launch2<__nv_bfloat16>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, sms, fault, s);
     return cudaErrorNotSupported;
 }
 

@@ -177,7 +177,7 @@ struct Model {
 
 // The plan of one run in the session's staging and device memory.
 struct PlanLayout {
-    size_t tok_id, tok_type, tok_pos, tok_live, pool, attn, total;
+    size_t tok_id, tok_type, tok_pos, tok_live, pool, attn, attn2, total;
 };
 
 struct Session {
@@ -186,7 +186,7 @@ struct Session {
     uint32_t task = TURBO_TASK_EMBED, precision = 0;
     Dt dt = Dt::F32;
     int max_batch = 0, max_seq = 0, max_ranges = 0, cap_tokens = 0, cap_vectors = 0;
-    int max_attn_items = 0;
+    int max_attn_items = 0, max_attn2_items = 0;
     // activations
     void *x = nullptr, *xn = nullptr, *qkv = nullptr, *ctxb = nullptr, *ffn = nullptr;
     Buffer *out = nullptr;
@@ -201,7 +201,7 @@ struct Session {
     CUtensorMap out_x{}, out_qkv{}, out_ffn{};
     // the written state
     bool written = false;
-    int tokens = 0, batch = 0, n_vectors = 0, n_attn = 0, max_len = 0;
+    int tokens = 0, batch = 0, n_vectors = 0, n_attn = 0, n_attn2 = 0, max_len = 0;
     uint32_t normalize = TURBO_NORMALIZE_NONE, output_dim = 0;
     uint64_t h2d_bytes = 0;
     std::vector<int32_t> row_start, row_len;
@@ -670,7 +670,7 @@ cudaError_t narrowed(Model *m, Dt dt) {
 
 // ---- sessions ----------------------------------------------------------------
 
-PlanLayout plan_layout(int tokens, int vectors, int attn_items) {
+PlanLayout plan_layout(int tokens, int vectors, int attn_items, int attn2_items) {
     PlanLayout L;
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -684,6 +684,7 @@ PlanLayout plan_layout(int tokens, int vectors, int attn_items) {
     L.tok_live = take((size_t)tokens);
     L.pool = take((size_t)vectors * sizeof(PoolItem));
     L.attn = take((size_t)attn_items * sizeof(AttnItem));
+    L.attn2 = take((size_t)attn2_items * sizeof(AttnItem));
     L.total = o;
     return L;
 }
@@ -696,6 +697,16 @@ AttnKind attention_kind(const Session *s) {
     if (s->dt == Dt::F32) return AttnKind::SIMT;
     if (dh == 64) return AttnKind::TC;
     return attention_mma_takes(dh) ? AttnKind::MMA : AttnKind::SIMT;
+}
+// Full-attention layers of tcgen05 sessions run attention_tc2 over items of
+// two 128-query tiles, unless the environment sets TB_ATTN2=0 (an A/B
+// switch between the two tcgen05 kernels, read once).
+bool attention_pairs(const Session *s) {
+    static const bool on = [] {
+        const char *v = getenv("TB_ATTN2");
+        return !(v && v[0] == '0');
+    }();
+    return on && attention_kind(s) == AttnKind::TC;
 }
 int attention_queries(const Session *s) {
     switch (attention_kind(s)) {
@@ -746,7 +757,8 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
     s->cap_vectors = std::max(s->max_batch, s->max_ranges);
     const int qt = attention_queries(s.get());
     s->max_attn_items = (int)(cap / qt) + s->max_batch + 1;
-    s->lay = plan_layout(s->cap_tokens, s->cap_vectors, s->max_attn_items);
+    s->max_attn2_items = attention_pairs(s.get()) ? (int)(cap / ATTN_TC2_QUERIES) + s->max_batch + 1 : 0;
+    s->lay = plan_layout(s->cap_tokens, s->cap_vectors, s->max_attn_items, s->max_attn2_items);
     const int h = m->hidden, I = m->inter;
     const size_t es = dt_size(dt);
     // Activations: one row of slack past the capacity, so a 128-row tile
@@ -917,9 +929,20 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
     std::vector<int> order(r->batch);
     for (uint32_t b = 0; b < r->batch; ++b) order[b] = (int)b;
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return s->row_len[a] > s->row_len[b]; });
-    int na = 0;
-    for (int b : order)
-        for (int q0 = 0; q0 < s->row_len[b]; q0 += qt) attn[na++] = AttnItem{s->row_start[b], s->row_len[b], q0, 0};
+    // Rows of 1,024 tokens and more on average take the two-tile kernel for
+    // their full-attention layers (it shares K and V between two query tiles;
+    // on shorter rows the one-tile kernel's four CTAs an SM are faster).
+    AttnItem *attn2 = (AttnItem *)(H + s->lay.attn2);
+    const bool pairs = s->max_attn2_items > 0 && t >= 1024 * (int)r->batch;
+    int na = 0, na2 = 0;
+    for (int b : order) {
+        int holes = 0;
+        for (int p = 0; p < s->row_len[b]; ++p) holes |= !tok_live[s->row_start[b] + p];
+        for (int q0 = 0; q0 < s->row_len[b]; q0 += qt) attn[na++] = AttnItem{s->row_start[b], s->row_len[b], q0, holes};
+        if (pairs)
+            for (int q0 = 0; q0 < s->row_len[b]; q0 += ATTN_TC2_QUERIES)
+                attn2[na2++] = AttnItem{s->row_start[b], s->row_len[b], q0, holes};
+    }
     // One copy: the token arrays through the last attention item.
     const size_t tok_bytes = (size_t)t;
     CK(cudaMemcpyAsync(s->plan_dev + s->lay.tok_id, H + s->lay.tok_id, tok_bytes * 4, cudaMemcpyHostToDevice, c->stream), "upload");
@@ -928,13 +951,16 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
     CK(cudaMemcpyAsync(s->plan_dev + s->lay.tok_live, H + s->lay.tok_live, tok_bytes, cudaMemcpyHostToDevice, c->stream), "upload");
     CK(cudaMemcpyAsync(s->plan_dev + s->lay.pool, H + s->lay.pool, (size_t)nv * sizeof(PoolItem), cudaMemcpyHostToDevice, c->stream), "upload");
     CK(cudaMemcpyAsync(s->plan_dev + s->lay.attn, H + s->lay.attn, (size_t)na * sizeof(AttnItem), cudaMemcpyHostToDevice, c->stream), "upload");
+    if (na2)
+        CK(cudaMemcpyAsync(s->plan_dev + s->lay.attn2, H + s->lay.attn2, (size_t)na2 * sizeof(AttnItem), cudaMemcpyHostToDevice, c->stream), "upload");
     CK(cudaEventRecord(s->uploaded, c->stream), "upload");
     s->upload_pending = true;
-    s->h2d_bytes = tok_bytes * 13 + (size_t)nv * sizeof(PoolItem) + (size_t)na * sizeof(AttnItem);
+    s->h2d_bytes = tok_bytes * 13 + (size_t)nv * sizeof(PoolItem) + (size_t)(na + na2) * sizeof(AttnItem);
     s->tokens = t;
     s->batch = (int)r->batch;
     s->n_vectors = nv;
     s->n_attn = na;
+    s->n_attn2 = na2;
     s->max_len = max_len;
     s->normalize = r->normalize;
     s->output_dim = od;
@@ -1014,6 +1040,10 @@ cudaError_t encode(Session *s) {
     cudaError_t e;
     auto attention_raw = [&](int window) -> cudaError_t {
         const AttnKind kind = attention_kind(s);
+        if (kind == AttnKind::TC && window < 0 && s->n_attn2)
+            return attention_tc2(dt, s->map_qkv, s->map_qkv64, s->ctxb, pk.tok_live,
+                                 (const AttnItem *)(s->plan_dev + s->lay.attn2), s->n_attn2, m->heads, dh, h,
+                                 s->ctx->fault_dev, st);
         if (kind == AttnKind::TC)
             return attention_tc(dt, s->map_qkv, s->map_qkv64, s->ctxb, pk.tok_live, items, s->n_attn, m->heads, dh, h, window,
                                 s->ctx->fault_dev, st);

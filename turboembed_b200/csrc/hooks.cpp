@@ -172,9 +172,15 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
     const int h = (int)(heads * head_dim);
     std::vector<AttnItem> items;
     int T = 0, max_len = 0;
-    const int qt = variant == 0 ? ATTN_MMA_QUERIES : variant == 2 ? ATTN_TC_QUERIES : ATTN_F32_QUERIES;
+    const int qt = variant == 0   ? ATTN_MMA_QUERIES
+                   : variant == 2 ? ATTN_TC_QUERIES
+                   : variant == 3 ? ATTN_TC2_QUERIES
+                                  : ATTN_F32_QUERIES;
+    if (variant == 3 && window >= 0) return hook_fail(err, TURBO_E_INVALID_ARGUMENT, "variant 3 has no window", cudaSuccess);
     for (uint32_t b = 0; b < batch; ++b) {
-        for (int q0 = 0; q0 < lens[b]; q0 += qt) items.push_back(AttnItem{T, lens[b], q0, 0});
+        int holes = 0;
+        for (int p = 0; p < lens[b]; ++p) holes |= !live[T + p];
+        for (int q0 = 0; q0 < lens[b]; q0 += qt) items.push_back(AttnItem{T, lens[b], q0, holes});
         T += lens[b];
         max_len = lens[b] > max_len ? lens[b] : max_len;
     }
@@ -191,12 +197,14 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
     if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "attention_check setup", e);
     int *fault = (int *)dv.get(4);
     if (variant == 0) e = attention_mma(dt, dq, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, 0);
-    else if (variant == 2) {
+    else if (variant == 2 || variant == 3) {
         CUtensorMap map, map64;
         e = make_operand_map(dt, dq, (uint64_t)T, (uint64_t)3 * h, (uint64_t)3 * h, 128, &map);
         if (e == cudaSuccess) e = make_operand_map(dt, dq, (uint64_t)T, (uint64_t)3 * h, (uint64_t)3 * h, 64, &map64);
-        if (e == cudaSuccess)
+        if (e == cudaSuccess && variant == 2)
             e = attention_tc(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, fault, 0);
+        if (e == cudaSuccess && variant == 3)
+            e = attention_tc2(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, fault, 0);
     }
     else e = attention_simt(dt, dq, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, max_len, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();

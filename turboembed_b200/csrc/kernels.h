@@ -57,8 +57,11 @@ struct PoolItem {
 
 // One attention work item: `q_count` queries from query `q0` of a row whose
 // tokens start at packed token `start` and number `len`.
+// One attention work item: a query tile of a packed row. holes = 1 when a
+// key inside [0, len) is masked (its live flag is 0), else 0: then only the
+// row's end bounds the keys.
 struct AttnItem {
-    int32_t start, len, q0, pad;
+    int32_t start, len, q0, holes;
 };
 
 // dst[i] = src[i] narrowed from F32 to F16 or BF16 (round to nearest even).
@@ -132,9 +135,15 @@ cudaError_t attention_mma(Dt dt, const void *qkv, void *ctx, const uint8_t *tok_
 cudaError_t attention_tc(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_map, void *ctx,
                          const uint8_t *tok_live, const AttnItem *items, int n_items, int heads, int head_dim,
                          int hidden, int window, int *fault, cudaStream_t s);
+// Full attention (no window) with two 128-query tiles a work item (items at
+// q0 = 0, 256, 512, .. of each row), head width 64, F16/BF16.
+cudaError_t attention_tc2(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_map, void *ctx,
+                          const uint8_t *tok_live, const AttnItem *items, int n_items, int heads, int head_dim,
+                          int hidden, int *fault, cudaStream_t s);
 
 // Query tile of each attention kernel's items.
 constexpr int ATTN_TC_QUERIES = 128;
+constexpr int ATTN_TC2_QUERIES = 256;  // attention_tc2: two 128-query tiles an item
 constexpr int ATTN_MMA_QUERIES = 64;
 constexpr int ATTN_F32_QUERIES = 32;
 

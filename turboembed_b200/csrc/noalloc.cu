@@ -111,7 +111,7 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_noalloc(uint32_t dtype, const 
             const int tiles = (lens[b] + ATTN_TC_QUERIES - 1) / ATTN_TC_QUERIES;
             if (tiles == t) {
                 for (int q = 0; q < tiles; ++q) {
-                    piece[n++] = AttnItem{start, lens[b], q * ATTN_TC_QUERIES, 0};
+                    piece[n++] = AttnItem{start, lens[b], q * ATTN_TC_QUERIES, 1};  // the live flags are read on the device
                     if (n == 256) {
                         e = cudaMemcpyAsync(items + sent, piece, sizeof piece, cudaMemcpyHostToDevice, s);
                         sent += n;
