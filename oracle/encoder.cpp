@@ -531,3 +531,38 @@ extern "C" void oracle_rerank_head(const float *x, uint32_t n, uint32_t hidden, 
         scores[r] = (float)v;
     }
 }
+
+// core/src/quantize.rs:59-71: step = (max - min) / 255 in F32, 1 when that
+// is 0; code = clamp(floor((x - min) / step), 0, 255) - 128, every step an
+// F32 operation (no contraction); NaN clamps to NaN and casts to 0.
+// :74-85: bit x > 0, most significant bit first, a short last byte padded
+// with 0 bits.
+extern "C" int32_t oracle_quantize(uint32_t quantization, const float *x, uint32_t rows, uint32_t dim,
+                                   const float *ranges, uint8_t *out) {
+    if (quantization == 2) {
+        for (uint32_t r = 0; r < rows; ++r)
+            for (uint32_t d = 0; d < dim; ++d) {
+                const float lo = ranges[d], hi = ranges[dim + d];
+                const float step = (hi - lo) / 255.0f;
+                const float st = step == 0.0f ? 1.0f : step;
+                const float f = std::floor((x[(size_t)r * dim + d] - lo) / st);
+                int q;
+                if (std::isnan(f)) q = 0;
+                else q = (int)std::min(std::max(f, 0.0f), 255.0f);
+                out[(size_t)r * dim + d] = (uint8_t)(int8_t)(q - 128);
+            }
+        return 0;
+    }
+    if (quantization == 3) {
+        const uint32_t bpr = (dim + 7) / 8;
+        for (uint32_t r = 0; r < rows; ++r)
+            for (uint32_t j = 0; j < bpr; ++j) {
+                uint8_t byte = 0;
+                for (uint32_t i = 0; i < 8 && j * 8 + i < dim; ++i)
+                    if (x[(size_t)r * dim + j * 8 + i] > 0.0f) byte |= (uint8_t)(0x80u >> i);
+                out[(size_t)r * bpr + j] = byte;
+            }
+        return 0;
+    }
+    return -1;
+}

@@ -51,6 +51,14 @@ void oracle_rope_table(double global_theta, double local_theta, uint32_t positio
 void oracle_rerank_head(const float *x, uint32_t n, uint32_t hidden, const float *pooler_w,
                         const float *pooler_b, const float *cls_w, const float *cls_b, float *scores);
 
+/* int8 and ubinary codes of rows x dim F32 values (core/src/quantize.rs:
+ * int8_row :59-71, ubinary_row :74-85, rows :89-103). quantization is
+ * TURBO_QUANTIZE_INT8 (2) or TURBO_QUANTIZE_UBINARY (3); ranges [2, dim]
+ * (minimums, then maximums) for int8. out holds rows * dim bytes (int8) or
+ * rows * ((dim + 7) / 8) (ubinary). Returns 0, or -1 for another mode. */
+int32_t oracle_quantize(uint32_t quantization, const float *x, uint32_t rows, uint32_t dim, const float *ranges,
+                        uint8_t *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,8 @@ def lib():
                                               C.c_uint64, C.c_void_p]
         _lib.oracle_hidden_states.restype = C.c_int64
         _lib.oracle_rope_table.argtypes = [C.c_double, C.c_double, C.c_uint32, C.c_uint32, C.c_void_p]
+        _lib.oracle_quantize.argtypes = [C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
+        _lib.oracle_quantize.restype = C.c_int32
         _lib.oracle_rerank_head.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                             C.c_void_p, C.c_void_p]
     return _lib
@@ -90,3 +92,18 @@ def rerank_head(x, pooler_w, pooler_b, cls_w, cls_b):
                              *[None if a is None else a.ctypes.data_as(C.c_void_p) for a in args],
                              scores.ctypes.data_as(C.c_void_p))
     return scores
+
+
+def quantize(quantization, x, ranges=None):
+    """int8 (TURBO_QUANTIZE_INT8) or ubinary codes of the rows of x [rows,
+    dim] F32, as uint8 [rows, row_bytes] (core/src/quantize.rs)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, dim = x.shape
+    width = dim if quantization == abi.TURBO_QUANTIZE_INT8 else (dim + 7) // 8
+    out = np.zeros((rows, width), np.uint8)
+    rg = None if ranges is None else np.ascontiguousarray(ranges, np.float32)
+    rc = lib().oracle_quantize(quantization, x.ctypes.data_as(C.c_void_p), rows, dim,
+                               None if rg is None else rg.ctypes.data_as(C.c_void_p), out.ctypes.data_as(C.c_void_p))
+    if rc != 0:
+        raise ValueError(f"quantization {quantization}")
+    return out

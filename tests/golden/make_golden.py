@@ -20,6 +20,9 @@ Fixtures
   tiny_xlmr.npz        an XLM-R (RoBERTa family, position offset 2) with
                        seeded random weights, its mean-pooled L2 vectors
                        computed here by transformers' XLMRobertaModel in F64
+  quantize.npz         testdata/quantize/sentence-transformers-145ef47d.txt:
+                       30 rows (widths 1, 7, 8, 9, 64) of F32 values, int8
+                       ranges and the int8 / ubinary codes numpy made
 """
 import json
 import sys
@@ -164,10 +167,30 @@ def tiny_xlmr():
     np.savez_compressed(HERE / "tiny_xlmr.npz", meta=json.dumps(meta), **arrays)
 
 
+def quantize_table(ref):
+    """The reference's quantization golden table as arrays: per row its
+    width, values, [2, dim] ranges, int8 codes and ubinary codes, each
+    concatenated over the rows (offsets from the widths)."""
+    text = (ref / "testdata/quantize/sentence-transformers-145ef47d.txt").read_text()
+    dims, xs, rgs, i8, ub = [], [], [], [], []
+    for line in text.splitlines():
+        if line.startswith("#") or not line.strip():
+            continue
+        f = line.split(" ")
+        dims.append(int(f[0]))
+        xs.append(np.frombuffer(bytes.fromhex(f[1]), "<f4"))
+        rgs.append(np.frombuffer(bytes.fromhex(f[2]), "<f4"))
+        i8.append(np.frombuffer(bytes.fromhex(f[3]), np.uint8))
+        ub.append(np.frombuffer(bytes.fromhex(f[4]), np.uint8))
+    np.savez_compressed(HERE / "quantize.npz", dims=np.array(dims, np.int32), x=np.concatenate(xs),
+                        ranges=np.concatenate(rgs), int8=np.concatenate(i8), ubinary=np.concatenate(ub))
+
+
 if __name__ == "__main__":
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
     tiny_bert(ref)
     tiny_modernbert(ref)
     tiny_xlmr()
+    quantize_table(ref)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)

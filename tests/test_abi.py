@@ -82,3 +82,10 @@ def test_capability_answers_without_a_device(lib):
     st, dt, opts, reason = b.capability(0, abi.TURBO_TASK_EXTRACTIVE_QA if hasattr(abi, "TURBO_TASK_EXTRACTIVE_QA") else 3,
                                         abi.TURBO_PRECISION_EXACT)
     assert st == abi.TURBO_CAP_UNSUPPORTED and reason
+
+
+def test_table_offers_buffer_quantize(lib):
+    # The device int8 / ubinary codes (turbo_backend.h:609-626) are offered:
+    # the core quantizes device vectors through them instead of on the host.
+    t = runtime.table()
+    assert C.cast(t.buffer_quantize, C.c_void_p).value is not None

@@ -1,5 +1,7 @@
 """The CPU oracle (oracle/, a restatement of the reference CPU encoder) pinned
 against the reference's golden vectors, and its own invariants. CPU only."""
+from pathlib import Path
+
 import numpy as np
 
 from conftest import cosine, load_golden, mask_from_lengths, rerank_rows
@@ -99,3 +101,41 @@ def test_holes_are_masked_keys_and_cls_reads_column_zero():
     holed0[:, 0] = 0
     cls_b = oracle.encode(d, ids, holed0, pooling=abi.TURBO_POOLING_CLS)
     assert cls_a.shape == cls_b.shape and np.isfinite(cls_b).all()
+
+
+def quantize_rows():
+    z = np.load(Path(__file__).resolve().parent / "golden" / "quantize.npz")
+    xo = ro = io = uo = 0
+    for dim in z["dims"]:
+        dim = int(dim)
+        yield (dim, z["x"][xo:xo + dim], z["ranges"][ro:ro + 2 * dim], z["int8"][io:io + dim],
+               z["ubinary"][uo:uo + (dim + 7) // 8])
+        xo, ro, io, uo = xo + dim, ro + 2 * dim, io + dim, uo + (dim + 7) // 8
+
+
+def test_quantize_matches_sentence_transformers_byte_for_byte():
+    # The reference's golden table (core/src/quantize/tests.rs:13-31): five
+    # widths of six rows, int8 and ubinary codes as numpy made them.
+    seen = 0
+    for dim, x, ranges, i8, ub in quantize_rows():
+        assert np.array_equal(oracle.quantize(abi.TURBO_QUANTIZE_INT8, x[None], ranges)[0], i8), dim
+        assert np.array_equal(oracle.quantize(abi.TURBO_QUANTIZE_UBINARY, x[None])[0], ub), dim
+        seen += 1
+    assert seen == 30
+
+
+def test_quantize_edges_by_hand():
+    # core/src/quantize/tests.rs:33-94: buckets, step 0, NaN, infinities, bit
+    # order and padding.
+    q8 = lambda x, r: oracle.quantize(abi.TURBO_QUANTIZE_INT8, np.array([x], np.float32), np.array(r, np.float32))[0].view(np.int8)
+    qb = lambda x: oracle.quantize(abi.TURBO_QUANTIZE_UBINARY, np.array([x], np.float32))[0]
+    r = [0.0] * 5 + [255.0] * 5
+    assert list(q8([-3.0, 0.0, 0.999, 254.5, 1e9], r)) == [-128, -128, -128, 126, 127]
+    assert list(q8([2.0, 2.5, 1.0, 9.0, 0.0], [2.0] * 10)) == [-128, -128, -128, -121, -128]
+    assert list(q8([np.nan, np.inf], [0.0, 0.0, 1.0, 1.0])) == [-128, 127]
+    assert list(q8([1.0], [0.0, 255.0])) == [-127] and list(q8([1.999], [0.0, 255.0])) == [-127]
+    x = [1.0, -1.0, 0.0, -0.0, np.nan, 1e-30, np.inf, -2.0, 3.0]
+    assert list(qb(x)) == [0b1000_0110, 0b1000_0000]
+    assert list(qb([1.0, -1.0, 1.0])) == [0b1010_0000]
+    two = oracle.quantize(abi.TURBO_QUANTIZE_UBINARY, np.array([[1.0, -1.0], [-1.0, 1.0]], np.float32))
+    assert list(two.reshape(-1)) == [0x80, 0x40]

@@ -40,6 +40,7 @@ TURBO_EMBED_STAGE_DOWNLOAD = 6
 TURBO_STAGE_UNUSED, TURBO_STAGE_HOST, TURBO_STAGE_DEVICE, TURBO_STAGE_FUSED = 0, 1, 2, 3
 TURBO_NORMALIZE_MODEL, TURBO_NORMALIZE_NONE, TURBO_NORMALIZE_L2 = 0, 1, 2
 TURBO_POOLING_MODEL, TURBO_POOLING_MEAN, TURBO_POOLING_CLS, TURBO_POOLING_LAST = 0, 1, 2, 3
+TURBO_QUANTIZE_INT8, TURBO_QUANTIZE_UBINARY = 2, 3
 TURBO_PRECISION_MODEL, TURBO_PRECISION_FASTEST, TURBO_PRECISION_EXACT = 0, 1, 2
 TURBO_HANDLE_HOST_PTR, TURBO_HANDLE_CUDA_PTR = 1, 2
 TURBO_FAMILY_BERT, TURBO_FAMILY_ROBERTA, TURBO_FAMILY_MODERNBERT = 1, 2, 5

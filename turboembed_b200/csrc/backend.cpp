@@ -112,6 +112,8 @@ struct Context {
     std::mutex mu;
     int *fault = nullptr;       // device-mapped host word the kernels raise
     int *fault_dev = nullptr;   // its device address
+    void *qscratch = nullptr;   // buffer_quantize's codes and int8 ranges,
+    size_t qscratch_bytes = 0;  // grown on demand (under mu)
 
     void warn(const char *msg) {
         if (log) log(log_user, 1, turbo_text{msg, strlen(msg)});
@@ -335,6 +337,7 @@ void tb_context_release(void *p) {
     cudaStreamSynchronize(c->stream);
     cudaStreamDestroy(c->stream);
     cudaFreeHost(c->fault);
+    cudaFree(c->qscratch);
     delete c;
 }
 
@@ -1184,6 +1187,68 @@ template <class F> auto guarded(turbo_error *err, F f) -> int32_t {
 }
 
 // The table's entries: each a guarded call, so nothing throws across the ABI.
+// core/src/quantize.rs codes of the first rows x dim F32 values of a DEVICE
+// or SHARED buffer, into its leading bytes (turbo_backend.h:609-626; the
+// reference's buffer_quantize, core/cuda/backend.cpp:768-838). The codes go
+// to the context's scratch first (kept between calls, grown when a call
+// needs more: the only allocation, counted into run), then over the floats.
+int32_t tb_buffer_quantize(void *buf, uint32_t quantization, const float *int8_ranges, uint32_t rows, uint32_t dim,
+                           turbo_backend_run *run, turbo_error *err) {
+    auto *b = (Buffer *)buf;
+    if (!b) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "buffer is NULL");
+    if (rows == 0 || dim == 0) {
+        ok(err);
+        return TURBO_OK;
+    }
+    if (quantization != TURBO_QUANTIZE_INT8 && quantization != TURBO_QUANTIZE_UBINARY)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "quantization %u is not TURBO_QUANTIZE_INT8 or UBINARY",
+                    quantization);
+    if (quantization == TURBO_QUANTIZE_INT8 && !int8_ranges)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "int8_ranges is NULL");
+    if (b->placement != TURBO_PLACE_DEVICE && b->placement != TURBO_PLACE_SHARED)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "buffer_quantize needs a DEVICE or SHARED buffer");
+    const uint64_t floats = (uint64_t)rows * dim;
+    const uint64_t code_bytes = quantization == TURBO_QUANTIZE_INT8 ? floats : (uint64_t)rows * ((dim + 7ull) / 8);
+    if (b->bytes < floats * 4)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "buffer of %llu bytes is under the %llu F32 values to quantize",
+                    (unsigned long long)b->bytes, (unsigned long long)floats);
+    if (floats > (uint64_t)INT32_MAX || dim > (uint32_t)INT32_MAX)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "%u x %u values are too many for one call", rows, dim);
+    Context *c = b->ctx;
+    DeviceScope ds(c->device);
+    std::lock_guard<std::mutex> g(c->mu);
+    const uint64_t ranges_at = (code_bytes + 255) / 256 * 256;
+    const uint64_t need = ranges_at + (quantization == TURBO_QUANTIZE_INT8 ? (uint64_t)dim * 8 : 0);
+    if (c->qscratch_bytes < need) {
+        cudaFree(c->qscratch);
+        c->qscratch = nullptr;
+        c->qscratch_bytes = 0;
+        CK(dmalloc(&c->qscratch, need), "buffer_quantize scratch");
+        c->qscratch_bytes = need;
+        if (run) run->device_allocs += 1;
+    }
+    uint8_t *codes = (uint8_t *)c->qscratch;
+    cudaError_t e;
+    if (quantization == TURBO_QUANTIZE_INT8) {
+        float *rg = (float *)(codes + ranges_at);
+        CK(cudaMemcpyAsync(rg, int8_ranges, (size_t)dim * 8, cudaMemcpyHostToDevice, c->stream), "int8_ranges");
+        if (run) run->h2d_bytes += (uint64_t)dim * 8;
+        e = quantize_int8((const float *)b->ptr, rg, (int)rows, (int)dim, codes, c->stream);
+    } else {
+        e = quantize_ubinary((const float *)b->ptr, (int)rows, (int)dim, codes, c->stream);
+    }
+    CK(e, "buffer_quantize");
+    CK(cudaMemcpyAsync(b->ptr, codes, code_bytes, cudaMemcpyDeviceToDevice, c->stream), "buffer_quantize");
+    CK(cudaStreamSynchronize(c->stream), "buffer_quantize");
+    ok(err);
+    return TURBO_OK;
+}
+
+int32_t e_buffer_quantize(void *b, uint32_t q, const float *r, uint32_t rows, uint32_t dim, turbo_backend_run *run,
+                          turbo_error *err) {
+    return guarded(err, [&] { return tb_buffer_quantize(b, q, r, rows, dim, run, err); });
+}
+
 int32_t e_device_count(uint32_t *o, turbo_error *err) { return guarded(err, [&] { return tb_device_count(o, err); }); }
 int32_t e_device_info(uint32_t n, turbo_device_info *o, turbo_error *err) { return guarded(err, [&] { return tb_device_info(n, o, err); }); }
 int32_t e_capability(uint32_t n, uint32_t t, uint32_t p, uint32_t *s, uint32_t *d, uint32_t *o, char *r, uint32_t rl, turbo_error *err) {
@@ -1256,7 +1321,7 @@ TB_EXPORT const turbo_backend turbo_cuda_backend = {
     e_embed_write_ranges,
     0,
     0,
-    nullptr,
+    e_buffer_quantize,
 };
 
 TB_EXPORT uint64_t turbo_cuda_allocations(void) { return g_device_allocs.load(); }

@@ -141,6 +141,12 @@ cudaError_t attention_tc2(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv
                           const uint8_t *tok_live, const AttnItem *items, int n_items, int heads, int head_dim,
                           int hidden, int *fault, cudaStream_t s);
 
+// int8 / ubinary codes of rows x dim F32 values into codes (rows * dim
+// bytes, or rows * ((dim + 7) / 8)); ranges [2, dim] on the device
+// (core/src/quantize.rs).
+cudaError_t quantize_int8(const float *x, const float *ranges, int rows, int dim, uint8_t *codes, cudaStream_t s);
+cudaError_t quantize_ubinary(const float *x, int rows, int dim, uint8_t *codes, cudaStream_t s);
+
 // Query tile of each attention kernel's items.
 constexpr int ATTN_TC_QUERIES = 128;
 constexpr int ATTN_TC2_QUERIES = 256;  // attention_tc2: two 128-query tiles an item

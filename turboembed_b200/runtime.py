@@ -136,6 +136,15 @@ class Buffer:
         _check(self.t.buffer_read(self.h, _ptr(dst), nbytes, C.byref(err)), err, "buffer_read")
         return dst
 
+    def quantize(self, quantization, rows, dim, ranges=None, run=None):
+        """buffer_quantize: int8 / ubinary codes of the first rows x dim F32
+        values, into the buffer's leading bytes (core/src/quantize.rs)."""
+        rg = None if ranges is None else np.ascontiguousarray(ranges, np.float32)
+        err = abi.new_error()
+        _check(self.t.buffer_quantize(self.h, quantization, None if rg is None else rg.ctypes.data_as(C.POINTER(C.c_float)),
+                                      rows, dim, None if run is None else C.byref(run), C.byref(err)),
+               err, "buffer_quantize")
+
     def release(self):
         if self.h and self.owned:
             self.t.buffer_release(self.h)
