@@ -25,6 +25,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <functional>
 #include <cstring>
 #include <limits>
 #include <thread>
@@ -317,7 +318,14 @@ void norm_all(float *x, size_t tokens, uint32_t h, const float *w, const float *
 }
 
 // Returns the packed tokens' final hidden states.
-std::vector<float> encode(const Model &m, const turbo_backend_embed_rows *r, const Packing &P, unsigned threads) {
+// `layers` of the model's layers run (all, or a cut model's first ones);
+// tap(l, states) is handed each layer's output states when set, for layers
+// before the last one run: BERT's x after the layer, ModernBERT's with the
+// final norm applied, the scale the final states are on
+// (core/src/cpu/encoder/mod.rs:298-304, encoder/rotary/mod.rs:82-86).
+using Tap = std::function<void(uint32_t, const float *)>;
+std::vector<float> encode(const Model &m, const turbo_backend_embed_rows *r, const Packing &P, unsigned threads,
+                          uint32_t layers, const Tap &tap) {
     const turbo_backend_model *d = m.d;
     const uint32_t h = m.h, I = m.inter;
     const size_t T = P.tokens;
@@ -341,7 +349,7 @@ std::vector<float> encode(const Model &m, const turbo_backend_embed_rows *r, con
             }
         });
         ffn.resize(T * I);
-        for (uint32_t l = 0; l < d->layers; ++l) {
+        for (uint32_t l = 0; l < layers; ++l) {
             auto w = [&](uint32_t k) { return m.tensor(TURBO_BERT_EMBEDDING_TENSORS + l * TURBO_BERT_LAYER_TENSORS + k); };
             // Q, K and V rows as one [3h, h] product, as the reference packs them.
             std::vector<float> wqkv((size_t)3 * h * h), bqkv(3 * h);
@@ -361,6 +369,7 @@ std::vector<float> encode(const Model &m, const turbo_backend_embed_rows *r, con
             linear(L1, x.data(), h, T, w(TURBO_BERT_FFN_IN_BIAS), ffn.data(), I, EPI_GELU, threads);
             linear(L2, ffn.data(), I, T, w(TURBO_BERT_FFN_OUT_BIAS), x.data(), h, EPI_RESIDUAL, threads);
             norm_all(x.data(), T, h, w(TURBO_BERT_FFN_LN_WEIGHT), w(TURBO_BERT_FFN_LN_BIAS), eps, threads);
+            if (tap && l + 1 < layers) tap(l, x.data());
         }
         return x;
     }
@@ -378,7 +387,7 @@ std::vector<float> encode(const Model &m, const turbo_backend_embed_rows *r, con
     ffn.resize(T * I);
     const size_t positions = d->max_positions, pairs = d->rope_pairs, halftab = positions * pairs;
     const size_t window = d->attention_window ? d->attention_window / 2 : (size_t)-1;
-    for (uint32_t l = 0; l < d->layers; ++l) {
+    for (uint32_t l = 0; l < layers; ++l) {
         auto w = [&](uint32_t k) {
             return m.tensor(TURBO_MODERNBERT_EMBEDDING_TENSORS + l * TURBO_MODERNBERT_LAYER_TENSORS + k);
         };
@@ -412,6 +421,11 @@ std::vector<float> encode(const Model &m, const turbo_backend_embed_rows *r, con
                 }
         });
         linear(L2, ffn.data(), I, T, nullptr, x.data(), h, EPI_RESIDUAL, threads);
+        if (tap && l + 1 < layers) {
+            std::memcpy(xn.data(), x.data(), sizeof(float) * T * h);
+            norm_all(xn.data(), T, h, m.tensor(TURBO_MODERNBERT_FINAL_NORM_WEIGHT), nullptr, eps, threads);
+            tap(l, xn.data());
+        }
     }
     norm_all(x.data(), T, h, m.tensor(TURBO_MODERNBERT_FINAL_NORM_WEIGHT), nullptr, eps, threads);
     return x;
@@ -455,8 +469,32 @@ extern "C" int32_t oracle_encode(const turbo_backend_model *model, const turbo_b
     if (!load(model, m)) return TURBO_E_UNSUPPORTED;
     unsigned th = threads ? threads : std::max(1u, std::thread::hardware_concurrency());
     Packing P = pack(rows, ranges, count);
-    std::vector<float> x = encode(m, rows, P, th);
     const uint32_t h = m.h, od = rows->output_dim ? rows->output_dim : h;
+    const uint32_t L = m.d->layers;
+    // Taps (turbo_backend.h, turbo_backend_embed_rows.taps / tap_alone;
+    // core/src/cpu/encoder/mod.rs:292-304): T > 1 on a range write pools
+    // each range from each of the last T layers into blocks [T, count, od],
+    // the last block the final layer's; tap_alone runs the model cut after
+    // layer L - T + 1 and writes that one block.
+    const uint32_t T = count && rows->taps > 1 ? rows->taps : 1;
+    const bool alone = T > 1 && rows->tap_alone == 1;
+    if (T > L) return TURBO_E_INVALID_ARGUMENT;
+    const uint32_t layers = alone ? L - T + 1 : L, ntaps = alone ? 1 : T;
+    auto pool_ranges = [&](const float *x, uint32_t k) {
+        for (uint32_t i = 0; i < count; ++i) {
+            const turbo_token_range &g = ranges[i];
+            float *dst = out + ((size_t)k * count + i) * od;
+            mean(x, P, rows, g.row, g.start, std::min(g.end, P.len[g.row]), h, dst, od);
+            finish(dst, od, rows->normalize);
+        }
+    };
+    const uint32_t first = layers - ntaps;
+    Tap tap;
+    if (ntaps > 1)
+        tap = [&](uint32_t l, const float *states) {
+            if (l >= first) pool_ranges(states, l - first);
+        };
+    std::vector<float> x = encode(m, rows, P, th, layers, tap);
     if (count == 0) {
         for (uint32_t b = 0; b < rows->batch; ++b) {
             float *dst = out + (size_t)b * od;
@@ -469,12 +507,7 @@ extern "C" int32_t oracle_encode(const turbo_backend_model *model, const turbo_b
         }
         return 0;
     }
-    for (uint32_t i = 0; i < count; ++i) {
-        const turbo_token_range &g = ranges[i];
-        float *dst = out + (size_t)i * od;
-        mean(x.data(), P, rows, g.row, g.start, std::min(g.end, P.len[g.row]), h, dst, od);
-        finish(dst, od, rows->normalize);
-    }
+    pool_ranges(x.data(), ntaps - 1);
     return 0;
 }
 
@@ -484,7 +517,7 @@ extern "C" int64_t oracle_hidden_states(const turbo_backend_model *model, const 
     if (!load(model, m)) return -TURBO_E_UNSUPPORTED;
     unsigned th = threads ? threads : std::max(1u, std::thread::hardware_concurrency());
     Packing P = pack(rows, nullptr, 0);
-    std::vector<float> x = encode(m, rows, P, th);
+    std::vector<float> x = encode(m, rows, P, th, m.d->layers, Tap());
     if (x.size() > cap) return -TURBO_E_CAPACITY;
     std::memcpy(states, x.data(), sizeof(float) * x.size());
     for (uint32_t b = 0; b < rows->batch; ++b) {

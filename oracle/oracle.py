@@ -41,22 +41,25 @@ def lib():
     return _lib
 
 
-def _rows(ids, mask, types, pooling, normalize, output_dim, hidden):
+def _rows(ids, mask, types, pooling, normalize, output_dim, hidden, taps=0, tap_alone=0):
     keep = [np.ascontiguousarray(ids, np.int32), np.ascontiguousarray(mask, np.int32),
             None if types is None else np.ascontiguousarray(types, np.int32)]
     p = [None if a is None else a.ctypes.data_as(C.POINTER(C.c_int32)) for a in keep]
     b, s = keep[0].shape
     r = abi.turbo_backend_embed_rows(C.sizeof(abi.turbo_backend_embed_rows), b, s, s, p[0], p[1], p[2], pooling,
-                                     normalize, output_dim or hidden, 0, 0, 0)
+                                     normalize, output_dim or hidden, 0, taps, tap_alone)
     return r, keep
 
 
 def encode(desc, ids, mask, types=None, pooling=abi.TURBO_POOLING_MEAN, normalize=abi.TURBO_NORMALIZE_L2,
-           output_dim=0, ranges=None, threads=0):
-    """The reference CPU encoder's vectors, [batch or ranges, output_dim]."""
-    r, keep = _rows(ids, mask, types, pooling, normalize, output_dim, desc.hidden)
+           output_dim=0, ranges=None, threads=0, taps=0, tap_alone=0):
+    """The reference CPU encoder's vectors, [batch or ranges, output_dim];
+    with taps T > 1 on a range write [T * ranges, output_dim] (block k from
+    layer L - T + k), or with tap_alone the one block of the model cut
+    after layer L - T + 1."""
+    r, keep = _rows(ids, mask, types, pooling, normalize, output_dim, desc.hidden, taps, tap_alone)
     rg = None if ranges is None else np.ascontiguousarray(ranges, np.uint32).reshape(-1, 3)
-    n = r.batch if rg is None else len(rg)
+    n = r.batch if rg is None else len(rg) * (taps if taps > 1 and not tap_alone else 1)
     out = np.zeros((n, r.output_dim), np.float32)
     rc = lib().oracle_encode(C.byref(desc.struct), C.byref(r), None if rg is None else rg.ctypes.data_as(C.c_void_p),
                              0 if rg is None else len(rg), threads, out.ctypes.data_as(C.c_void_p))

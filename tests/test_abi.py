@@ -78,7 +78,8 @@ def test_device_count_without_a_gpu_is_zero_not_an_error(lib):
 def test_capability_answers_without_a_device(lib):
     b = runtime.Backend()
     st, dt, opts, reason = b.capability(0, abi.TURBO_TASK_EMBED, abi.TURBO_PRECISION_FASTEST)
-    assert st == abi.TURBO_CAP_EXPERIMENTAL and dt == abi.TURBO_DTYPE_F16 and opts == 0x38
+    # Fields 4, 5, 6, 9 and 10 honoured, as the reference's cuda cell (backend.cpp:400).
+    assert st == abi.TURBO_CAP_EXPERIMENTAL and dt == abi.TURBO_DTYPE_F16 and opts == 0x338
     st, dt, opts, reason = b.capability(0, abi.TURBO_TASK_EXTRACTIVE_QA if hasattr(abi, "TURBO_TASK_EXTRACTIVE_QA") else 3,
                                         abi.TURBO_PRECISION_EXACT)
     assert st == abi.TURBO_CAP_UNSUPPORTED and reason

@@ -139,3 +139,23 @@ def test_quantize_edges_by_hand():
     assert list(qb([1.0, -1.0, 1.0])) == [0b1010_0000]
     two = oracle.quantize(abi.TURBO_QUANTIZE_UBINARY, np.array([[1.0, -1.0], [-1.0, 1.0]], np.float32))
     assert list(two.reshape(-1)) == [0x80, 0x40]
+
+
+def test_a_tap_is_the_model_cut_after_its_layer():
+    # core/src/cpu/encoder/taps_tests.rs:70-115: block k of a T-tap range
+    # write equals, bit for bit, the plain range write of the model cut after
+    # layer L - T + k + 1; tap_alone writes that cut model's block alone.
+    for name, L in (("minilm", 3), ("modernbert-base", 4)):
+        d = models.synthetic(name, 7, layers=L)
+        ids, mask, lens = models.rows_long(3, 2, 20, 40, 40, 1000, 30000)
+        ranges = models.ranges_tiling(4, lens, 5, 12)
+        for T in (2, L):
+            got = oracle.encode(d, ids, mask, ranges=ranges, taps=T)
+            n = len(ranges)
+            for k in range(T):
+                # The same seed draws the same first layers.
+                cut = models.synthetic(name, 7, layers=L - T + k + 1)
+                want = oracle.encode(cut, ids, mask, ranges=ranges)
+                assert np.array_equal(got[k * n:(k + 1) * n], want), (name, T, k)
+            alone = oracle.encode(d, ids, mask, ranges=ranges, taps=T, tap_alone=1)
+            assert np.array_equal(alone, got[:n]), (name, T)

@@ -205,6 +205,10 @@ struct Session {
     bool written = false;
     int tokens = 0, batch = 0, n_vectors = 0, n_attn = 0, n_attn2 = 0, max_len = 0;
     uint32_t normalize = TURBO_NORMALIZE_NONE, output_dim = 0;
+    // A range write's layer taps: the run pools each range from each of the
+    // last `taps` of the `layers_run` layers it runs into blocks [taps,
+    // n_vectors, output_dim] (a tap_alone write runs the cut model: taps 1).
+    int taps = 1, layers_run = 0;
     uint64_t h2d_bytes = 0;
     std::vector<int32_t> row_start, row_len;
     // Device time of the last run (events on the context's stream), and,
@@ -285,7 +289,10 @@ int32_t tb_device_info(uint32_t ordinal, turbo_device_info *out, turbo_error *er
 }
 
 // options_honored bits: field 4 (normalize), 5 (pooling), 6 (output_dim).
-constexpr uint32_t OPTIONS_HONORED = (1u << 3) | (1u << 4) | (1u << 5);
+// turbo_embed_options fields 4, 5, 6 (pooling, normalize, output_dim), 9
+// (layer taps) and 10 (layer_alone), one bit each at field - 1: the
+// reference's cuda cell (core/cuda/backend.cpp:400).
+constexpr uint32_t OPTIONS_HONORED = (1u << 3) | (1u << 4) | (1u << 5) | (1u << 8) | (1u << 9);
 
 int32_t tb_capability(uint32_t ordinal, uint32_t task, uint32_t precision, uint32_t *status, uint32_t *dtype,
                       uint32_t *options, char *reason, uint32_t reason_len, turbo_error *err) {
@@ -856,7 +863,15 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
         return fail(err, TURBO_E_CAPACITY, 0, "batch %u x seq %u over the session's %d x %d", r->batch, r->seq,
                     s->max_batch, s->max_seq);
     if (count > (uint32_t)s->max_ranges) return fail(err, TURBO_E_CAPACITY, 0, "%u ranges over max_ranges %d", count, s->max_ranges);
-    if (r->taps > 1 || r->tap_alone) return fail(err, TURBO_E_UNSUPPORTED_OPTION, 9, "layer taps are not built");
+    // Layer taps (turbo_backend.h, turbo_backend_embed_rows.taps and
+    // tap_alone; checked as core/cuda/backend.cpp:3518-3531 checks them).
+    const uint32_t L = (uint32_t)s->m->layers;
+    const bool tapped = r->taps > 1, alone = tapped && r->tap_alone == 1;
+    if (tapped && (count == 0 || r->head || r->taps > L || r->tap_alone > 1 ||
+                   (uint64_t)count * (alone ? 1 : r->taps) > (uint64_t)s->max_ranges))
+        return fail(err, TURBO_E_INTERNAL, 9, "%u ranges from %u layers%s for a session of max_ranges %d and a model of %u layers",
+                    count, r->taps, alone ? ", the first alone," : "", s->max_ranges, L);
+    if (!tapped && r->tap_alone) return fail(err, TURBO_E_INTERNAL, 10, "tap_alone without taps");
     if (r->head) return fail(err, TURBO_E_UNSUPPORTED_OPTION, 0, "a token head is not built");
     const int h = s->m->hidden;
     const uint32_t od = r->output_dim ? r->output_dim : (uint32_t)h;
@@ -967,6 +982,8 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
     s->max_len = max_len;
     s->normalize = r->normalize;
     s->output_dim = od;
+    s->taps = tapped && !alone ? (int)r->taps : 1;
+    s->layers_run = alone ? (int)(L - r->taps + 1) : (int)L;
     s->written = true;
     ok(err);
     return TURBO_OK;
@@ -1026,6 +1043,18 @@ cudaError_t linear(Session *s, const CUtensorMap *amap, const void *a, const Lin
     return timed(s, 0, 2.0 * M * L.n * L.k, [&] { return linear_launch(s, amap, a, L, epi, M, out_map); });
 }
 
+// Block k of a tapped range write: the ranges pooled from layer l's states
+// (l from layers_run - taps, before the last layer; the run pools the last
+// block at its end).
+cudaError_t pool_tap(Session *s, int l, const void *states) {
+    const int first = s->layers_run - s->taps;
+    if (s->taps <= 1 || l < first || l + 1 >= s->layers_run) return cudaSuccess;
+    float *out = (float *)s->out->ptr + (size_t)(l - first) * s->n_vectors * s->output_dim;
+    return pool_vectors(s->dt, states, s->plan_dev + s->lay.tok_live, (const PoolItem *)(s->plan_dev + s->lay.pool),
+                        s->n_vectors, s->m->hidden, (int)s->output_dim, s->normalize == TURBO_NORMALIZE_L2, out,
+                        s->ctx->stream);
+}
+
 cudaError_t encode(Session *s) {
     Model *m = s->m;
     const int h = m->hidden, I = m->inter, T = s->tokens, dh = h / m->heads;
@@ -1064,7 +1093,7 @@ cudaError_t encode(Session *s) {
                                     m->eps, st);
         });
         if (e != cudaSuccess) return e;
-        for (int l = 0; l < m->layers; ++l) {
+        for (int l = 0; l < s->layers_run; ++l) {
             const LayerWeights &L = ws.layers[l];
             Epilogue q;
             q.kind = EPI_STORE, q.bias = L.qkv.bias, q.out = s->qkv, q.ldo = 3 * h;
@@ -1088,6 +1117,7 @@ cudaError_t encode(Session *s) {
             if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln2_w, L.ln2_b, T, h, m->eps, st); })) !=
                 cudaSuccess)
                 return e;
+            if ((e = pool_tap(s, l, s->x)) != cudaSuccess) return e;
         }
         return cudaSuccess;
     }
@@ -1097,7 +1127,7 @@ cudaError_t encode(Session *s) {
     });
     if (e != cudaSuccess) return e;
     const size_t half_tab = (size_t)m->positions * m->rope_pairs;
-    for (int l = 0; l < m->layers; ++l) {
+    for (int l = 0; l < s->layers_run; ++l) {
         const LayerWeights &L = ws.layers[l];
         const bool global = m->global_every == 0 || l % m->global_every == 0;
         const float *cos_t = m->rope + (global ? 0 : 2 * half_tab), *sin_t = cos_t + half_tab;
@@ -1127,6 +1157,12 @@ cudaError_t encode(Session *s) {
         Epilogue f2;
         f2.kind = EPI_RESIDUAL, f2.out = s->x, f2.ldo = h;
         if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) return e;
+        // A tap before the last layer reads the layer's states through the
+        // final norm, the scale the final states are on.
+        if (s->taps > 1 && l + 1 < s->layers_run && l >= s->layers_run - s->taps) {
+            if ((e = layer_norm(dt, s->x, s->xn, m->final_w, nullptr, T, h, m->eps, st)) != cudaSuccess) return e;
+            if ((e = pool_tap(s, l, s->xn)) != cudaSuccess) return e;
+        }
     }
     (void)es;
     return timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, m->final_w, nullptr, T, h, m->eps, st); });
@@ -1146,7 +1182,7 @@ int32_t tb_session_run(void *p, turbo_backend_run *out, turbo_error *err) {
     if (e == cudaSuccess)
         e = pool_vectors(s->dt, s->x, s->plan_dev + s->lay.tok_live, (const PoolItem *)(s->plan_dev + s->lay.pool),
                          s->n_vectors, s->m->hidden, (int)s->output_dim, s->normalize == TURBO_NORMALIZE_L2,
-                         (float *)s->out->ptr, c->stream);
+                         (float *)s->out->ptr + (size_t)(s->taps - 1) * s->n_vectors * s->output_dim, c->stream);
     if (e != cudaSuccess) {
         cudaStreamSynchronize(c->stream);
         return cuda_fail(err, e, "session_run launch");

@@ -187,14 +187,14 @@ class Session:
         self.hidden = model.desc.hidden
         self._out_dim, self._count = 0, 0
 
-    def _rows(self, ids, mask, types, pooling, normalize, output_dim):
+    def _rows(self, ids, mask, types, pooling, normalize, output_dim, taps=0, tap_alone=0):
         ids = np.ascontiguousarray(ids, np.int32)
         mask = np.ascontiguousarray(mask, np.int32)
         types = None if types is None else np.ascontiguousarray(types, np.int32)
         self._keep = (ids, mask, types)
         b, s = ids.shape
         r = abi.turbo_backend_embed_rows(C.sizeof(abi.turbo_backend_embed_rows), b, s, s, _i32p(ids), _i32p(mask),
-                                         _i32p(types), pooling, normalize, output_dim or self.hidden, 0, 0, 0)
+                                         _i32p(types), pooling, normalize, output_dim or self.hidden, 0, taps, tap_alone)
         return r
 
     def write(self, ids, mask, types=None, pooling=abi.TURBO_POOLING_MEAN, normalize=abi.TURBO_NORMALIZE_L2,
@@ -204,14 +204,18 @@ class Session:
         _check(self.t.embed_write(self.h, C.byref(r), C.byref(err)), err, "embed_write")
         self._out_dim, self._count = r.output_dim, r.batch
 
-    def write_ranges(self, ids, mask, ranges, types=None, normalize=abi.TURBO_NORMALIZE_L2, output_dim=0):
-        r = self._rows(ids, mask, types, abi.TURBO_POOLING_MEAN, normalize, output_dim)
+    def write_ranges(self, ids, mask, ranges, types=None, normalize=abi.TURBO_NORMALIZE_L2, output_dim=0, taps=0,
+                     tap_alone=0):
+        """embed_write_ranges; taps T > 1 pools each range from each of the
+        last T layers ([T * ranges, output_dim] after the run), tap_alone 1
+        from the model cut after layer L - T + 1 alone."""
+        r = self._rows(ids, mask, types, abi.TURBO_POOLING_MEAN, normalize, output_dim, taps, tap_alone)
         rg = np.ascontiguousarray(ranges, np.uint32).reshape(-1, 3)
         self._keep_ranges = rg
         err = abi.new_error()
         _check(self.t.embed_write_ranges(self.h, C.byref(r), rg.ctypes.data_as(C.POINTER(abi.turbo_token_range)),
                                          len(rg), C.byref(err)), err, "embed_write_ranges")
-        self._out_dim, self._count = r.output_dim, len(rg)
+        self._out_dim, self._count = r.output_dim, len(rg) * (taps if taps > 1 and not tap_alone else 1)
 
     def run(self):
         out, err = abi.turbo_backend_run(), abi.new_error()
