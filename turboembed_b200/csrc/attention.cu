@@ -6,14 +6,21 @@
 // sliding window (|i - j| > window), scores -inf; softmax over the row's keys;
 // a query that reads no live key gets a zero context.
 //
-//  attention_simt: one warp per query, scores in shared memory, F32 sums:
-//    the EXACT tier's, and the F16/BF16 one for head widths other than
-//    16, 32 and 64.
+//  attention_simt: F32 (the EXACT tier) at head widths 32 and 64 runs
+//    attn_f32_kernel, a flash-style FFMA kernel: 64 queries x 64 keys a
+//    step, Q, K, V and P tiles in shared memory (Q, K and P transposed so a
+//    thread's four rows or keys are one 16-byte read), each thread a 4 x 4
+//    block of scores and of the context, online softmax with expf and F32
+//    sums. Other widths (and F16/BF16 at widths the tensor-core kernels do
+//    not take) run attn_simt_kernel: one warp per query, scores in shared
+//    memory, F32 sums.
 //  attention_mma: F16/BF16 operands with F32 sums, flash-style: 64 queries a
 //    block (16 a warp), keys in chunks of 64 through a double-buffered
 //    cp.async ring, online softmax in base 2, mma.sync m16n8k16. Chunks
 //    wholly outside a sliding window are never loaded.
 #include "kernels.h"
+
+#include <type_traits>
 
 namespace tb {
 namespace {
@@ -76,6 +83,147 @@ attn_simt_kernel(const T *__restrict__ qkv, T *__restrict__ ctx, const uint8_t *
             st(out + c, acc);
         }
         __syncwarp();
+    }
+}
+
+// ----------------------------------------------------- F32 flash (FFMA) ----
+
+constexpr int FQ = ATTN_F32_QUERIES;  // 64 queries a block
+constexpr int FK = 64;                // keys a step
+constexpr int FPAD = 4;               // floats of padding per transposed row
+
+template <int D> constexpr int f32_smem_bytes() { return (2 * D * (FQ + FPAD) + FK * D + FK * (FQ + FPAD) + FK) * 4; }
+
+// Threads (tq, tk) = (tid / 16, tid % 16): query rows 4 tq .. 4 tq + 3, keys
+// 4 tk .. 4 tk + 3 of a step's scores, and columns CPT tk .. of the context.
+template <int D>
+__global__ void __launch_bounds__(256) attn_f32_kernel(const float *__restrict__ qkv, float *__restrict__ ctx,
+                                                       const uint8_t *__restrict__ live,
+                                                       const AttnItem *__restrict__ items, int h, int window) {
+    constexpr int CPT = D / 16;   // context columns a thread
+    constexpr int LQ = FQ + FPAD;  // transposed row length (queries or keys)
+    extern __shared__ float4 f32_smem[];
+    auto Qt = reinterpret_cast<float(*)[LQ]>(f32_smem);
+    auto Kt = reinterpret_cast<float(*)[LQ]>(&Qt[D][0]);
+    auto Vs = reinterpret_cast<float(*)[D]>(&Kt[D][0]);
+    auto Pt = reinterpret_cast<float(*)[LQ]>(&Vs[FK][0]);
+    float *kbias = &Pt[FK][0];
+    pdl_wait();
+    pdl_trigger();
+    const int tid = threadIdx.x, tq = tid >> 4, tk = tid & 15;
+    const AttnItem it = items[blockIdx.x];
+    const int head = blockIdx.y;
+    const int64_t ld = 3 * (int64_t)h;
+    const float *base = qkv + (int64_t)it.start * ld;
+    const float scale = 1.0f / sqrtf((float)D);
+    // Q tile, transposed; rows past the row's end read row 0 (never stored).
+    for (int i = tid; i < FQ * D / 4; i += 256) {
+        const int q = i / (D / 4), c4 = (i % (D / 4)) * 4;
+        const int qi = it.q0 + q < it.len ? it.q0 + q : 0;
+        const float4 v = *reinterpret_cast<const float4 *>(base + qi * ld + head * D + c4);
+        Qt[c4][q] = v.x, Qt[c4 + 1][q] = v.y, Qt[c4 + 2][q] = v.z, Qt[c4 + 3][q] = v.w;
+    }
+    int klo = 0, khi = it.len;
+    if (window >= 0) {
+        klo = max(0, it.q0 - window);
+        khi = min(it.len, it.q0 + FQ - 1 + window + 1);
+    }
+    float o[4][CPT] = {};
+    float m[4], l[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) m[r] = -INFINITY, l[r] = 0.0f;
+    for (int k0 = klo; k0 < khi; k0 += FK) {
+        __syncthreads();  // the previous step's K, V and P are read
+        for (int i = tid; i < FK * D / 4; i += 256) {
+            const int k = i / (D / 4), c4 = (i % (D / 4)) * 4;
+            const int kj = k0 + k < khi ? k0 + k : klo;
+            const float *row = base + kj * ld + head * D + c4;
+            const float4 kv = *reinterpret_cast<const float4 *>(row + h);
+            Kt[c4][k] = kv.x, Kt[c4 + 1][k] = kv.y, Kt[c4 + 2][k] = kv.z, Kt[c4 + 3][k] = kv.w;
+            *reinterpret_cast<float4 *>(&Vs[k][c4]) = *reinterpret_cast<const float4 *>(row + 2 * h);
+        }
+        if (tid < FK) kbias[tid] = (k0 + tid < khi && live[it.start + k0 + tid]) ? 0.0f : -INFINITY;
+        __syncthreads();
+        // Scores: one FMA chain over d per (query, key), as the CPU path.
+        float sc[4][4] = {};
+#pragma unroll 8
+        for (int d = 0; d < D; ++d) {
+            const float4 a = *reinterpret_cast<const float4 *>(&Qt[d][4 * tq]);
+            const float4 b = *reinterpret_cast<const float4 *>(&Kt[d][4 * tk]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sc[r][c] = fmaf(av[r], bv[c], sc[r][c]);
+        }
+        float cmax[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int qi = it.q0 + 4 * tq + r;
+            cmax[r] = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int kj = k0 + 4 * tk + c;
+                float v = sc[r][c] * scale + kbias[4 * tk + c];
+                if (window >= 0 && abs(qi - kj) > window) v = -INFINITY;
+                sc[r][c] = v;
+                cmax[r] = fmaxf(cmax[r], v);
+            }
+        }
+        // Row maxima over the 16 threads of a row group (one half-warp).
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) cmax[r] = fmaxf(cmax[r], __shfl_xor_sync(0xffffffffu, cmax[r], off));
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float mn = fmaxf(m[r], cmax[r]);
+            const float corr = mn == -INFINITY ? 1.0f : expf(m[r] - mn);  // exp(-inf) = 0 for the first step
+            m[r] = mn;
+            l[r] *= corr;
+#pragma unroll
+            for (int c = 0; c < CPT; ++c) o[r][c] *= corr;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float p = mn == -INFINITY ? 0.0f : expf(sc[r][c] - mn);
+                sc[r][c] = p;
+                l[r] += p;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<float4 *>(&Pt[4 * tk + c][4 * tq]) = make_float4(sc[0][c], sc[1][c], sc[2][c], sc[3][c]);
+        __syncthreads();
+        // Context: O[rows][cols] += P[rows][keys] V[keys][cols].
+#pragma unroll 4
+        for (int k = 0; k < FK; ++k) {
+            const float4 p = *reinterpret_cast<const float4 *>(&Pt[k][4 * tq]);
+            const float pv[4] = {p.x, p.y, p.z, p.w};
+            float vv[CPT];
+            if constexpr (CPT == 4) {
+                const float4 v = *reinterpret_cast<const float4 *>(&Vs[k][4 * tk]);
+                vv[0] = v.x, vv[1] = v.y, vv[2] = v.z, vv[3] = v.w;
+            } else {
+                const float2 v = *reinterpret_cast<const float2 *>(&Vs[k][2 * tk]);
+                vv[0] = v.x, vv[1] = v.y;
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < CPT; ++c) o[r][c] = fmaf(pv[r], vv[c], o[r][c]);
+        }
+    }
+    // Row sums over the row group; a query that read no live key gets 0.
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) l[r] += __shfl_xor_sync(0xffffffffu, l[r], off);
+        const int qi = it.q0 + 4 * tq + r;
+        if (qi >= it.len) continue;
+        const float inv = l[r] > 0.0f ? 1.0f / l[r] : 0.0f;
+        float *out = ctx + ((int64_t)it.start + qi) * h + head * D + CPT * tk;
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) out[c] = o[r][c] * inv;
     }
 }
 
@@ -300,6 +448,18 @@ cudaError_t launch_mma(const void *qkv, void *ctx, const uint8_t *live, const At
 template <class T>
 cudaError_t launch_simt(const void *qkv, void *ctx, const uint8_t *tok_live, const AttnItem *items, int n_items,
                         int heads, int head_dim, int hidden, int window, int max_len, cudaStream_t s) {
+    if (std::is_same<T, float>::value && (head_dim == 64 || head_dim == 32)) {
+        dim3 grid(n_items, heads);
+        if (head_dim == 64) {
+            cudaError_t e = cudaFuncSetAttribute(attn_f32_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 f32_smem_bytes<64>());
+            if (e != cudaSuccess) return e;
+            return launch_pdl(attn_f32_kernel<64>, grid, 256, f32_smem_bytes<64>(), s, (const float *)qkv, (float *)ctx,
+                              tok_live, items, hidden, window);
+        }
+        return launch_pdl(attn_f32_kernel<32>, grid, 256, f32_smem_bytes<32>(), s, (const float *)qkv, (float *)ctx,
+                          tok_live, items, hidden, window);
+    }
     int lp = (max_len + 31) / 32 * 32;
     size_t smem = (size_t)F32_WARPS * (lp + 128) * sizeof(float);
     if (head_dim > 128) return cudaErrorNotSupported;

@@ -151,6 +151,6 @@ cudaError_t quantize_ubinary(const float *x, int rows, int dim, uint8_t *codes, 
 constexpr int ATTN_TC_QUERIES = 128;
 constexpr int ATTN_TC2_QUERIES = 256;  // attention_tc2: two 128-query tiles an item
 constexpr int ATTN_MMA_QUERIES = 64;
-constexpr int ATTN_F32_QUERIES = 32;
+constexpr int ATTN_F32_QUERIES = 64;
 
 }  // namespace tb
