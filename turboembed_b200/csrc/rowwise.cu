@@ -168,6 +168,79 @@ __global__ void __launch_bounds__(256) ln_vec_kernel(const T *__restrict__ src, 
     }
 }
 
+// The F16/BF16 LayerNorm: as ln_vec_kernel (the same sums in the same
+// order, so the same bits), with each lane's weights and biases held in
+// registers for all its rows (its columns never change) and the next row's
+// loads issued before this row's arithmetic. Two blocks an SM.
+template <class T, int CPL>
+__global__ void __launch_bounds__(256, 2) ln_reg_kernel(const T *__restrict__ src, T *dst,
+                                                        const float *__restrict__ ln_w,
+                                                        const float *__restrict__ ln_b, int tokens, int h, float eps) {
+    using V = Vec<T>;
+    constexpr int N = V::N;
+    const int lane = threadIdx.x & 31;
+    const int chunks = h / N;
+    float w[CPL][N], b[CPL][N];
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+        const int c = lane + 32 * i;
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            w[i][j] = c < chunks ? ln_w[c * N + j] : 0.0f;
+            b[i][j] = c < chunks && ln_b ? ln_b[c * N + j] : 0.0f;
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    float cur[CPL][N], nxt[CPL][N];
+    auto load = [&](int tok, float (*v)[N]) {
+        const T *in = src + (int64_t)tok * h;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) V::load(in + c * N, v[i]);
+        }
+    };
+    if (t < tokens) load(t, cur);
+    for (; t < tokens; t += warps) {
+        if (t + warps < tokens) load(t + warps, nxt);
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i)
+            if (lane + 32 * i < chunks)
+#pragma unroll
+                for (int j = 0; j < N; ++j) s += cur[i][j];
+        const float mean = warp_sum(s) / (float)h;
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i)
+            if (lane + 32 * i < chunks)
+#pragma unroll
+                for (int j = 0; j < N; ++j) {
+                    const float d = cur[i][j] - mean;
+                    q += d * d;
+                }
+        const float inv = 1.0f / sqrt(warp_sum(q) / (float)h + eps);
+        T *out = dst + (int64_t)t * h;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+                float o[N];
+#pragma unroll
+                for (int j = 0; j < N; ++j) o[j] = (float)((cur[i][j] - mean) * inv) * w[i][j] + b[i][j];
+                V::store(out + c * N, o);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < CPL; ++i)
+#pragma unroll
+            for (int j = 0; j < N; ++j) cur[i][j] = nxt[i][j];
+    }
+}
+
 // One block per output vector. Each thread owns columns tid, tid + blockDim,
 // .. of the cut and sums its tokens in column (position) order, as the
 // reference's mean does; L2 in F64 over the block.
@@ -317,11 +390,20 @@ template <class T>
 cudaError_t ln_launch(const void *src, void *dst, const float *w, const float *b, int tokens, int h, double eps,
                       cudaStream_t s) {
     const int chunks = h / Vec<T>::N, cpl = (chunks + 31) / 32;
+    const T *in = (const T *)src;
+    T *out = (T *)dst;
+    if constexpr (sizeof(T) == 2) {
+        // Resident blocks only (2 of 256 threads an SM), each warp streaming rows.
+        const int g = std::min(148 * 2, (tokens + 7) / 8);
+        const float fe = (float)eps;
+        if (cpl <= 1) return launch_pdl(ln_reg_kernel<T, 1>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
+        if (cpl <= 2) return launch_pdl(ln_reg_kernel<T, 2>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
+        if (cpl <= 3) return launch_pdl(ln_reg_kernel<T, 3>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
+        // Wider rows would spill their weights: the shared-memory kernel.
+    }
     // Resident blocks only (3 of 256 threads an SM at 78 registers), each
     // warp streaming rows.
     const int g = std::min(148 * 3, (tokens + 15) / 16);
-    const T *in = (const T *)src;
-    T *out = (T *)dst;
     if (cpl <= 1) return launch_pdl(ln_vec_kernel<T, 1>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
     if (cpl <= 2) return launch_pdl(ln_vec_kernel<T, 2>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
     if (cpl <= 3) return launch_pdl(ln_vec_kernel<T, 3>, g, 256, 0, s, in, out, w, b, tokens, h, eps);
