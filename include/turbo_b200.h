@@ -69,6 +69,14 @@ TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t variant, uint32
                                         const float *cos_t, const float *sin_t, uint32_t positions,
                                         turbo_error *err);
 
+/* The fused residual + LayerNorm GEMM on N = 768 or 1024 columns (a
+ * cluster of N / 256 CTA pairs exchanging row statistics):
+ * y_out = LN(y_in + a w^T + bias) * ln_w + ln_b with LayerNorm epsilon eps,
+ * host F32 operands narrowed to dtype (F16 or BF16), y_out widened back. */
+TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K, const float *a,
+                                           const float *w, const float *bias, const float *y_in, const float *ln_w,
+                                           const float *ln_b, float eps, float *y_out, turbo_error *err);
+
 /* Attention over `batch` rows packed one after another (row b has lens[b]
  * tokens), qkv [tokens, 3 * hidden] host F32 narrowed to dtype, live [tokens]
  * the mask entries, window < 0 for whole rows. variant 0 is the F16/BF16

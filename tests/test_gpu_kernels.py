@@ -100,6 +100,33 @@ def test_tcgen05_gemm_rope(dtype, head_dim, h):
     assert rel_err(got, simt) < tol
 
 
+LN_SHAPES = [(300, 768, 768), (2000, 768, 3072), (513, 1024, 1024), (1, 768, 768), (77, 1024, 4096),
+             (4096, 768, 768)]
+
+
+@pytest.mark.parametrize("dtype", [F16, BF16])
+@pytest.mark.parametrize("shape", LN_SHAPES)
+def test_tcgen05_gemm_residual_layernorm(dtype, shape):
+    # The post-LN layers' residual + LayerNorm fused into the GEMM: a cluster
+    # of N / 256 CTA pairs exchanges row statistics; against numpy in F64 on
+    # the same narrowed operands.
+    M, N, K = shape
+    rng = np.random.default_rng(M + N + K)
+    a = rng.standard_normal((M, K), np.float32)
+    w = rng.standard_normal((N, K), np.float32) * np.float32(1 / np.sqrt(K))
+    bias = rng.standard_normal(N).astype(np.float32)
+    y_in = rng.standard_normal((M, N)).astype(np.float32) * 3
+    ln_w = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    ln_b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    got = runtime.gemm_ln_check(dtype, a, w, bias, y_in, ln_w, ln_b, 1e-12)
+    v = ref_gemm(dtype, 2, a, w, bias, y_in)
+    mean = v.mean(1, keepdims=True)
+    var = ((v - mean) ** 2).mean(1, keepdims=True)
+    want = (v - mean) / np.sqrt(var + 1e-12) * ln_w + ln_b
+    # The sum v is rounded to nothing here (F32 in TMEM); the output to F16 / BF16.
+    assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
+
+
 @pytest.mark.parametrize("epi", [0, 1, 2, 3])
 def test_ffma_gemm_f32_is_one_chain_over_k(epi):
     M, N, K = 150, 160, 200

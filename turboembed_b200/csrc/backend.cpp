@@ -209,6 +209,10 @@ struct Session {
     // last `taps` of the `layers_run` layers it runs into blocks [taps,
     // n_vectors, output_dim] (a tap_alone write runs the cut model: taps 1).
     int taps = 1, layers_run = 0;
+    // Post-LN layers fold their LayerNorm into the residual GEMMs
+    // (EPI_RESIDUAL_LN), unless the environment sets TB_LNFUSE=0 (an A/B
+    // switch, read at session open).
+    bool fuse_ln = false;
     uint64_t h2d_bytes = 0;
     std::vector<int32_t> row_start, row_len;
     // Device time of the last run (events on the context's stream), and,
@@ -765,6 +769,10 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
     if (cap > (int64_t)1 << 30) return fail(err, TURBO_E_CAPACITY, 1, "max_batch x max_seq too large");
     s->cap_tokens = (int)cap;
     s->cap_vectors = std::max(s->max_batch, s->max_ranges);
+    {
+        const char *v = getenv("TB_LNFUSE");
+        s->fuse_ln = !m->modern && dt != Dt::F32 && !(v && v[0] == '0') && gemm_ln_fusable(dt, m->hidden);
+    }
     const int qt = attention_queries(s.get());
     s->max_attn_items = (int)(cap / qt) + s->max_batch + 1;
     s->max_attn2_items = attention_pairs(s.get()) ? (int)(cap / ATTN_TC2_QUERIES) + s->max_batch + 1 : 0;
@@ -1101,9 +1109,11 @@ cudaError_t encode(Session *s) {
             if ((e = attention(-1)) != cudaSuccess) return e;
             Epilogue o;
             o.kind = EPI_RESIDUAL, o.bias = L.out.bias, o.out = s->x, o.ldo = h;
+            if (s->fuse_ln) o.kind = EPI_RESIDUAL_LN, o.ln_w = L.ln1_w, o.ln_b = L.ln1_b, o.ln_eps = (float)m->eps;
             if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
-            if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln1_w, L.ln1_b, T, h, m->eps, st); })) !=
-                cudaSuccess)
+            if (!s->fuse_ln &&
+                (e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln1_w, L.ln1_b, T, h, m->eps, st); })) !=
+                    cudaSuccess)
                 return e;
             Epilogue f1;
             // FASTEST takes the tanh form, as the reference's FASTEST does;
@@ -1113,9 +1123,11 @@ cudaError_t encode(Session *s) {
             if ((e = linear(s, &s->map_x, s->x, L.ffn_in, f1, T, &s->out_ffn)) != cudaSuccess) return e;
             Epilogue f2;
             f2.kind = EPI_RESIDUAL, f2.bias = L.ffn_out.bias, f2.out = s->x, f2.ldo = h;
+            if (s->fuse_ln) f2.kind = EPI_RESIDUAL_LN, f2.ln_w = L.ln2_w, f2.ln_b = L.ln2_b, f2.ln_eps = (float)m->eps;
             if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) return e;
-            if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln2_w, L.ln2_b, T, h, m->eps, st); })) !=
-                cudaSuccess)
+            if (!s->fuse_ln &&
+                (e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln2_w, L.ln2_b, T, h, m->eps, st); })) !=
+                    cudaSuccess)
                 return e;
             if ((e = pool_tap(s, l, s->x)) != cudaSuccess) return e;
         }

@@ -36,7 +36,10 @@ namespace {
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
 using namespace tc;
 
-template <int BN, bool PAIR> struct Cfg {
+// LNS > 0: the fused residual + LayerNorm epilogue over rows of N = 256 LNS
+// columns, computed by a cluster of LNS CTA pairs (one 256-column slice a
+// pair) that exchange row statistics through distributed shared memory.
+template <int BN, bool PAIR, int LNS = 0> struct Cfg {
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // W rows this CTA loads a stage
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -44,11 +47,14 @@ template <int BN, bool PAIR> struct Cfg {
     static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : 5;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int MAX_BIAS = 4096;  // the bias vector, staged in shared memory once per CTA
+    static constexpr int MAX_BIAS = LNS ? 1024 : 4096;  // the bias vector, staged in shared memory once per CTA
     // Output staging for TMA stores: two [32 x 32] 16-bit tiles per epilogue warp.
     static constexpr int STORE_BYTES = 8 * 2 * 2048;
-    // ring | barriers (padded to 1 KB) | store staging | bias
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + STORE_BYTES + MAX_BIAS * 4 + 1024;
+    // LayerNorm weight and bias [N], and the row statistics two tiles deep:
+    // [2][4 row quarters][2 LNS parts][32 rows] (mean, M2).
+    static constexpr int LN_BYTES = LNS ? 2 * 1024 * 4 + 2 * 4 * 2 * LNS * 32 * 8 : 0;
+    // ring | barriers (padded to 1 KB) | store staging | bias | LayerNorm
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + STORE_BYTES + MAX_BIAS * 4 + LN_BYTES + 1024;
 };
 
 // Instruction descriptor of kind::f16: F32 accumulator, A and B the same
@@ -287,17 +293,127 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
     }
 }
 
+// The fused residual + LayerNorm epilogue (EPI_RESIDUAL_LN) of one warp's 32
+// rows and COLS columns of a 256-column slice. v = acc + bias + residual;
+// the warp's part of each row's statistics (mean and M2 over its COLS
+// columns, one pass over TMEM) goes to every CTA of the cluster holding
+// the same rows (slot `slot` of their statistics buffers, then an arrival
+// on their barrier for this row quarter); once all 2 LNS parts are in, the
+// row's mean and variance follow by Chan's pairwise formula, and a second
+// pass writes (v - mean) / sqrt(var + eps) * ln_w + ln_b. Returns false when
+// a wait gave up.
+struct LnStep {
+    const float *w_s, *b_s;  // LayerNorm weight and bias in shared memory [N]
+    uint32_t stats;          // this CTA's statistics block for this tile and quarter: [2 LNS][32] float2
+    const float2 *stats_p;   // the same, as a generic pointer
+    uint32_t bar;            // this quarter's statistics barrier
+    uint32_t phase;
+    uint32_t half;           // the pair half (rank & 1): the CTAs with the same rows are half + 2 j
+    int slot;                // 2 * slice + part
+};
+
+template <class T, int COLS, int LNS, class Release>
+__device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
+                                                 bool row_ok, int col_base, const uint4 *res, StoreStage &ss,
+                                                 const CUtensorMap *out_map, const LnStep &L, volatile int *abort_flag,
+                                                 int *fault, Release release) {
+    const int lane = threadIdx.x & 31;
+    float v[32];
+    // Pass 1: v = accumulator + bias + residual, written back to TMEM (pass
+    // 2 reads it from there); the part's sums of (v - k) and (v - k)^2 about
+    // k, its first value (a shift that keeps the one-pass variance from
+    // cancelling).
+    float s1 = 0.0f, s2 = 0.0f, k = 0.0f;
+#pragma unroll
+    for (int c = 0; c < COLS; c += 32) {
+        __syncwarp();
+        tmem_ld32(tbase + c, v);
+        const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col_base + c);
+        const uint4 *rq = res + (c / 32) * 4;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 bb = e.bias ? b4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            v[4 * i] += bb.x, v[4 * i + 1] += bb.y, v[4 * i + 2] += bb.z, v[4 * i + 3] += bb.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w4[4] = {rq[i].x, rq[i].y, rq[i].z, rq[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = unpack2<T>(w4[j]);
+                v[8 * i + 2 * j] += f.x;
+                v[8 * i + 2 * j + 1] += f.y;
+            }
+        }
+        tmem_st32(tbase + c, v);
+        if (c == 0) k = v[0];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float d = v[i] - k;
+            s1 += d;
+            s2 = fmaf(d, d, s2);
+        }
+    }
+    const float mean_p = k + s1 / (float)COLS;
+    const float m2 = fmaxf(s2 - s1 * (s1 / (float)COLS), 0.0f);
+    // This part to the LNS CTAs holding these rows, then one arrival each.
+    const uint32_t mine = L.stats + (uint32_t)((L.slot * 32 + lane) * 8);
+#pragma unroll
+    for (int j = 0; j < LNS; ++j) st_cluster_v2(mapa(mine, L.half + 2 * j), mean_p, m2);
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+    __syncwarp();
+    if (lane == 0)
+#pragma unroll
+        for (int j = 0; j < LNS; ++j) mbar_arrive_cluster(mapa(L.bar, L.half + 2 * j));
+    if (!mbar_wait_cluster(L.bar, L.phase, abort_flag, fault)) {
+        release();
+        return false;
+    }
+    // Chan: mean = the parts' mean (equal counts), M2 = sum M2_p + COLS sum (mean_p - mean)^2.
+    float ms = 0.0f;
+#pragma unroll
+    for (int p = 0; p < 2 * LNS; ++p) ms += L.stats_p[p * 32 + lane].x;
+    const float mean = ms / (float)(2 * LNS);
+    float M2 = 0.0f;
+#pragma unroll
+    for (int p = 0; p < 2 * LNS; ++p) {
+        const float2 q = L.stats_p[p * 32 + lane];
+        const float d = q.x - mean;
+        M2 += q.y + (float)COLS * d * d;
+    }
+    const float inv = 1.0f / sqrtf(M2 / (float)(2 * LNS * COLS) + e.ln_eps);
+    // Pass 2: normalise and store.
+#pragma unroll 1
+    for (int c = 0; c < COLS; c += 32) {
+        __syncwarp();
+        tmem_ld32(tbase + c, v);
+        if (c + 32 >= COLS) release();
+        const int col = col_base + c;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = (v[i] - mean) * inv * L.w_s[col + i] + L.b_s[col + i];
+        if (ss.tma) stage_store32<T>(v, col, ss, out_map);
+        else if (row_ok) store_n<T, 32>((T *)e.out + (int64_t)row * e.ldo + col, v);
+    }
+    return true;
+}
+
 // PAIR = false: one CTA computes a 128 x BN tile. PAIR = true: a cluster of
 // two CTAs computes a 256 x BN tile with tcgen05.mma.cta_group::2: each CTA
 // loads its own 128 rows of A and BN/2 rows of W (no multicast), the
 // leader (rank 0) issues the MMAs for both, and each CTA's TMEM holds its
 // 128 rows of the product.
-template <class T, int BN, int EPI_WG, bool PAIR>
+//
+// LNS > 0 (EPI_RESIDUAL_LN, N = 256 LNS): a cluster of LNS pairs, ranks 2 j
+// and 2 j + 1 the pair of column slice j, loops over 256-row blocks; every
+// pair takes the same block, so each row's statistics meet within the
+// cluster (epilogue_ln_tile).
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0>
 __global__ void __launch_bounds__(128 + 128 * EPI_WG, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
                const __grid_constant__ CUtensorMap tout, int use_tma_store, int M, int N, int K, Epilogue e,
                int *fault) {
-    using C = Cfg<BN, PAIR>;
+    static_assert(LNS == 0 || (PAIR && BN == 256), "the fused LayerNorm runs on 256-column CTA pairs");
+    using C = Cfg<BN, PAIR, LNS>;
     constexpr int TM = PAIR ? 2 * BM : BM;  // rows a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -309,12 +425,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     uint8_t *staging = bars + 1024;
     float *bias_s = (float *)(staging + C::STORE_BYTES);
     for (int i = threadIdx.x; i < N && e.bias; i += blockDim.x) bias_s[i] = e.bias[i];
+    float *lnw_s = bias_s + C::MAX_BIAS, *lnb_s = lnw_s + 1024;
+    float2 *stats_s = (float2 *)(lnb_s + 1024);  // [2 tiles][4 quarters][2 LNS][32]
+    const uint32_t stats0 = smem_u32(stats_s), sbar0 = full0 + 16 * C::STAGES + 64;  // [2 tiles][4 quarters]
+    if constexpr (LNS > 0)
+        for (int i = threadIdx.x; i < N; i += blockDim.x) {
+            lnw_s[i] = e.ln_w[i];
+            lnb_s[i] = e.ln_b ? e.ln_b[i] : 0.0f;
+        }
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_rank() : 0;
-    const bool leader = rank == 0;
-    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
-    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const uint32_t pr = rank & 1u, lead = rank & ~1u;  // this CTA's half of its pair; the pair's leader
+    const bool leader = pr == 0;
+    constexpr int CL = LNS ? 2 * LNS : (PAIR ? 2 : 1);  // CTAs a cluster (1: no cluster)
+    const int unit = (int)(blockIdx.x / CL);
+    const int units = (int)(gridDim.x / CL);
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
@@ -324,6 +450,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             mbar_init(tfull0 + 8 * a, 1);
             mbar_init(tempty0 + 8 * a, (PAIR ? 2 : 1) * 4 * EPI_WG);
         }
+        if constexpr (LNS > 0)
+            for (int b = 0; b < 8; ++b) mbar_init(sbar0 + 8 * b, 2 * LNS);  // the 2 LNS parts of a quarter's rows
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -347,7 +475,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     pdl_trigger();
 
     const int m_tiles = (M + TM - 1) / TM, n_tiles = (N + BN - 1) / BN;
-    const int tiles = m_tiles * n_tiles, kblocks = (K + BK - 1) / BK;
+    const int kblocks = (K + BK - 1) / BK;
+    // Tile t's row block and column block: with LNS the cluster's pairs all
+    // take row block t, pair j column slice j.
+    const int tiles = LNS ? m_tiles : m_tiles * n_tiles;
+    auto tile_m = [&](int t) { return LNS ? t : t / n_tiles; };
+    auto tile_n = [&](int t) { return LNS ? (int)(rank >> 1) : t % n_tiles; };
 
     if (warp == 0) {
         if (lane == 0) {
@@ -355,8 +488,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             uint32_t phase = 0;
             bool ok = true;
             for (int tile = unit; tile < tiles && ok; tile += units) {
-                const int m0 = (tile / n_tiles) * TM + (int)rank * BM;
-                const int n0 = (tile % n_tiles) * BN + (int)rank * C::B_ROWS;
+                const int m0 = tile_m(tile) * TM + (int)pr * BM;
+                const int n0 = tile_n(tile) * BN + (int)pr * C::B_ROWS;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, fault)) {
                         ok = false;
@@ -367,7 +500,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                     if constexpr (PAIR) {
                         // Both CTAs' bytes complete on the leader's barrier.
                         if (leader) mbar_expect_tx(fb, 2 * C::STAGE_BYTES);
-                        const uint32_t fb0 = mapa(fb, 0);
+                        const uint32_t fb0 = mapa(fb, lead);
                         tma_load_2d_pair(sa, &ta, kb * BK, m0, fb0);
                         tma_load_2d_pair(sa + C::A_BYTES, &tw, kb * BK, n0, fb0);
                     } else {
@@ -405,12 +538,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                         if constexpr (PAIR) umma_f16_pair(d, da + off, db + off, idesc, (kb | kk) ? 1u : 0u);
                         else umma_f16(d, da + off, db + off, idesc, (kb | kk) ? 1u : 0u);
                     }
-                    if constexpr (PAIR) umma_commit_pair(empty0 + 8 * stage);
+                    if constexpr (PAIR) umma_commit_pair(empty0 + 8 * stage, lead);
                     else umma_commit(empty0 + 8 * stage);
                     if (++stage == C::STAGES) stage = 0, phase ^= 1;
                 }
                 if (!ok) break;
-                if constexpr (PAIR) umma_commit_pair(tfull0 + 8 * acc);
+                if constexpr (PAIR) umma_commit_pair(tfull0 + 8 * acc, lead);
                 else umma_commit(tfull0 + 8 * acc);
                 if (++acc == 2) acc = 0, acc_phase ^= 1;
             }
@@ -418,21 +551,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     } else if (warp >= 4) {
         const int ew = warp - 4, quad = warp & 3, part = ew >> 2;
         constexpr int COLS = BN / EPI_WG;  // this warp's columns of a tile
-        const uint32_t tempty_leader = PAIR ? mapa(tempty0, 0) : tempty0;
+        const uint32_t tempty_leader = PAIR ? mapa(tempty0, lead) : tempty0;
         // Gated tiles store 32 outputs per 64 columns: whole tiles need N % 64 == 0.
         const bool tma_out = use_tma_store && (e.kind != EPI_GATED || N % 64 == 0);
         StoreStage ss{tma_out, staging + ew * 4096, 0, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = unit; tile < tiles; tile += units) {
-            const int m0 = (tile / n_tiles) * TM + (int)rank * BM, n0 = (tile % n_tiles) * BN;
+        uint32_t it = 0;  // tiles done: the LayerNorm statistics buffer and phase
+        for (int tile = unit; tile < tiles; tile += units, ++it) {
+            const int m0 = tile_m(tile) * TM + (int)pr * BM, n0 = tile_n(tile) * BN;
             const int row = m0 + quad * 32 + lane;
             const bool row_ok = row < M;
             const int col_base = n0 + part * COLS;
             // The residual rows of this warp's columns, fetched while the
             // mainloop still runs: one memory round trip a tile.
             uint4 res[COLS / 32 * 4];
-            if (e.kind == EPI_RESIDUAL && row_ok) {
+            if constexpr (LNS > 0)
+                if (!row_ok)
+#pragma unroll
+                    for (int i = 0; i < COLS / 32 * 4; ++i) res[i] = make_uint4(0, 0, 0, 0);
+            if ((e.kind == EPI_RESIDUAL || e.kind == EPI_RESIDUAL_LN) && row_ok) {
 #pragma unroll
                 for (int c = 0; c < COLS / 32; ++c) {
                     const int col = col_base + c * 32;
@@ -446,14 +584,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + part * COLS;
             const int a_now = acc;
             ss.row0 = m0 + quad * 32;
-            epilogue_tile<T, COLS>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, [&]() {
+            auto release = [&]() {
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     if constexpr (PAIR) mbar_arrive_cluster(tempty_leader + 8 * a_now);
                     else mbar_arrive(tempty0 + 8 * a_now);
                 }
-            });
+            };
+            if constexpr (LNS > 0) {
+                const uint32_t qb = (it & 1) * 4 + quad;  // this tile's buffer, this quarter
+                LnStep L{lnw_s, lnb_s, stats0 + qb * (2 * LNS * 32 * 8), stats_s + qb * (2 * LNS * 32),
+                         sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * 2 + part};
+                if (!epilogue_ln_tile<T, COLS, LNS>(e, bias_s, tbase, row, row_ok, col_base, res, ss, &tout, L,
+                                                    abort_flag, fault, release))
+                    break;
+            } else {
+                epilogue_tile<T, COLS>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, release);
+            }
             if (++acc == 2) acc = 0, acc_phase ^= 1;
         }
         if (ss.tma && lane == 0) tma_store_wait<0>();  // every store written before the CTA leaves
@@ -482,18 +630,48 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-template <class T, int BN, int EPI_WG, bool PAIR>
+// The clusters of 2 LNS CTAs that fit the device at once (the GPCs bound
+// it, not only the SM count); 0 when none does. Asked once a kernel.
+template <class T, int LNS> int ln_clusters() {
+    static const int n = [] {
+        using C = Cfg<256, true, LNS>;
+        auto kern = gemm_tc_kernel<T, 256, 2, true, LNS>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * LNS);
+        cfg.blockDim = dim3(128 + 128 * 2);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2 * LNS;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return clusters;
+    }();
+    return n;
+}
+
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0>
 cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
-    using C = Cfg<BN, PAIR>;
-    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR>;
+    using C = Cfg<BN, PAIR, LNS>;
+    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (err != cudaSuccess) return err;
     const int TM = PAIR ? 2 * BM : BM;
-    const int tiles = ((M + TM - 1) / TM) * ((N + BN - 1) / BN);
-    const int units = PAIR ? sms / 2 : sms;
+    constexpr int CL = LNS ? 2 * LNS : (PAIR ? 2 : 1);
+    const int tiles = LNS ? (M + TM - 1) / TM : ((M + TM - 1) / TM) * ((N + BN - 1) / BN);
+    const int units = LNS ? ln_clusters<T, LNS>() : sms / CL;
+    if (units <= 0) return cudaErrorNotSupported;
     const int grid_units = tiles < units ? tiles : units;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(PAIR ? 2 * grid_units : grid_units);
+    cfg.gridDim = dim3(CL * grid_units);
     cfg.blockDim = dim3(128 + 128 * EPI_WG);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = s;
@@ -505,7 +683,7 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
     if (!pdl_enabled()) attr[0].val.programmaticStreamSerializationAllowed = 0;
     if (PAIR) {
         attr[1].id = cudaLaunchAttributeClusterDimension;
-        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.x = CL;
         attr[1].val.clusterDim.y = 1;
         attr[1].val.clusterDim.z = 1;
         cfg.numAttrs = 2;
@@ -515,6 +693,11 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
 
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
+    if (e.kind == EPI_RESIDUAL_LN) {
+        if (N == 768) return launch<T, 256, 2, true, 3>(maps, M, N, K, e, sms, fault, s);
+        if (N == 1024) return launch<T, 256, 2, true, 4>(maps, M, N, K, e, sms, fault, s);
+        return cudaErrorNotSupported;
+    }
     if (maps.pair) return launch<T, 256, 2, true>(maps, M, N, K, e, sms, fault, s);
     if (maps.bn == 256) return launch<T, 256, 2, false>(maps, M, N, K, e, sms, fault, s);
     return launch<T, 128, 2, false>(maps, M, N, K, e, sms, fault, s);
@@ -552,6 +735,15 @@ cudaError_t make_store_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+bool gemm_ln_fusable(Dt dt, int n) {
+    // 1024-column rows take clusters of 8, of which too few fit the GPCs:
+    // measured slower than the separate LayerNorm, so only 768 is fused.
+    if (n != 768) return false;
+    if (dt == Dt::F16) return (n == 768 ? ln_clusters<__half, 3>() : ln_clusters<__half, 4>()) > 0;
+    if (dt == Dt::BF16) return (n == 768 ? ln_clusters<__nv_bfloat16, 3>() : ln_clusters<__nv_bfloat16, 4>()) > 0;
+    return false;
+}
+
 cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilogue &epi, int sms, int *fault,
                     cudaStream_t s) {
     if (M == 0) return cudaSuccess;
@@ -559,6 +751,8 @@ cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilog
     if (epi.kind == EPI_ROPE && (epi.head_dim > 64 || 64 % epi.head_dim != 0)) return cudaErrorNotSupported;
     if (epi.bias && N > Cfg<256, false>::MAX_BIAS) return cudaErrorNotSupported;
     if (maps.pair && maps.bn != 256) return cudaErrorNotSupported;
+    if (epi.kind == EPI_RESIDUAL_LN && (!maps.pair || !epi.ln_w || (N != 768 && N != 1024)))
+        return cudaErrorNotSupported;
     if (dt == Dt::F16) return dispatch<__half>(maps, M, N, K, epi, sms, fault, s);
     if (dt == Dt::BF16) return dispatch<__nv_bfloat16>(maps, M, N, K, epi, sms, fault, s);
     return cudaErrorNotSupported;

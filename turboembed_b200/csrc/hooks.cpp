@@ -163,6 +163,55 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t vari
     return TURBO_OK;
 }
 
+// The fused residual + LayerNorm GEMM (EPI_RESIDUAL_LN) on N = 768 or
+// 1024 columns: y = LN(y_in + a w^T + bias) * ln_w + ln_b, operands narrowed
+// to dtype as turbo_b200_gemm_check does.
+extern "C" TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K,
+                                                      const float *a, const float *w, const float *bias,
+                                                      const float *y_in, const float *ln_w, const float *ln_b,
+                                                      float eps, float *y_out, turbo_error *err) {
+    Dt dt;
+    if (!dt_of(dtype, &dt) || dt == Dt::F32) return hook_fail(err, TURBO_E_INVALID_ENUM, "dtype", cudaSuccess);
+    Dev dv;
+    cudaError_t e = cudaSuccess;
+    void *da = to_device(dv, dt, a, (size_t)M * K, &e);
+    void *dw = e == cudaSuccess ? to_device(dv, dt, w, (size_t)N * K, &e) : nullptr;
+    void *dy = e == cudaSuccess ? to_device(dv, dt, y_in, (size_t)M * N, &e) : nullptr;
+    float *db = (float *)dv.get((size_t)N * 4), *dlw = (float *)dv.get((size_t)N * 4), *dlb = (float *)dv.get((size_t)N * 4);
+    int *fault = (int *)dv.get(4);
+    if (e == cudaSuccess && (!db || !dlw || !dlb || !fault)) e = cudaErrorMemoryAllocation;
+    if (e == cudaSuccess) e = cudaMemcpy(db, bias, (size_t)N * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(dlw, ln_w, (size_t)N * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(dlb, ln_b, (size_t)N * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "gemm_ln_check setup", e);
+    Epilogue ep;
+    ep.kind = EPI_RESIDUAL_LN;
+    ep.bias = db;
+    ep.out = dy;
+    ep.ldo = (int64_t)N;
+    ep.ln_w = dlw;
+    ep.ln_b = dlb;
+    ep.ln_eps = eps;
+    TcMaps maps;
+    maps.bn = 256;
+    maps.pair = true;
+    e = make_operand_map(dt, da, M, K, K, 128, &maps.a);
+    if (e == cudaSuccess) e = make_operand_map(dt, dw, N, K, K, 128, &maps.w);
+    if (e == cudaSuccess) e = make_store_map(dt, dy, M, N, N, &maps.out);
+    maps.has_out = true;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    if (e == cudaSuccess) e = gemm_tc(dt, maps, (int)M, (int)N, (int)K, ep, sms, fault, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "gemm_ln_check", e);
+    int f = 0;
+    cudaMemcpy(&f, fault, 4, cudaMemcpyDeviceToHost);
+    if (f) return hook_fail(err, TURBO_E_RUNTIME, "gemm_ln_check: the kernel's fault word is set", cudaSuccess);
+    widen_host(dt, dy, y_out, (size_t)M * N);
+    if (err) err->code = 0, err->message[0] = 0;
+    return TURBO_OK;
+}
+
 extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, uint32_t batch,
                                                         const int32_t *lens, const float *qkv, const uint8_t *live,
                                                         uint32_t heads, uint32_t head_dim, int32_t window,

@@ -20,6 +20,7 @@ enum EpiKind : int {
     EPI_GATED = 3,     // y[:, j] = act(acc[:, 2j] + b) * (acc[:, 2j+1] + b): weights interleaved
     EPI_ROPE = 4,      // as STORE, then Q and K columns (< rope_cols) rotated by position
     EPI_GELU_TANH = 5, // y = gelu_tanh(acc + b): the FASTEST tier's GELU
+    EPI_RESIDUAL_LN = 6,  // y = LN(y + acc + b) * ln_w + ln_b over whole rows (post-LN layers)
 };
 
 struct Epilogue {
@@ -34,6 +35,9 @@ struct Epilogue {
     const float *cos = nullptr, *sin = nullptr;
     const int32_t *tok_pos = nullptr;
     int head_dim = 0, rope_cols = 0;
+    // EPI_RESIDUAL_LN: the LayerNorm's weight and bias [N] F32 and epsilon.
+    const float *ln_w = nullptr, *ln_b = nullptr;
+    float ln_eps = 0.0f;
 };
 
 // The packed batch of one run, in device memory: each packed token's id,
@@ -55,8 +59,6 @@ struct PoolItem {
     int32_t live_only;  // 1: only live columns count; 0: every column (a range of mask-0 columns)
 };
 
-// One attention work item: `q_count` queries from query `q0` of a row whose
-// tokens start at packed token `start` and number `len`.
 // One attention work item: a query tile of a packed row. holes = 1 when a
 // key inside [0, len) is masked (its live flag is 0), else 0: then only the
 // row's end bounds the keys.
@@ -115,6 +117,9 @@ cudaError_t make_operand_map(Dt dt, const void *ptr, uint64_t rows, uint64_t col
                              uint32_t box_rows, CUtensorMap *out);
 cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilogue &epi, int sms,
                     int *fault, cudaStream_t s);
+// Whether EPI_RESIDUAL_LN runs for rows of n columns at dt: n = 768 or 1024
+// and the device fits at least one cluster of n / 128 CTAs.
+bool gemm_ln_fusable(Dt dt, int n);
 
 // Attention within each row and head, Q/K/V read from qkv [tokens, 3h],
 // context written to ctx [tokens, h]. window < 0: whole row; else query i

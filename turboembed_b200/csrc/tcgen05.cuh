@@ -185,6 +185,11 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Two floats into shared memory of a CTA of the cluster (a shared::cluster
+// address); a later release-arrive orders them before the arrival.
+__device__ __forceinline__ void st_cluster_v2(uint32_t cluster_addr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(cluster_addr), "f"(a), "f"(b) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
@@ -232,9 +237,9 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t da, uint
         "l"(da), "l"(db), "r"(idesc), "r"(acc));
 }
 // Commit of the pair's MMAs, arriving on the barrier at this offset in
-// both CTAs of the pair.
-__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
-    const uint16_t mask = 3;
+// both CTAs of the pair (cluster ranks lead and lead + 1).
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint32_t lead = 0) {
+    const uint16_t mask = (uint16_t)(3u << lead);
     asm volatile(
         "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
         "h"(mask)

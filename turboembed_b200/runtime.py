@@ -287,6 +287,22 @@ def gemm_check(dtype, variant, epi, a, w, bias=None, y_in=None, head_dim=0, pos=
     return y
 
 
+def gemm_ln_check(dtype, a, w, bias, y_in, ln_w, ln_b, eps):
+    """turbo_b200_gemm_ln_check: LN(y_in + a w^T + bias) * ln_w + ln_b on the
+    fused tcgen05 GEMM (N = 768 or 1024)."""
+    lib = library()
+    f = lib.turbo_b200_gemm_ln_check
+    f.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32] + [C.c_void_p] * 6 + [C.c_float, C.c_void_p,
+                                                                                         C.POINTER(abi.turbo_error)]
+    arrs = [np.ascontiguousarray(x, np.float32) for x in (a, w, bias, y_in, ln_w, ln_b)]
+    M, K = arrs[0].shape
+    N = arrs[1].shape[0]
+    out = np.zeros((M, N), np.float32)
+    err = abi.new_error()
+    _check(f(dtype, M, N, K, *[_ptr(x) for x in arrs], eps, _ptr(out), C.byref(err)), err, "gemm_ln_check")
+    return out
+
+
 def attention_check(dtype, variant, lens, qkv, live, heads, head_dim, window=-1):
     lib = library()
     lens = np.ascontiguousarray(lens, np.int32)
