@@ -109,27 +109,27 @@ WORKLOADS = {
                          "L~U[16,128], mean + L2, EXACT (F32)", "minilm", 0, abi.TURBO_DTYPE_F32,
                    abi.TURBO_PRECISION_EXACT, "f32", 32, 128,
                    lambda seed, n: _no_types(models.rows_bert(seed, n, 16, 128, 128)), abi.TURBO_POOLING_MEAN,
-                   abi.TURBO_NORMALIZE_L2, cpu_rows=128, ref_rows=16),
+                   abi.TURBO_NORMALIZE_L2, cpu_rows=512, ref_rows=16),
     "c2": Workload("c2", "BERT-base (BASELINE config 2): 12L h768 12 heads FFN3072 GELU, batch 256/GPU, "
                          "L~U[64,512], CLS + L2, FASTEST (F16 operands, F32 sums), varlen-packed", "bert-base", 1,
                    abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 256, 512,
                    lambda seed, n: _no_types(models.rows_bert(seed, n, 64, 512, 512)), abi.TURBO_POOLING_CLS,
-                   abi.TURBO_NORMALIZE_L2, cpu_rows=6, ref_rows=2),
+                   abi.TURBO_NORMALIZE_L2, cpu_rows=36, ref_rows=2),
     "c2x": Workload("c2x", "BERT-base (BASELINE config 2) at EXACT (F32): 12L h768, batch 256/GPU, L~U[64,512], "
                            "CLS + L2, varlen-packed", "bert-base", 1, abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_EXACT,
                     "f32", 256, 512, lambda seed, n: _no_types(models.rows_bert(seed, n, 64, 512, 512)),
-                    abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_L2, cpu_rows=6, ref_rows=2),
+                    abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_L2, cpu_rows=36, ref_rows=2),
     "c3": Workload("c3", "cross-encoder rerank (BASELINE config 3): BERT-base body + 768->1 head on CLS, "
                          "1 query x 1024 passages/GPU, [101] q [102] p [102], BF16 (MODEL)", "bert-base", 2,
                    abi.TURBO_DTYPE_BF16, abi.TURBO_PRECISION_MODEL, "bf16", 1024, 512,
                    lambda seed, n: models.rows_rerank(seed, n), abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_NONE,
-                   task=abi.TURBO_TASK_RERANK, head=True, cpu_rows=6, ref_rows=2),
+                   task=abi.TURBO_TASK_RERANK, head=True, cpu_rows=36, ref_rows=2),
     "c4": Workload("c4", "ModernBERT-base (BASELINE config 4): 22L h768 GeGLU 1152, global every 3rd layer, "
                          "local window 128, batch 8/GPU, L~U[1024,8192] unpadded, mean + L2, FASTEST (F16)",
                    "modernbert-base", 3, abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 8, 8192,
                    lambda seed, n: _no_types(models.rows_long(seed, n, 1024, 8192, 8192, 100, 50367)),
                    abi.TURBO_POOLING_MEAN, abi.TURBO_NORMALIZE_L2,
-                   cpu_rows=lambda seed: _no_types(models.rows_long(seed, 1, 1024, 1024, 1024, 100, 50367)),
+                   cpu_rows=lambda seed: _no_types(models.rows_long(seed, 4, 1024, 1024, 1024, 100, 50367)),
                    ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 256, 256, 256, 100, 50367))),
     "c5": Workload("c5", "XLM-R-large / bge-m3 shape (BASELINE config 5): 24L h1024 16 heads FFN4096, 16 documents"
                          "/GPU (128 over 8 GPUs) of 8192 tokens, range pooling U[32,256] + L2, BF16 (MODEL)",
@@ -137,7 +137,7 @@ WORKLOADS = {
                    lambda seed, n: _no_types(models.rows_long(seed, n, 8192, 8192, 8192, 5, 250001)),
                    abi.TURBO_POOLING_MEAN, abi.TURBO_NORMALIZE_L2,
                    ranges=lambda seed, lens: models.ranges_tiling(seed, lens, 32, 256),
-                   cpu_rows=lambda seed: _no_types(models.rows_long(seed, 1, 512, 512, 512, 5, 250001)),
+                   cpu_rows=lambda seed: _no_types(models.rows_long(seed, 2, 1024, 1024, 1024, 5, 250001)),
                    ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 128, 128, 128, 5, 250001))),
 }
 
