@@ -39,20 +39,22 @@ using namespace tc;
 // LNS > 0: the fused residual + LayerNorm epilogue over rows of N = 256 LNS
 // columns, computed by a cluster of LNS CTA pairs (one 256-column slice a
 // pair) that exchange row statistics through distributed shared memory.
-template <int BN, bool PAIR, int LNS = 0> struct Cfg {
+template <int BN, bool PAIR, int LNS = 0, int EPI_WG = 2> struct Cfg {
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // W rows this CTA loads a stage
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : 5;
+    // 16 epilogue warps (with the fused LayerNorm) take the room of two stages.
+    static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : (LNS && EPI_WG > 2 ? 3 : 5);
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BAR_BYTES = 256;
     static constexpr int MAX_BIAS = LNS ? 1024 : 4096;  // the bias vector, staged in shared memory once per CTA
     // Output staging for TMA stores: two [32 x 32] 16-bit tiles per epilogue warp.
-    static constexpr int STORE_BYTES = 8 * 2 * 2048;
+    static constexpr int STORE_BYTES = 4 * EPI_WG * 2 * 2048;
     // LayerNorm weight and bias [N], and the row statistics two tiles deep:
-    // [2][4 row quarters][2 LNS parts][32 rows] (mean, M2).
-    static constexpr int LN_BYTES = LNS ? 2 * 1024 * 4 + 2 * 4 * 2 * LNS * 32 * 8 : 0;
+    // [2][4 row quarters][EPI_WG LNS parts][32 rows] (mean, M2).
+    static constexpr int PARTS = EPI_WG * LNS;
+    static constexpr int LN_BYTES = LNS ? 2 * 1024 * 4 + 2 * 4 * PARTS * 32 * 8 : 0;
     // ring | barriers (padded to 1 KB) | store staging | bias | LayerNorm
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + STORE_BYTES + MAX_BIAS * 4 + LN_BYTES + 1024;
 };
@@ -297,8 +299,8 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
 // rows and COLS columns of a 256-column slice. v = acc + bias + residual;
 // the warp's part of each row's statistics (mean and M2 over its COLS
 // columns, one pass over TMEM) goes to every CTA of the cluster holding
-// the same rows (slot `slot` of their statistics buffers, then an arrival
-// on their barrier for this row quarter); once all 2 LNS parts are in, the
+// the same rows (slot `slot` of their statistics buffers, then each lane's
+// arrival on their barrier for this row quarter); once all 2 LNS parts are in, the
 // row's mean and variance follow by Chan's pairwise formula, and a second
 // pass writes (v - mean) / sqrt(var + eps) * ln_w + ln_b. Returns false when
 // a wait gave up.
@@ -312,7 +314,7 @@ struct LnStep {
     int slot;                // 2 * slice + part
 };
 
-template <class T, int COLS, int LNS, class Release>
+template <class T, int COLS, int LNS, int PARTS, class Release>
 __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
                                                  bool row_ok, int col_base, const uint4 *res, StoreStage &ss,
                                                  const CUtensorMap *out_map, const LnStep &L, volatile int *abort_flag,
@@ -356,32 +358,31 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
     }
     const float mean_p = k + s1 / (float)COLS;
     const float m2 = fmaxf(s2 - s1 * (s1 / (float)COLS), 0.0f);
-    // This part to the LNS CTAs holding these rows, then one arrival each.
+    // This row's part to the LNS CTAs holding the row, each store followed
+    // by this lane's own release-arrival there (which orders it).
     const uint32_t mine = L.stats + (uint32_t)((L.slot * 32 + lane) * 8);
 #pragma unroll
-    for (int j = 0; j < LNS; ++j) st_cluster_v2(mapa(mine, L.half + 2 * j), mean_p, m2);
-    asm volatile("fence.acq_rel.cluster;" ::: "memory");
-    __syncwarp();
-    if (lane == 0)
-#pragma unroll
-        for (int j = 0; j < LNS; ++j) mbar_arrive_cluster(mapa(L.bar, L.half + 2 * j));
+    for (int j = 0; j < LNS; ++j) {
+        st_cluster_v2(mapa(mine, L.half + 2 * j), mean_p, m2);
+        mbar_arrive_cluster(mapa(L.bar, L.half + 2 * j));
+    }
     if (!mbar_wait_cluster(L.bar, L.phase, abort_flag, fault)) {
         release();
         return false;
     }
-    // Chan: mean = the parts' mean (equal counts), M2 = sum M2_p + COLS sum (mean_p - mean)^2.
+    // Chan: mean = the PARTS parts' mean (equal counts), M2 = sum M2_p + COLS sum (mean_p - mean)^2.
     float ms = 0.0f;
 #pragma unroll
-    for (int p = 0; p < 2 * LNS; ++p) ms += L.stats_p[p * 32 + lane].x;
-    const float mean = ms / (float)(2 * LNS);
+    for (int p = 0; p < PARTS; ++p) ms += L.stats_p[p * 32 + lane].x;
+    const float mean = ms / (float)PARTS;
     float M2 = 0.0f;
 #pragma unroll
-    for (int p = 0; p < 2 * LNS; ++p) {
+    for (int p = 0; p < PARTS; ++p) {
         const float2 q = L.stats_p[p * 32 + lane];
         const float d = q.x - mean;
         M2 += q.y + (float)COLS * d * d;
     }
-    const float inv = 1.0f / sqrtf(M2 / (float)(2 * LNS * COLS) + e.ln_eps);
+    const float inv = 1.0f / sqrtf(M2 / (float)(PARTS * COLS) + e.ln_eps);
     // Pass 2: normalise and store.
 #pragma unroll 1
     for (int c = 0; c < COLS; c += 32) {
@@ -413,7 +414,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                const __grid_constant__ CUtensorMap tout, int use_tma_store, int M, int N, int K, Epilogue e,
                int *fault) {
     static_assert(LNS == 0 || (PAIR && BN == 256), "the fused LayerNorm runs on 256-column CTA pairs");
-    using C = Cfg<BN, PAIR, LNS>;
+    using C = Cfg<BN, PAIR, LNS, EPI_WG>;
     constexpr int TM = PAIR ? 2 * BM : BM;  // rows a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -426,7 +427,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     float *bias_s = (float *)(staging + C::STORE_BYTES);
     for (int i = threadIdx.x; i < N && e.bias; i += blockDim.x) bias_s[i] = e.bias[i];
     float *lnw_s = bias_s + C::MAX_BIAS, *lnb_s = lnw_s + 1024;
-    float2 *stats_s = (float2 *)(lnb_s + 1024);  // [2 tiles][4 quarters][2 LNS][32]
+    float2 *stats_s = (float2 *)(lnb_s + 1024);  // [2 tiles][4 quarters][PARTS][32]
     const uint32_t stats0 = smem_u32(stats_s), sbar0 = full0 + 16 * C::STAGES + 64;  // [2 tiles][4 quarters]
     if constexpr (LNS > 0)
         for (int i = threadIdx.x; i < N; i += blockDim.x) {
@@ -451,7 +452,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             mbar_init(tempty0 + 8 * a, (PAIR ? 2 : 1) * 4 * EPI_WG);
         }
         if constexpr (LNS > 0)
-            for (int b = 0; b < 8; ++b) mbar_init(sbar0 + 8 * b, 2 * LNS);  // the 2 LNS parts of a quarter's rows
+            for (int b = 0; b < 8; ++b) mbar_init(sbar0 + 8 * b, C::PARTS * 32);  // each lane of every part
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -594,10 +595,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             };
             if constexpr (LNS > 0) {
                 const uint32_t qb = (it & 1) * 4 + quad;  // this tile's buffer, this quarter
-                LnStep L{lnw_s, lnb_s, stats0 + qb * (2 * LNS * 32 * 8), stats_s + qb * (2 * LNS * 32),
-                         sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * 2 + part};
-                if (!epilogue_ln_tile<T, COLS, LNS>(e, bias_s, tbase, row, row_ok, col_base, res, ss, &tout, L,
-                                                    abort_flag, fault, release))
+                LnStep L{lnw_s, lnb_s, stats0 + qb * (C::PARTS * 32 * 8), stats_s + qb * (C::PARTS * 32),
+                         sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * EPI_WG + part};
+                if (!epilogue_ln_tile<T, COLS, LNS, C::PARTS>(e, bias_s, tbase, row, row_ok, col_base, res, ss,
+                                                              &tout, L, abort_flag, fault, release))
                     break;
             } else {
                 epilogue_tile<T, COLS>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, release);
@@ -632,14 +633,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // The clusters of 2 LNS CTAs that fit the device at once (the GPCs bound
 // it, not only the SM count); 0 when none does. Asked once a kernel.
+// The fused LayerNorm's epilogue warpgroups: 2 (8 warps) keeps the 5-stage
+// ring; 4 measured slower (3 stages starve FFN-out's K = 3072 mainloop).
+constexpr int LN_EPI_WG = 2;
+
 template <class T, int LNS> int ln_clusters() {
     static const int n = [] {
-        using C = Cfg<256, true, LNS>;
-        auto kern = gemm_tc_kernel<T, 256, 2, true, LNS>;
+        using C = Cfg<256, true, LNS, LN_EPI_WG>;
+        auto kern = gemm_tc_kernel<T, 256, LN_EPI_WG, true, LNS>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return 0;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * LNS);
-        cfg.blockDim = dim3(128 + 128 * 2);
+        cfg.blockDim = dim3(128 + 128 * LN_EPI_WG);
         cfg.dynamicSmemBytes = C::SMEM;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -660,7 +665,7 @@ template <class T, int LNS> int ln_clusters() {
 
 template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0>
 cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
-    using C = Cfg<BN, PAIR, LNS>;
+    using C = Cfg<BN, PAIR, LNS, EPI_WG>;
     auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (err != cudaSuccess) return err;
@@ -694,8 +699,8 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     if (e.kind == EPI_RESIDUAL_LN) {
-        if (N == 768) return launch<T, 256, 2, true, 3>(maps, M, N, K, e, sms, fault, s);
-        if (N == 1024) return launch<T, 256, 2, true, 4>(maps, M, N, K, e, sms, fault, s);
+        if (N == 768) return launch<T, 256, LN_EPI_WG, true, 3>(maps, M, N, K, e, sms, fault, s);
+        if (N == 1024) return launch<T, 256, LN_EPI_WG, true, 4>(maps, M, N, K, e, sms, fault, s);
         return cudaErrorNotSupported;
     }
     if (maps.pair) return launch<T, 256, 2, true>(maps, M, N, K, e, sms, fault, s);
