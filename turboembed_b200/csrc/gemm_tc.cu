@@ -135,6 +135,39 @@ __device__ __forceinline__ void stage_store32(const float *v, int col, StoreStag
     ++ss.nstore;
 }
 
+// Two neighbouring 32-column tiles at once: both staging buffers, one fence
+// and one bulk group. Every earlier store has finished reading the buffers
+// first (they were issued a whole 64-column step before).
+template <class T>
+__device__ __forceinline__ void stage_store64(const float *v0, const float *v1, int col, StoreStage &ss,
+                                              const CUtensorMap *out_map) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) tma_store_wait_read<0>();
+    __syncwarp();
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        const float *v = b ? v1 : v0;
+        uint8_t *buf = ss.buf + b * 2048;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint4 u;
+            u.x = pack2<T>(v[8 * q + 0], v[8 * q + 1]);
+            u.y = pack2<T>(v[8 * q + 2], v[8 * q + 3]);
+            u.z = pack2<T>(v[8 * q + 4], v[8 * q + 5]);
+            u.w = pack2<T>(v[8 * q + 6], v[8 * q + 7]);
+            *reinterpret_cast<uint4 *>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = u;
+        }
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(out_map, smem_u32(ss.buf), col, ss.row0);
+        tma_store_2d(out_map, smem_u32(ss.buf + 2048), col + 32, ss.row0);
+        tma_store_commit();
+    }
+    ss.nstore += 2;
+}
+
 // The RoPE epilogue (QKV of rotary models): 64 columns at a time, whole
 // heads of width HD; within each head of the first rope_cols columns,
 // (x1, x2) = (v[k], v[k + HD/2]) -> (x1 cos - x2 sin, x2 cos + x1 sin) with
@@ -235,15 +268,16 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
             stage_store32<T>(o, col / 2, ss, out_map);
             continue;
         }
+        // The math in place on the loaded registers, as F32.
+        float(*vv)[32] = reinterpret_cast<float(*)[32]>(raw);
+        bool staged[2] = {false, false};  // warp-uniform: which halves go out through TMA
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int c = c2 + hh * 32;
             const int col = col_base + c;
             if (c >= COLS || col >= N) continue;
             if (!row_ok && (e.kind == EPI_GATED || !ss.tma)) continue;
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[hh][i]);
+            float *v = vv[hh];
             if (e.bias) {
                 const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col);
 #pragma unroll
@@ -290,8 +324,11 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                 store_n<T, 32>(y, v);
                 continue;
             }
-            stage_store32<T>(v, col, ss, out_map);
+            staged[hh] = true;
         }
+        if (staged[0] && staged[1]) stage_store64<T>(vv[0], vv[1], col_base + c2, ss, out_map);
+        else if (staged[0]) stage_store32<T>(vv[0], col_base + c2, ss, out_map);
+        else if (staged[1]) stage_store32<T>(vv[1], col_base + c2 + 32, ss, out_map);
     }
 }
 
@@ -383,17 +420,29 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
         M2 += q.y + (float)COLS * d * d;
     }
     const float inv = 1.0f / sqrtf(M2 / (float)(PARTS * COLS) + e.ln_eps);
-    // Pass 2: normalise and store.
+    // Pass 2: normalise and store, 64 columns a step.
+    static_assert(COLS % 64 == 0, "the LayerNorm epilogue stores 64 columns a step");
 #pragma unroll 1
-    for (int c = 0; c < COLS; c += 32) {
+    for (int c = 0; c < COLS; c += 64) {
+        uint32_t raw[2][32];
         __syncwarp();
-        tmem_ld32(tbase + c, v);
-        if (c + 32 >= COLS) release();
-        const int col = col_base + c;
+        tmem_ld32_async(tbase + c, raw[0]);
+        tmem_ld32_async(tbase + c + 32, raw[1]);
+        tmem_wait_ld();
+        if (c + 64 >= COLS) release();
+        float w[2][32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = (v[i] - mean) * inv * L.w_s[col + i] + L.b_s[col + i];
-        if (ss.tma) stage_store32<T>(v, col, ss, out_map);
-        else if (row_ok) store_n<T, 32>((T *)e.out + (int64_t)row * e.ldo + col, v);
+        for (int hh = 0; hh < 2; ++hh) {
+            const int col = col_base + c + 32 * hh;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                w[hh][i] = (__uint_as_float(raw[hh][i]) - mean) * inv * L.w_s[col + i] + L.b_s[col + i];
+        }
+        if (ss.tma) stage_store64<T>(w[0], w[1], col_base + c, ss, out_map);
+        else if (row_ok) {
+            store_n<T, 32>((T *)e.out + (int64_t)row * e.ldo + col_base + c, w[0]);
+            store_n<T, 32>((T *)e.out + (int64_t)row * e.ldo + col_base + c + 32, w[1]);
+        }
     }
     return true;
 }
