@@ -77,6 +77,14 @@ TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M, uint32_t 
                                            const float *w, const float *bias, const float *y_in, const float *ln_w,
                                            const float *ln_b, float eps, float *y_out, turbo_error *err);
 
+/* Failure detection without a GPU fault: a kernel waits on an mbarrier
+ * nothing completes with the library's bounded wait, limited to limit_ns;
+ * it gives up, sets the fault word (fault_out = 1) and returns; a second
+ * launch, whose wait completes, reports completed_out = 1: the context
+ * stays usable. */
+TB_EXPORT int32_t turbo_b200_wait_check(uint64_t limit_ns, int32_t *fault_out, int32_t *completed_out,
+                                        turbo_error *err);
+
 /* Attention over `batch` rows packed one after another (row b has lens[b]
  * tokens), qkv [tokens, 3 * hidden] host F32 narrowed to dtype, live [tokens]
  * the mask entries, window < 0 for whole rows. variant 0 is the F16/BF16

@@ -255,3 +255,20 @@ def test_simt_attention_takes_other_head_widths(dtype):
     want = ref_attention(qkv, lens, live, heads, d, -1)
     # Output rounding to BF16 (8 significant bits) or F16 (11) bounds the error relative to its scale.
     assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
+
+
+def test_a_device_wait_that_nothing_completes_gives_up():
+    # The failure path of every pipeline wait, without a GPU fault: a wait
+    # on an mbarrier nothing arrives at ends after its limit (50 ms here,
+    # 2 s in the library's kernels) with the fault word set, and the next
+    # launch on the same context runs and completes its wait.
+    import ctypes as C
+    import time
+    lib = runtime.library()
+    f = lib.turbo_b200_wait_check
+    f.argtypes = [C.c_uint64, C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(abi.turbo_error)]
+    fault, done, err = C.c_int32(), C.c_int32(), abi.new_error()
+    t0 = time.perf_counter()
+    assert f(50_000_000, C.byref(fault), C.byref(done), C.byref(err)) == 0, err.message
+    assert fault.value == 1 and done.value == 1
+    assert time.perf_counter() - t0 < 5.0

@@ -122,6 +122,26 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+// The erf form of GELU for F16/BF16 outputs, from Abramowitz and Stegun's
+// rational approximation 7.1.26 (Handbook of Mathematical Functions, 1964):
+// erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^(-z^2),
+// t = 1 / (1 + p z), z >= 0, absolute error at most 1.5e-7, with the
+// reciprocal and the exponential on the MUFU (rcp.approx, ex2.approx) and
+// the rest on the FMA pipe. The F32 (EXACT) path keeps erff.
+__device__ __forceinline__ float gelu_erf_fast(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    float t, e;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.0f)));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * z * z));
+    float p = fmaf(1.061405429f, t, -1.453152027f);
+    p = fmaf(p, t, 1.421413741f);
+    p = fmaf(p, t, -0.284496736f);
+    p = fmaf(p, t, 0.254829592f);
+    const float erf_abs = fmaf(-p * t, e, 1.0f);
+    const float hx = 0.5f * x;
+    return fmaf(hx, copysignf(erf_abs, x), hx);
+}
+
 // GELU in its tanh form, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
 // on the hardware tanh: what the reference's FASTEST tier computes by
 // default (core/cuda/kernels.cu:162, backend.cpp:1575-1582). Within about

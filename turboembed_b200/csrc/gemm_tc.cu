@@ -263,7 +263,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                         g += bias_s[col + hh * 32 + 2 * i];
                         u += bias_s[col + hh * 32 + 2 * i + 1];
                     }
-                    o[hh * 16 + i] = (e.act == 2 ? silu(g) : gelu_erf(g)) * u;
+                    o[hh * 16 + i] = (e.act == 2 ? silu(g) : gelu_erf_fast(g)) * u;
                 }
             stage_store32<T>(o, col / 2, ss, out_map);
             continue;
@@ -294,7 +294,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const float g = v[2 * i];
-                    o[i] = (e.act == 2 ? silu(g) : gelu_erf(g)) * v[2 * i + 1];
+                    o[i] = (e.act == 2 ? silu(g) : gelu_erf_fast(g)) * v[2 * i + 1];
                 }
                 store_n<T, 16>((T *)e.out + (int64_t)row * e.ldo + col / 2, o);
                 continue;
@@ -302,7 +302,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
             T *y = (T *)e.out + (int64_t)row * e.ldo + col;
             if (e.kind == EPI_GELU) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+                for (int i = 0; i < 32; ++i) v[i] = gelu_erf_fast(v[i]);
             } else if (e.kind == EPI_GELU_TANH) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);

@@ -7,6 +7,7 @@
 
 #include "../../include/turbo_b200.h"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 using namespace tb;
 
@@ -208,6 +209,53 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M
     cudaMemcpy(&f, fault, 4, cudaMemcpyDeviceToHost);
     if (f) return hook_fail(err, TURBO_E_RUNTIME, "gemm_ln_check: the kernel's fault word is set", cudaSuccess);
     widen_host(dt, dy, y_out, (size_t)M * N);
+    if (err) err->code = 0, err->message[0] = 0;
+    return TURBO_OK;
+}
+
+namespace {
+// One mbarrier that nothing arrives at (arrive = 0) or that this thread
+// arrives at first (arrive = 1), waited on with the tensor-core kernels'
+// bounded wait: the first gives up after limit_ns, sets the fault word and
+// returns, as every pipeline wait of the library does.
+__global__ void bounded_wait_kernel(int *fault, unsigned long long limit_ns, int arrive, int *waited) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x != 0) return;
+    abort_flag = 0;
+    const uint32_t b = tc::smem_u32(&bar);
+    tc::mbar_init(b, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (arrive) tc::mbar_arrive(b);
+    *waited = tc::mbar_wait(b, 0, &abort_flag, fault, limit_ns) ? 1 : 0;
+}
+}  // namespace
+
+// Failure detection without a GPU fault: a device wait that nothing
+// completes gives up after limit_ns (the library's waits use 2 s), writes
+// the fault word and the kernel returns; a second launch whose wait does
+// complete shows the context still works. fault_out receives the fault
+// word after the first launch, completed_out whether the second one's wait
+// completed.
+extern "C" TB_EXPORT int32_t turbo_b200_wait_check(uint64_t limit_ns, int32_t *fault_out, int32_t *completed_out,
+                                                   turbo_error *err) {
+    Dev dv;
+    int *fault = (int *)dv.get(4), *waited = (int *)dv.get(4);
+    if (!fault || !waited) return hook_fail(err, TURBO_E_OUT_OF_MEMORY, "wait_check", cudaErrorMemoryAllocation);
+    bounded_wait_kernel<<<1, 32>>>(fault, (unsigned long long)limit_ns, 0, waited);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "wait_check", e);
+    int f = 0, w = 0;
+    cudaMemcpy(&f, fault, 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(&w, waited, 4, cudaMemcpyDeviceToHost);
+    *fault_out = f && !w ? 1 : 0;
+    cudaMemset(fault, 0, 4);
+    bounded_wait_kernel<<<1, 32>>>(fault, (unsigned long long)limit_ns, 1, waited);
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "wait_check", e);
+    cudaMemcpy(&f, fault, 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(&w, waited, 4, cudaMemcpyDeviceToHost);
+    *completed_out = w && !f ? 1 : 0;
     if (err) err->code = 0, err->message[0] = 0;
     return TURBO_OK;
 }

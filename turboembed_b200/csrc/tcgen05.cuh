@@ -40,14 +40,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 // Wait for the phase of `parity` to complete, at most WAIT_NS, or until
 // another role has given up. Returns false when the kernel must stop.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *fault) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *fault,
+                                          uint64_t limit_ns = WAIT_NS) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try(bar, parity)) return true;
         if ((i & 255) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer() - t0 > WAIT_NS) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort_flag = 1;
                 atomicExch(fault, 1);
                 return false;
