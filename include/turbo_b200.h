@@ -56,8 +56,9 @@ TB_EXPORT uint64_t turbo_b200_kernel_launches(void);
 /* One GEMM y = epi(a w^T + bias) on the device, operands given as host F32
  * and narrowed to dtype (TURBO_DTYPE_F16 / BF16 / F32) first, run through
  * `variant` 0 (the tcgen05 kernel as the backend runs it: CTA pairs when N
- * is a multiple of 256), 1 (the FFMA kernel) or 2 (the tcgen05 kernel on
- * single CTAs), the result
+ * is a multiple of 256), 1 (the FFMA kernel), 2 (the tcgen05 kernel on
+ * single CTAs) or 3 (F32 only: the kind::tf32 kernel with the three-product
+ * split, the EXACT tier's), the result
  * widened back into y_out. epi is 0 store, 1 GELU, 2 residual (y_in holds
  * y's starting values), 3 gated (interleaved gate/up columns; y is
  * [M, N/2]), 4 RoPE on the columns below 2 * (N / 3) with head_dim, pos [M],

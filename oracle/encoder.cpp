@@ -151,6 +151,8 @@ struct Linear {
 void linear(const Linear &L, const float *x, size_t ldx, size_t tokens, const float *bias, float *y,
             size_t ldy, Epi epi, unsigned threads) {
     const uint32_t n = L.n, k = L.k;
+    // Register blocks of TB tokens x OB outputs, each accumulator one FMA
+    // chain over i in order (the CPU path's arithmetic, kernels/mod.rs:1-19).
     constexpr int TB = 4, OB = 32;
     parallel((tokens + TB - 1) / TB, threads, [&](size_t lo, size_t hi) {
         for (size_t tb = lo; tb < hi; ++tb) {
@@ -159,13 +161,25 @@ void linear(const Linear &L, const float *x, size_t ldx, size_t tokens, const fl
                 uint32_t on = std::min<uint32_t>(OB, n - o0);
                 float acc[TB][OB];
                 std::memset(acc, 0, sizeof(acc));
-                for (uint32_t i = 0; i < k; ++i) {
-                    const float *w = &L.wt[(size_t)i * n + o0];
-                    float wv[OB];
-                    for (int j = 0; j < OB; ++j) wv[j] = j < (int)on ? w[j] : 0.0f;
-                    for (size_t r = 0; r < tn; ++r) {
-                        float a = x[(t0 + r) * ldx + i];
-                        for (int j = 0; j < OB; ++j) acc[r][j] = std::fma(a, wv[j], acc[r][j]);
+                if (on == OB && tn == TB) {
+                    const float *xr[TB];
+                    for (int r = 0; r < TB; ++r) xr[r] = x + (t0 + r) * ldx;
+                    for (uint32_t i = 0; i < k; ++i) {
+                        const float *w = &L.wt[(size_t)i * n + o0];
+                        for (int r = 0; r < TB; ++r) {
+                            const float a = xr[r][i];
+                            for (int j = 0; j < OB; ++j) acc[r][j] = std::fma(a, w[j], acc[r][j]);
+                        }
+                    }
+                } else {
+                    for (uint32_t i = 0; i < k; ++i) {
+                        const float *w = &L.wt[(size_t)i * n + o0];
+                        float wv[OB];
+                        for (int j = 0; j < OB; ++j) wv[j] = j < (int)on ? w[j] : 0.0f;
+                        for (size_t r = 0; r < tn; ++r) {
+                            float a = x[(t0 + r) * ldx + i];
+                            for (int j = 0; j < OB; ++j) acc[r][j] = std::fma(a, wv[j], acc[r][j]);
+                        }
                     }
                 }
                 for (size_t r = 0; r < tn; ++r) {

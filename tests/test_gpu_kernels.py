@@ -142,6 +142,25 @@ def test_ffma_gemm_f32_is_one_chain_over_k(epi):
     assert np.array_equal(got, runtime.gemm_check(F32, 1, epi, a, w, bias, y_in))
 
 
+@pytest.mark.parametrize("shape", [(150, 256, 200), (2000, 768, 3072), (77, 2304, 768), (513, 1536, 384)])
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+def test_tf32x3_gemm_has_f32_accuracy(shape, epi):
+    # The EXACT tier's tensor-core GEMM: hi/lo TF32 split, three products,
+    # F32 sums. Against numpy in F64, to the same bound as the FFMA kernel
+    # (one F32 chain over k).
+    M, N, K = shape
+    rng = np.random.default_rng(M + N + K + epi)
+    a = rng.standard_normal((M, K), np.float32)
+    w = rng.standard_normal((N, K), np.float32) * np.float32(1 / np.sqrt(K))
+    bias = rng.standard_normal(N).astype(np.float32)
+    y_in = rng.standard_normal((M, N // 2 if epi == 3 else N)).astype(np.float32) if epi == 2 else None
+    got = runtime.gemm_check(F32, 3, epi, a, w, bias, y_in)
+    want = ref_gemm(F32, epi, a, w, bias, y_in)
+    assert np.abs(got - want).max() < 1e-4 * max(1.0, np.abs(want).max())
+    simt = runtime.gemm_check(F32, 1, epi, a, w, bias, y_in)
+    assert np.abs(got - simt).max() < 1e-4 * max(1.0, np.abs(want).max())
+
+
 def ref_attention(qkv, lens, live, heads, d, window):
     h = heads * d
     out = np.zeros((qkv.shape[0], h))

@@ -213,6 +213,7 @@ struct Session {
     // (EPI_RESIDUAL_LN), unless the environment sets TB_LNFUSE=0 (an A/B
     // switch, read at session open).
     bool fuse_ln = false;
+    bool exact_tf32 = false;  // F32 sessions: GEMMs on kind::tf32 x3 (else FFMA)
     uint64_t h2d_bytes = 0;
     std::vector<int32_t> row_start, row_len;
     // Device time of the last run (events on the context's stream), and,
@@ -640,6 +641,10 @@ int32_t tb_model_load(void *ctx, const turbo_backend_model *d, void **out, turbo
         if (e == cudaSuccess)
             e = upload(m.get(), d->rope_table, (size_t)4 * d->max_positions * d->rope_pairs, &m->rope);
     }
+    // F32 TMA maps of the EXACT set's weights, for the kind::tf32 GEMM.
+    for (LayerWeights &L : ws.layers)
+        for (Linear *x : {&L.qkv, &L.out, &L.ffn_in, &L.ffn_out})
+            if (e == cudaSuccess && x->w) e = make_operand_map_f32((const float *)x->w, x->n, x->k, x->k, &x->map);
     if (e != cudaSuccess) return cuda_fail(err, e, "model_load");
     ws.ready = true;
     *out = m.release();
@@ -822,6 +827,17 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         if (e == cudaSuccess) e = make_store_map(dt, s->x, rows, h, h, &s->out_x);
         if (e == cudaSuccess) e = make_store_map(dt, s->qkv, rows, 3 * h, 3 * h, &s->out_qkv);
         if (e == cudaSuccess) e = make_store_map(dt, s->ffn, rows, I, I, &s->out_ffn);
+    }
+    if (e == cudaSuccess && dt == Dt::F32) {
+        e = make_operand_map_f32((const float *)s->x, rows, h, h, &s->map_x);
+        if (e == cudaSuccess) e = make_operand_map_f32((const float *)s->ctxb, rows, h, h, &s->map_ctx);
+        if (e == cudaSuccess) e = make_operand_map_f32((const float *)s->ffn, rows, I, I, &s->map_ffn);
+        if (e == cudaSuccess && m->modern) e = make_operand_map_f32((const float *)s->xn, rows, h, h, &s->map_xn);
+        // The EXACT tier's GEMMs on tcgen05 kind::tf32 with the three-product
+        // split, unless the environment sets TB_EXACT_TF32=0 (then the FFMA
+        // kernel, one F32 chain over k per output).
+        const char *v = getenv("TB_EXACT_TF32");
+        s->exact_tf32 = !(v && v[0] == '0');
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return cuda_fail(err, e, "session_open");
@@ -1024,14 +1040,15 @@ template <class F> cudaError_t timed(Session *s, int kind, double flops, F launc
 cudaError_t linear_launch(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi,
                           int M, const CUtensorMap *out_map) {
     if (s->dt == Dt::F32) {
-        if (epi.kind == EPI_ROPE) {
-            Epilogue e2 = epi;
-            e2.kind = EPI_STORE;
-            cudaError_t e = gemm_simt(Dt::F32, a, L.k, L.w, M, L.n, L.k, e2, s->ctx->stream);
-            if (e != cudaSuccess) return e;
-            return rope_qk(Dt::F32, epi.out, epi.tok_pos, epi.cos, epi.sin, M, s->m->hidden, epi.head_dim, s->ctx->stream);
-        }
-        return gemm_simt(Dt::F32, a, L.k, L.w, M, L.n, L.k, epi, s->ctx->stream);
+        Epilogue e2 = epi;
+        if (epi.kind == EPI_ROPE) e2.kind = EPI_STORE;
+        cudaError_t e;
+        if (s->exact_tf32 && gemm_tf32_takes(L.n, L.k, e2))
+            e = gemm_tf32(*amap, L.map, M, L.n, L.k, e2, s->ctx->sms, s->ctx->fault_dev, s->ctx->stream);
+        else
+            e = gemm_simt(Dt::F32, a, L.k, L.w, M, L.n, L.k, e2, s->ctx->stream);
+        if (e != cudaSuccess || epi.kind != EPI_ROPE) return e;
+        return rope_qk(Dt::F32, epi.out, epi.tok_pos, epi.cos, epi.sin, M, s->m->hidden, epi.head_dim, s->ctx->stream);
     }
     TcMaps maps;
     maps.a = *amap;

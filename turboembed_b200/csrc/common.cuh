@@ -122,24 +122,66 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
-// The erf form of GELU for F16/BF16 outputs, from Abramowitz and Stegun's
-// rational approximation 7.1.26 (Handbook of Mathematical Functions, 1964):
-// erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^(-z^2),
-// t = 1 / (1 + p z), z >= 0, absolute error at most 1.5e-7, with the
-// reciprocal and the exponential on the MUFU (rcp.approx, ex2.approx) and
-// the rest on the FMA pipe. The F32 (EXACT) path keeps erff.
-__device__ __forceinline__ float gelu_erf_fast(float x) {
-    const float z = fabsf(x) * 0.70710678118654752f;
-    float t, e;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.0f)));
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * z * z));
-    float p = fmaf(1.061405429f, t, -1.453152027f);
-    p = fmaf(p, t, 1.421413741f);
-    p = fmaf(p, t, -0.284496736f);
-    p = fmaf(p, t, 0.254829592f);
-    const float erf_abs = fmaf(-p * t, e, 1.0f);
-    const float hx = 0.5f * x;
-    return fmaf(hx, copysignf(erf_abs, x), hx);
+// Packed pairs of F32 (Blackwell's two-wide FP32 operations): each half is
+// rounded exactly as the scalar operation would round it.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// The erf form of GELU for F16/BF16 outputs, for a pair of values, from
+// Abramowitz and Stegun's rational approximation 7.1.26 (Handbook of
+// Mathematical Functions, 1964): erf(z) = 1 - (a1 t + ... + a5 t^5) e^(-z^2),
+// t = 1 / (1 + p z), z >= 0, absolute error at most 1.5e-7. Packed F32x2
+// arithmetic on the FMA pipe; only the exponential runs on the MUFU
+// (ex2.approx). 1 / d for d = 1 + p z in [1, 2.5] comes from the classic
+// exponent-bit guess (0x7EF311C7 minus d's bits, within 12%) and three
+// Newton steps r <- r (2 - d r), each squaring the error (about 4e-8 left).
+// z is clamped at 4.5, where erf is 1 to F32 precision. The F32 (EXACT)
+// path keeps erff.
+__device__ __forceinline__ void gelu_erf_fast2(float &x0, float &x1) {
+    const float z0 = fminf(fabsf(x0) * 0.70710678118654752f, 4.5f), z1 = fminf(fabsf(x1) * 0.70710678118654752f, 4.5f);
+    const uint64_t z = pk2(z0, z1);
+    const uint64_t d = fma2(pk2(0.3275911f, 0.3275911f), z, pk2(1.0f, 1.0f));
+    float d0, d1;
+    upk2(d, d0, d1);
+    uint64_t r = pk2(__int_as_float(0x7EF311C7 - __float_as_int(d0)), __int_as_float(0x7EF311C7 - __float_as_int(d1)));
+    const uint64_t two = pk2(2.0f, 2.0f), nd = pk2(-d0, -d1);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) r = mul2(r, fma2(nd, r, two));
+    uint64_t p = fma2(pk2(1.061405429f, 1.061405429f), r, pk2(-1.453152027f, -1.453152027f));
+    p = fma2(p, r, pk2(1.421413741f, 1.421413741f));
+    p = fma2(p, r, pk2(-0.284496736f, -0.284496736f));
+    p = fma2(p, r, pk2(0.254829592f, 0.254829592f));
+    p = mul2(p, r);
+    float q0, q1;
+    upk2(mul2(mul2(z, z), pk2(-1.4426950408889634f, -1.4426950408889634f)), q0, q1);
+    float e0, e1;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(q0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(q1));
+    float a0, a1;
+    upk2(fma2(pk2(-1.0f, -1.0f), mul2(p, pk2(e0, e1)), pk2(1.0f, 1.0f)), a0, a1);
+    const uint64_t hx = mul2(pk2(x0, x1), pk2(0.5f, 0.5f));
+    upk2(fma2(hx, pk2(copysignf(a0, x0), copysignf(a1, x1)), hx), x0, x1);
 }
 
 // GELU in its tanh form, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),

@@ -257,13 +257,23 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float g = __uint_as_float(raw[hh][2 * i]), u = __uint_as_float(raw[hh][2 * i + 1]);
+                for (int i = 0; i < 16; i += 2) {
+                    float g0 = __uint_as_float(raw[hh][2 * i]), u0 = __uint_as_float(raw[hh][2 * i + 1]);
+                    float g1 = __uint_as_float(raw[hh][2 * i + 2]), u1 = __uint_as_float(raw[hh][2 * i + 3]);
                     if (e.bias) {
-                        g += bias_s[col + hh * 32 + 2 * i];
-                        u += bias_s[col + hh * 32 + 2 * i + 1];
+                        g0 += bias_s[col + hh * 32 + 2 * i];
+                        u0 += bias_s[col + hh * 32 + 2 * i + 1];
+                        g1 += bias_s[col + hh * 32 + 2 * i + 2];
+                        u1 += bias_s[col + hh * 32 + 2 * i + 3];
                     }
-                    o[hh * 16 + i] = (e.act == 2 ? silu(g) : gelu_erf_fast(g)) * u;
+                    if (e.act == 2) {
+                        g0 = silu(g0);
+                        g1 = silu(g1);
+                    } else {
+                        gelu_erf_fast2(g0, g1);
+                    }
+                    o[hh * 16 + i] = g0 * u0;
+                    o[hh * 16 + i + 1] = g1 * u1;
                 }
             stage_store32<T>(o, col / 2, ss, out_map);
             continue;
@@ -292,9 +302,16 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
             if (e.kind == EPI_GATED) {
                 float o[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float g = v[2 * i];
-                    o[i] = (e.act == 2 ? silu(g) : gelu_erf_fast(g)) * v[2 * i + 1];
+                for (int i = 0; i < 16; i += 2) {
+                    float g0 = v[2 * i], g1 = v[2 * i + 2];
+                    if (e.act == 2) {
+                        g0 = silu(g0);
+                        g1 = silu(g1);
+                    } else {
+                        gelu_erf_fast2(g0, g1);
+                    }
+                    o[i] = g0 * v[2 * i + 1];
+                    o[i + 1] = g1 * v[2 * i + 3];
                 }
                 store_n<T, 16>((T *)e.out + (int64_t)row * e.ldo + col / 2, o);
                 continue;
@@ -302,7 +319,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
             T *y = (T *)e.out + (int64_t)row * e.ldo + col;
             if (e.kind == EPI_GELU) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = gelu_erf_fast(v[i]);
+                for (int i = 0; i < 32; i += 2) gelu_erf_fast2(v[i], v[i + 1]);
             } else if (e.kind == EPI_GELU_TANH) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
