@@ -227,11 +227,13 @@ __device__ __forceinline__ void rope_tile(const Epilogue &e, const float *bias_s
     }
 }
 
-template <class T, int COLS, class Release>
+// KIND >= 0: the epilogue kind fixed at compile time (e.kind otherwise).
+template <class T, int COLS, int KIND, class Release>
 __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
                                               bool row_ok, int col_base, int N, const uint4 *res, StoreStage &ss,
                                               const CUtensorMap *out_map, Release release) {
-    if (e.kind == EPI_ROPE) {
+    const int kind = KIND >= 0 ? KIND : e.kind;
+    if (kind == EPI_ROPE) {
         switch (e.head_dim) {
         case 64: rope_tile<T, COLS, 64>(e, bias_s, tbase, row, row_ok, col_base, N, ss, out_map, release); break;
         case 32: rope_tile<T, COLS, 32>(e, bias_s, tbase, row, row_ok, col_base, N, ss, out_map, release); break;
@@ -249,7 +251,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
         if (c2 + 32 < COLS) tmem_ld32_async(tbase + c2 + 32, raw[1]);
         tmem_wait_ld();
         if (c2 + 64 >= COLS) release();
-        if (e.kind == EPI_GATED && ss.tma) {
+        if (kind == EPI_GATED && ss.tma) {
             // 64 interleaved (gate, up) columns -> 32 outputs, one staged tile.
             const int col = col_base + c2;
             if (col >= N) continue;
@@ -286,7 +288,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
             const int c = c2 + hh * 32;
             const int col = col_base + c;
             if (c >= COLS || col >= N) continue;
-            if (!row_ok && (e.kind == EPI_GATED || !ss.tma)) continue;
+            if (!row_ok && (kind == EPI_GATED || !ss.tma)) continue;
             float *v = vv[hh];
             if (e.bias) {
                 const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col);
@@ -299,7 +301,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                     v[4 * i + 3] += bb.w;
                 }
             }
-            if (e.kind == EPI_GATED) {
+            if (kind == EPI_GATED) {
                 float o[16];
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
@@ -317,13 +319,13 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                 continue;
             }
             T *y = (T *)e.out + (int64_t)row * e.ldo + col;
-            if (e.kind == EPI_GELU) {
+            if (kind == EPI_GELU) {
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) gelu_erf_fast2(v[i], v[i + 1]);
-            } else if (e.kind == EPI_GELU_TANH) {
+            } else if (kind == EPI_GELU_TANH) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
-            } else if (e.kind == EPI_RESIDUAL && row_ok) {
+            } else if (kind == EPI_RESIDUAL && row_ok) {
                 // This chunk's residual, loaded before the accumulator was ready.
                 const uint4 *rq = res + (c / 32) * 4;
 #pragma unroll
@@ -451,9 +453,17 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int col = col_base + c + 32 * hh;
+            const float4 *w4 = reinterpret_cast<const float4 *>(L.w_s + col);
+            const float4 *b4 = reinterpret_cast<const float4 *>(L.b_s + col);
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                w[hh][i] = (__uint_as_float(raw[hh][i]) - mean) * inv * L.w_s[col + i] + L.b_s[col + i];
+            for (int i = 0; i < 8; ++i) {
+                const float4 ww = w4[i], bb = b4[i];
+                const float *r = reinterpret_cast<const float *>(raw[hh]) + 4 * i;
+                w[hh][4 * i] = (r[0] - mean) * inv * ww.x + bb.x;
+                w[hh][4 * i + 1] = (r[1] - mean) * inv * ww.y + bb.y;
+                w[hh][4 * i + 2] = (r[2] - mean) * inv * ww.z + bb.z;
+                w[hh][4 * i + 3] = (r[3] - mean) * inv * ww.w + bb.w;
+            }
         }
         if (ss.tma) stage_store64<T>(w[0], w[1], col_base + c, ss, out_map);
         else if (row_ok) {
@@ -474,7 +484,7 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
 // and 2 j + 1 the pair of column slice j, loops over 256-row blocks; every
 // pair takes the same block, so each row's statistics meet within the
 // cluster (epilogue_ln_tile).
-template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0>
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1>
 __global__ void __launch_bounds__(128 + 128 * EPI_WG, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
                const __grid_constant__ CUtensorMap tout, int use_tma_store, int M, int N, int K, Epilogue e,
@@ -620,7 +630,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         constexpr int COLS = BN / EPI_WG;  // this warp's columns of a tile
         const uint32_t tempty_leader = PAIR ? mapa(tempty0, lead) : tempty0;
         // Gated tiles store 32 outputs per 64 columns: whole tiles need N % 64 == 0.
-        const bool tma_out = use_tma_store && (e.kind != EPI_GATED || N % 64 == 0);
+        const int kind = LNS ? EPI_RESIDUAL_LN : (KIND >= 0 ? KIND : e.kind);
+        const bool tma_out = use_tma_store && (kind != EPI_GATED || N % 64 == 0);
         StoreStage ss{tma_out, staging + ew * 4096, 0, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -630,6 +641,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             const int row = m0 + quad * 32 + lane;
             const bool row_ok = row < M;
             const int col_base = n0 + part * COLS;
+            // The next tile's residual rows into L2 now, so that its loads
+            // below wait on L2 rather than DRAM.
+            if ((kind == EPI_RESIDUAL || kind == EPI_RESIDUAL_LN) && tile + units < tiles) {
+                const int nt = tile + units;
+                const int nrow = tile_m(nt) * TM + (int)pr * BM + quad * 32 + lane;
+                const int ncol = tile_n(nt) * BN + part * COLS;
+                if (nrow < M && ncol < N) {
+                    const char *p = (const char *)((const T *)e.out + (int64_t)nrow * e.ldo + ncol);
+                    const int bytes = (N - ncol < COLS ? N - ncol : COLS) * (int)sizeof(T);
+#pragma unroll
+                    for (int b = 0; b < COLS * (int)sizeof(T); b += 128)
+                        if (b < bytes) prefetch_l2(p + b);
+                }
+            }
             // The residual rows of this warp's columns, fetched while the
             // mainloop still runs: one memory round trip a tile.
             uint4 res[COLS / 32 * 4];
@@ -637,7 +662,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                 if (!row_ok)
 #pragma unroll
                     for (int i = 0; i < COLS / 32 * 4; ++i) res[i] = make_uint4(0, 0, 0, 0);
-            if ((e.kind == EPI_RESIDUAL || e.kind == EPI_RESIDUAL_LN) && row_ok) {
+            if ((kind == EPI_RESIDUAL || kind == EPI_RESIDUAL_LN) && row_ok) {
 #pragma unroll
                 for (int c = 0; c < COLS / 32; ++c) {
                     const int col = col_base + c * 32;
@@ -667,7 +692,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                                                               &tout, L, abort_flag, fault, release))
                     break;
             } else {
-                epilogue_tile<T, COLS>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, release);
+                epilogue_tile<T, COLS, KIND>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, release);
             }
             if (++acc == 2) acc = 0, acc_phase ^= 1;
         }
@@ -729,10 +754,10 @@ template <class T, int LNS> int ln_clusters() {
     return n;
 }
 
-template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0>
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1>
 cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     using C = Cfg<BN, PAIR, LNS, EPI_WG>;
-    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS>;
+    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS, KIND>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (err != cudaSuccess) return err;
     const int TM = PAIR ? 2 * BM : BM;
@@ -769,7 +794,20 @@ cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e,
         if (N == 1024) return launch<T, 256, LN_EPI_WG, true, 4>(maps, M, N, K, e, sms, fault, s);
         return cudaErrorNotSupported;
     }
-    if (maps.pair) return launch<T, 256, 2, true>(maps, M, N, K, e, sms, fault, s);
+    // The paired kernels (every large GEMM) are compiled once per epilogue
+    // kind: each holds only its own epilogue code (fewer registers, no
+    // spills, a smaller instruction footprint).
+    if (maps.pair) {
+        switch (e.kind) {
+        case EPI_STORE: return launch<T, 256, 2, true, 0, EPI_STORE>(maps, M, N, K, e, sms, fault, s);
+        case EPI_GELU: return launch<T, 256, 2, true, 0, EPI_GELU>(maps, M, N, K, e, sms, fault, s);
+        case EPI_RESIDUAL: return launch<T, 256, 2, true, 0, EPI_RESIDUAL>(maps, M, N, K, e, sms, fault, s);
+        case EPI_GATED: return launch<T, 256, 2, true, 0, EPI_GATED>(maps, M, N, K, e, sms, fault, s);
+        case EPI_ROPE: return launch<T, 256, 2, true, 0, EPI_ROPE>(maps, M, N, K, e, sms, fault, s);
+        case EPI_GELU_TANH: return launch<T, 256, 2, true, 0, EPI_GELU_TANH>(maps, M, N, K, e, sms, fault, s);
+        default: return cudaErrorNotSupported;
+        }
+    }
     if (maps.bn == 256) return launch<T, 256, 2, false>(maps, M, N, K, e, sms, fault, s);
     return launch<T, 128, 2, false>(maps, M, N, K, e, sms, fault, s);
 }

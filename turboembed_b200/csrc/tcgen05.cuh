@@ -259,6 +259,8 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint32_t lead = 0
 }
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Bring a 128-byte line of global memory into L2 (no registers, no wait).
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 }  // namespace tc
 }  // namespace tb
