@@ -100,8 +100,10 @@ def test_tcgen05_gemm_rope(dtype, head_dim, h):
     assert rel_err(got, simt) < tol
 
 
+# 12000 rows: more 256-row blocks than clusters fit the device, so each
+# cluster takes several tiles (the staged residual rows of the next tile).
 LN_SHAPES = [(300, 768, 768), (2000, 768, 3072), (513, 1024, 1024), (1, 768, 768), (77, 1024, 4096),
-             (4096, 768, 768)]
+             (4096, 768, 768), (12000, 768, 768), (12000, 768, 3072)]
 
 
 @pytest.mark.parametrize("dtype", [F16, BF16])

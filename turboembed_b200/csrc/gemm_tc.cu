@@ -39,18 +39,22 @@ using namespace tc;
 // LNS > 0: the fused residual + LayerNorm epilogue over rows of N = 256 LNS
 // columns, computed by a cluster of LNS CTA pairs (one 256-column slice a
 // pair) that exchange row statistics through distributed shared memory.
-template <int BN, bool PAIR, int LNS = 0, int EPI_WG = 2> struct Cfg {
+// RS (with LNS): each epilogue warp's 8 KB buffer holds its next tile's
+// residual rows (TMA loads) and then its output rows (one TMA store group).
+template <int BN, bool PAIR, int LNS = 0, int EPI_WG = 2, bool RS = false> struct Cfg {
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // W rows this CTA loads a stage
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     // 16 epilogue warps (with the fused LayerNorm) take the room of two stages.
-    static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : (LNS && EPI_WG > 2 ? 3 : 5);
+    static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : (RS ? 4 : (LNS && EPI_WG > 2 ? 3 : 5));
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BAR_BYTES = 256;
     static constexpr int MAX_BIAS = LNS ? 1024 : 4096;  // the bias vector, staged in shared memory once per CTA
-    // Output staging for TMA stores: two [32 x 32] 16-bit tiles per epilogue warp.
-    static constexpr int STORE_BYTES = 4 * EPI_WG * 2 * 2048;
+    // Output staging for TMA stores: two [32 x 32] 16-bit tiles per epilogue
+    // warp (RS: four, the warp's 128 columns).
+    static constexpr int WARP_STAGE = RS ? 4 * 2048 : 2 * 2048;
+    static constexpr int STORE_BYTES = 4 * EPI_WG * WARP_STAGE;
     // LayerNorm weight and bias [N], and the row statistics two tiles deep:
     // [2][4 row quarters][EPI_WG LNS parts][32 rows] (mean, M2).
     static constexpr int PARTS = EPI_WG * LNS;
@@ -359,7 +363,9 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
 // arrival on their barrier for this row quarter); once all 2 LNS parts are in, the
 // row's mean and variance follow by Chan's pairwise formula, and a second
 // pass writes (v - mean) / sqrt(var + eps) * ln_w + ln_b. Returns false when
-// a wait gave up.
+// a wait gave up. RS: the residual comes from the warp's staged tile
+// (ss.buf, [COLS / 32] swizzled [32 x 32] tiles, lane l's row at l * 64),
+// and the output goes back into it and out as one TMA store group.
 struct LnStep {
     const float *w_s, *b_s;  // LayerNorm weight and bias in shared memory [N]
     uint32_t stats;          // this CTA's statistics block for this tile and quarter: [2 LNS][32] float2
@@ -370,7 +376,7 @@ struct LnStep {
     int slot;                // 2 * slice + part
 };
 
-template <class T, int COLS, int LNS, int PARTS, class Release>
+template <class T, int COLS, int LNS, int PARTS, bool RS, class Release>
 __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
                                                  bool row_ok, int col_base, const uint4 *res, StoreStage &ss,
                                                  const CUtensorMap *out_map, const LnStep &L, volatile int *abort_flag,
@@ -387,7 +393,6 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
         __syncwarp();
         tmem_ld32(tbase + c, v);
         const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col_base + c);
-        const uint4 *rq = res + (c / 32) * 4;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float4 bb = e.bias ? b4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -395,7 +400,13 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t w4[4] = {rq[i].x, rq[i].y, rq[i].z, rq[i].w};
+            uint4 r4;
+            if constexpr (RS)
+                r4 = *reinterpret_cast<const uint4 *>(ss.buf + (c / 32) * 2048 + lane * 64 +
+                                                      ((i ^ ((lane >> 1) & 3)) << 4));
+            else
+                r4 = res[(c / 32) * 4 + i];
+            const uint32_t w4[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float2 f = unpack2<T>(w4[j]);
@@ -465,10 +476,33 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
                 w[hh][4 * i + 3] = (r[3] - mean) * inv * ww.w + bb.w;
             }
         }
-        if (ss.tma) stage_store64<T>(w[0], w[1], col_base + c, ss, out_map);
+        if constexpr (RS) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint8_t *buf = ss.buf + (c / 32 + hh) * 2048 + lane * 64;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    uint4 u;
+                    u.x = pack2<T>(w[hh][8 * q + 0], w[hh][8 * q + 1]);
+                    u.y = pack2<T>(w[hh][8 * q + 2], w[hh][8 * q + 3]);
+                    u.z = pack2<T>(w[hh][8 * q + 4], w[hh][8 * q + 5]);
+                    u.w = pack2<T>(w[hh][8 * q + 6], w[hh][8 * q + 7]);
+                    *reinterpret_cast<uint4 *>(buf + ((q ^ ((lane >> 1) & 3)) << 4)) = u;
+                }
+            }
+        } else if (ss.tma) stage_store64<T>(w[0], w[1], col_base + c, ss, out_map);
         else if (row_ok) {
             store_n<T, 32>((T *)e.out + (int64_t)row * e.ldo + col_base + c, w[0]);
             store_n<T, 32>((T *)e.out + (int64_t)row * e.ldo + col_base + c + 32, w[1]);
+        }
+    }
+    if constexpr (RS) {
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+            for (int j = 0; j < COLS / 32; ++j) tma_store_2d(out_map, smem_u32(ss.buf + j * 2048), col_base + 32 * j, ss.row0);
+            tma_store_commit();
         }
     }
     return true;
@@ -484,13 +518,14 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
 // and 2 j + 1 the pair of column slice j, loops over 256-row blocks; every
 // pair takes the same block, so each row's statistics meet within the
 // cluster (epilogue_ln_tile).
-template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1>
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false>
 __global__ void __launch_bounds__(128 + 128 * EPI_WG, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
                const __grid_constant__ CUtensorMap tout, int use_tma_store, int M, int N, int K, Epilogue e,
                int *fault) {
     static_assert(LNS == 0 || (PAIR && BN == 256), "the fused LayerNorm runs on 256-column CTA pairs");
-    using C = Cfg<BN, PAIR, LNS, EPI_WG>;
+    static_assert(!RS || (LNS > 0 && BN / EPI_WG == 128), "staged residual rows: LayerNorm tiles of 128 columns a warp");
+    using C = Cfg<BN, PAIR, LNS, EPI_WG, RS>;
     constexpr int TM = PAIR ? 2 * BM : BM;  // rows a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -505,6 +540,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     float *lnw_s = bias_s + C::MAX_BIAS, *lnb_s = lnw_s + 1024;
     float2 *stats_s = (float2 *)(lnb_s + 1024);  // [2 tiles][4 quarters][PARTS][32]
     const uint32_t stats0 = smem_u32(stats_s), sbar0 = full0 + 16 * C::STAGES + 64;  // [2 tiles][4 quarters]
+    const uint32_t rbar0 = full0 + 16 * C::STAGES + 128;  // RS: each epilogue warp's residual arrival
     if constexpr (LNS > 0)
         for (int i = threadIdx.x; i < N; i += blockDim.x) {
             lnw_s[i] = e.ln_w[i];
@@ -529,6 +565,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         }
         if constexpr (LNS > 0)
             for (int b = 0; b < 8; ++b) mbar_init(sbar0 + 8 * b, C::PARTS * 32);  // each lane of every part
+        if constexpr (RS)
+            for (int b = 0; b < 4 * EPI_WG; ++b) mbar_init(rbar0 + 8 * b, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -632,10 +670,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         // Gated tiles store 32 outputs per 64 columns: whole tiles need N % 64 == 0.
         const int kind = LNS ? EPI_RESIDUAL_LN : (KIND >= 0 ? KIND : e.kind);
         const bool tma_out = use_tma_store && (kind != EPI_GATED || N % 64 == 0);
-        StoreStage ss{tma_out, staging + ew * 4096, 0, 0};
+        StoreStage ss{tma_out, staging + ew * C::WARP_STAGE, 0, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
         uint32_t it = 0;  // tiles done: the LayerNorm statistics buffer and phase
+        // RS: this warp's rows and columns of tile t into its buffer (TMA, zero
+        // past the last row), completing on its residual barrier.
+        const uint32_t rbar = rbar0 + 8 * ew;
+        auto load_residual = [&](int t) {
+            const int r0 = tile_m(t) * TM + (int)pr * BM + quad * 32;
+            const int c0 = tile_n(t) * BN + part * COLS;
+            mbar_expect_tx(rbar, (uint32_t)(COLS * 32 * sizeof(T)));
+#pragma unroll
+            for (int j = 0; j < COLS / 32; ++j) tma_load_2d(smem_u32(ss.buf + j * 2048), &tout, c0 + 32 * j, r0, rbar);
+        };
+        bool res_pending = false;  // RS: a residual load in flight (lane 0's view)
+        if constexpr (RS)
+            if (lane == 0 && unit < tiles) {
+                load_residual(unit);
+                res_pending = true;
+            }
         for (int tile = unit; tile < tiles; tile += units, ++it) {
             const int m0 = tile_m(tile) * TM + (int)pr * BM, n0 = tile_n(tile) * BN;
             const int row = m0 + quad * 32 + lane;
@@ -643,7 +697,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             const int col_base = n0 + part * COLS;
             // The next tile's residual rows into L2 now, so that its loads
             // below wait on L2 rather than DRAM.
-            if ((kind == EPI_RESIDUAL || kind == EPI_RESIDUAL_LN) && tile + units < tiles) {
+            if ((kind == EPI_RESIDUAL || kind == EPI_RESIDUAL_LN) && !RS && tile + units < tiles) {
                 const int nt = tile + units;
                 const int nrow = tile_m(nt) * TM + (int)pr * BM + quad * 32 + lane;
                 const int ncol = tile_n(nt) * BN + part * COLS;
@@ -662,7 +716,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                 if (!row_ok)
 #pragma unroll
                     for (int i = 0; i < COLS / 32 * 4; ++i) res[i] = make_uint4(0, 0, 0, 0);
-            if ((kind == EPI_RESIDUAL || kind == EPI_RESIDUAL_LN) && row_ok) {
+            if ((kind == EPI_RESIDUAL || kind == EPI_RESIDUAL_LN) && !RS && row_ok) {
 #pragma unroll
                 for (int c = 0; c < COLS / 32; ++c) {
                     const int col = col_base + c * 32;
@@ -672,6 +726,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                 }
             }
             if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, fault)) break;
+            if constexpr (RS) {
+                if (!mbar_wait(rbar, it & 1, abort_flag, fault)) break;
+                res_pending = false;
+            }
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + acc * BN + part * COLS;
             const int a_now = acc;
@@ -688,15 +746,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                 const uint32_t qb = (it & 1) * 4 + quad;  // this tile's buffer, this quarter
                 LnStep L{lnw_s, lnb_s, stats0 + qb * (C::PARTS * 32 * 8), stats_s + qb * (C::PARTS * 32),
                          sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * EPI_WG + part};
-                if (!epilogue_ln_tile<T, COLS, LNS, C::PARTS>(e, bias_s, tbase, row, row_ok, col_base, res, ss,
-                                                              &tout, L, abort_flag, fault, release))
+                if (!epilogue_ln_tile<T, COLS, LNS, C::PARTS, RS>(e, bias_s, tbase, row, row_ok, col_base, res, ss,
+                                                                  &tout, L, abort_flag, fault, release))
                     break;
+                if constexpr (RS)
+                    if (lane == 0 && tile + units < tiles) {
+                        tma_store_wait_read<0>();  // the output left the buffer
+                        load_residual(tile + units);
+                        res_pending = true;
+                    }
             } else {
                 epilogue_tile<T, COLS, KIND>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, release);
             }
             if (++acc == 2) acc = 0, acc_phase ^= 1;
         }
         if (ss.tma && lane == 0) tma_store_wait<0>();  // every store written before the CTA leaves
+        // After a failed wait: the residual load still in flight lands before
+        // the CTA leaves (bounded; the abort flag is already set).
+        if (RS && res_pending) {
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try(rbar, it & 1) && globaltimer() - t0 < WAIT_NS / 4) {
+            }
+        }
     }
     tc_fence_before();
     if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal it
@@ -728,10 +799,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // ring; 4 measured slower (3 stages starve FFN-out's K = 3072 mainloop).
 constexpr int LN_EPI_WG = 2;
 
-template <class T, int LNS> int ln_clusters() {
+template <class T, int LNS, bool RS = false> int ln_clusters() {
     static const int n = [] {
-        using C = Cfg<256, true, LNS, LN_EPI_WG>;
-        auto kern = gemm_tc_kernel<T, 256, LN_EPI_WG, true, LNS>;
+        using C = Cfg<256, true, LNS, LN_EPI_WG, RS>;
+        auto kern = gemm_tc_kernel<T, 256, LN_EPI_WG, true, LNS, -1, RS>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return 0;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * LNS);
@@ -754,16 +825,16 @@ template <class T, int LNS> int ln_clusters() {
     return n;
 }
 
-template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1>
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false>
 cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
-    using C = Cfg<BN, PAIR, LNS, EPI_WG>;
-    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS, KIND>;
+    using C = Cfg<BN, PAIR, LNS, EPI_WG, RS>;
+    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS, KIND, RS>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (err != cudaSuccess) return err;
     const int TM = PAIR ? 2 * BM : BM;
     constexpr int CL = LNS ? 2 * LNS : (PAIR ? 2 : 1);
     const int tiles = LNS ? (M + TM - 1) / TM : ((M + TM - 1) / TM) * ((N + BN - 1) / BN);
-    const int units = LNS ? ln_clusters<T, LNS>() : sms / CL;
+    const int units = LNS ? ln_clusters<T, LNS, RS>() : sms / CL;
     if (units <= 0) return cudaErrorNotSupported;
     const int grid_units = tiles < units ? tiles : units;
     cudaLaunchConfig_t cfg = {};
@@ -790,6 +861,10 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     if (e.kind == EPI_RESIDUAL_LN) {
+        // Short mainloops (K up to 1024: attention-out) are bound by the
+        // epilogue: they take the staged residual rows and 4 stages.
+        if (N == 768 && K <= 1024 && maps.has_out)
+            return launch<T, 256, LN_EPI_WG, true, 3, -1, true>(maps, M, N, K, e, sms, fault, s);
         if (N == 768) return launch<T, 256, LN_EPI_WG, true, 3>(maps, M, N, K, e, sms, fault, s);
         if (N == 1024) return launch<T, 256, LN_EPI_WG, true, 4>(maps, M, N, K, e, sms, fault, s);
         return cudaErrorNotSupported;
@@ -848,8 +923,8 @@ bool gemm_ln_fusable(Dt dt, int n) {
     // 1024-column rows take clusters of 8, of which too few fit the GPCs:
     // measured slower than the separate LayerNorm, so only 768 is fused.
     if (n != 768) return false;
-    if (dt == Dt::F16) return (n == 768 ? ln_clusters<__half, 3>() : ln_clusters<__half, 4>()) > 0;
-    if (dt == Dt::BF16) return (n == 768 ? ln_clusters<__nv_bfloat16, 3>() : ln_clusters<__nv_bfloat16, 4>()) > 0;
+    if (dt == Dt::F16) return ln_clusters<__half, 3>() > 0 && ln_clusters<__half, 3, true>() > 0;
+    if (dt == Dt::BF16) return ln_clusters<__nv_bfloat16, 3>() > 0 && ln_clusters<__nv_bfloat16, 3, true>() > 0;
     return false;
 }
 
