@@ -359,9 +359,9 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
 // rows and COLS columns of a 256-column slice. v = acc + bias + residual;
 // the warp's part of each row's statistics (mean and M2 over its COLS
 // columns, one pass over TMEM) goes to every CTA of the cluster holding
-// the same rows (slot `slot` of their statistics buffers, then each lane's
-// arrival on their barrier for this row quarter); once all 2 LNS parts are in, the
-// row's mean and variance follow by Chan's pairwise formula, and a second
+// the same rows (slot `slot` of their statistics buffers, by st.async
+// completing its bytes on their barrier for this row quarter); once all
+// PARTS parts are in, the row's mean and variance follow by Chan's pairwise formula, and a second
 // pass writes (v - mean) / sqrt(var + eps) * ln_w + ln_b. Returns false when
 // a wait gave up. RS: the residual comes from the warp's staged tile
 // (ss.buf, [COLS / 32] swizzled [32 x 32] tiles, lane l's row at l * 64),
@@ -374,6 +374,7 @@ struct LnStep {
     uint32_t phase;
     uint32_t half;           // the pair half (rank & 1): the CTAs with the same rows are half + 2 j
     int slot;                // 2 * slice + part
+    bool arm;                // this lane arms the quarter's barrier for this tile (one lane a quarter)
 };
 
 template <class T, int COLS, int LNS, int PARTS, bool RS, class Release>
@@ -425,14 +426,13 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
     }
     const float mean_p = k + s1 / (float)COLS;
     const float m2 = fmaxf(s2 - s1 * (s1 / (float)COLS), 0.0f);
-    // This row's part to the LNS CTAs holding the row, each store followed
-    // by this lane's own release-arrival there (which orders it).
+    // This row's part to the LNS CTAs holding the row: asynchronous stores
+    // that complete their bytes on the receiver's barrier, which one lane a
+    // quarter arms with all PARTS x 32 rows' bytes.
     const uint32_t mine = L.stats + (uint32_t)((L.slot * 32 + lane) * 8);
 #pragma unroll
-    for (int j = 0; j < LNS; ++j) {
-        st_cluster_v2(mapa(mine, L.half + 2 * j), mean_p, m2);
-        mbar_arrive_cluster(mapa(L.bar, L.half + 2 * j));
-    }
+    for (int j = 0; j < LNS; ++j) st_async_v2(mapa(mine, L.half + 2 * j), mean_p, m2, mapa(L.bar, L.half + 2 * j));
+    if (L.arm) mbar_expect_tx(L.bar, (uint32_t)(PARTS * 32 * 8));
     if (!mbar_wait_cluster(L.bar, L.phase, abort_flag, fault)) {
         release();
         return false;
@@ -564,7 +564,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             mbar_init(tempty0 + 8 * a, (PAIR ? 2 : 1) * 4 * EPI_WG);
         }
         if constexpr (LNS > 0)
-            for (int b = 0; b < 8; ++b) mbar_init(sbar0 + 8 * b, C::PARTS * 32);  // each lane of every part
+            for (int b = 0; b < 8; ++b) mbar_init(sbar0 + 8 * b, 1);  // armed by one lane; the stores complete it
         if constexpr (RS)
             for (int b = 0; b < 4 * EPI_WG; ++b) mbar_init(rbar0 + 8 * b, 1);
         *abort_flag = 0;
@@ -745,7 +745,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             if constexpr (LNS > 0) {
                 const uint32_t qb = (it & 1) * 4 + quad;  // this tile's buffer, this quarter
                 LnStep L{lnw_s, lnb_s, stats0 + qb * (C::PARTS * 32 * 8), stats_s + qb * (C::PARTS * 32),
-                         sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * EPI_WG + part};
+                         sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * EPI_WG + part, lane == 0 && part == 0};
                 if (!epilogue_ln_tile<T, COLS, LNS, C::PARTS, RS>(e, bias_s, tbase, row, row_ok, col_base, res, ss,
                                                                   &tout, L, abort_flag, fault, release))
                     break;

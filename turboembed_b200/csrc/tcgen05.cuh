@@ -202,6 +202,15 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void st_cluster_v2(uint32_t cluster_addr, float a, float b) {
     asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(cluster_addr), "f"(a), "f"(b) : "memory");
 }
+// An asynchronous 8-byte store into a cluster peer's shared memory that
+// completes 8 bytes of transactions on the peer's mbarrier `cluster_bar`
+// (the peer arms it with expect_tx): no fence or wait on the sender.
+__device__ __forceinline__ void st_async_v2(uint32_t cluster_addr, float a, float b, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                     cluster_addr),
+                 "f"(a), "f"(b), "r"(cluster_bar)
+                 : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
