@@ -738,7 +738,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    if constexpr (PAIR) mbar_arrive_cluster(tempty_leader + 8 * a_now);
+                    if constexpr (PAIR) mbar_arrive_remote(tempty_leader + 8 * a_now);
                     else mbar_arrive(tempty0 + 8 * a_now);
                 }
             };

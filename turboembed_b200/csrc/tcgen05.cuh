@@ -211,8 +211,13 @@ __device__ __forceinline__ void st_async_v2(uint32_t cluster_addr, float a, floa
                  "f"(a), "f"(b), "r"(cluster_bar)
                  : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+// Arrive on a barrier of a cluster peer (or this CTA, through its cluster
+// address) with the default semantics (release at CTA scope): for barriers
+// that hand over TMEM, ordered by tcgen05.fence::before_thread_sync, not
+// memory written for the peer (a cluster-scope release would wait for
+// every store of the warp still in flight).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
     uint32_t ok;
