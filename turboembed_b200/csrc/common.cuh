@@ -200,5 +200,16 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     const float hx = 0.5f * x;
     return fmaf(hx, tanh_approx(u), hx);
 }
+// The same for a pair in packed F32x2 arithmetic (each lane rounds as the
+// scalar form does: the same bits), the two tanh on the MUFU.
+__device__ __forceinline__ void gelu_tanh2(float &x0, float &x1) {
+    const uint64_t x = pk2(x0, x1);
+    const uint64_t p = fma2(pk2(0.035677408136300125f, 0.035677408136300125f), mul2(x, x),
+                            pk2(0.7978845608028654f, 0.7978845608028654f));
+    float u0, u1;
+    upk2(mul2(x, p), u0, u1);
+    const uint64_t hx = mul2(pk2(0.5f, 0.5f), x);
+    upk2(fma2(hx, pk2(tanh_approx(u0), tanh_approx(u1)), hx), x0, x1);
+}
 
 }  // namespace tb

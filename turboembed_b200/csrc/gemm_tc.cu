@@ -328,7 +328,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                 for (int i = 0; i < 32; i += 2) gelu_erf_fast2(v[i], v[i + 1]);
             } else if (kind == EPI_GELU_TANH) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+                for (int i = 0; i < 32; i += 2) gelu_tanh2(v[i], v[i + 1]);
             } else if (kind == EPI_RESIDUAL && row_ok) {
                 // This chunk's residual, loaded before the accumulator was ready.
                 const uint4 *rq = res + (c / 32) * 4;
