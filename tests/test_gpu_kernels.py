@@ -209,8 +209,11 @@ def test_mma_attention(dtype, case):
     assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
 
 
+# The last case has more units than the persistent CTAs (several a CTA),
+# two-tile and one-tile units mixed.
 TC_CASES = [([128], 2, 64, -1), ([300, 5, 129], 12, 64, -1), ([500, 130], 2, 64, 64), ([1], 1, 64, -1),
-            ([513, 7, 256, 1000], 3, 64, -1), ([900, 200], 2, 64, 64), ([64, 33], 2, 64, 4)]
+            ([513, 7, 256, 1000], 3, 64, -1), ([900, 200], 2, 64, 64), ([64, 33], 2, 64, 4),
+            ([1000] * 16 + [100, 300] * 8, 8, 64, -1)]
 
 
 @pytest.mark.parametrize("dtype", [F16, BF16])
