@@ -295,7 +295,19 @@ def main():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        # NCCL prints its version banner on stdout when the first
+        # communicator comes up (the first collective): keep stdout for the
+        # one JSON line by sending the process's fd 1 to stderr meanwhile.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            dist.barrier(device_ids=[local])
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
 
     def reduce(x, op):
         if dist is None:
