@@ -78,6 +78,14 @@ TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M, uint32_t 
                                            const float *w, const float *bias, const float *y_in, const float *ln_w,
                                            const float *ln_b, float eps, float *y_out, turbo_error *err);
 
+/* The pre-norm form of the same (N = 768, K up to 1280), as ModernBERT's
+ * layers run it: sum_out = y_in + a w^T + bias (rounded to dtype, the
+ * residual stream) and ln_out = LN(that sum) * ln_w + ln_b, one launch. */
+TB_EXPORT int32_t turbo_b200_gemm_ln_dual_check(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K, const float *a,
+                                                const float *w, const float *bias, const float *y_in,
+                                                const float *ln_w, const float *ln_b, float eps, float *sum_out,
+                                                float *ln_out, turbo_error *err);
+
 /* Failure detection without a GPU fault: a kernel waits on an mbarrier
  * nothing completes with the library's bounded wait, limited to limit_ns;
  * it gives up, sets the fault word (fault_out = 1) and returns; a second

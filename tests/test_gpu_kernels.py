@@ -129,6 +129,28 @@ def test_tcgen05_gemm_residual_layernorm(dtype, shape):
     assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
 
 
+@pytest.mark.parametrize("dtype", [F16, BF16])
+@pytest.mark.parametrize("shape", [(300, 768, 768), (12000, 768, 1152), (1, 768, 1152), (5000, 768, 768)])
+def test_tcgen05_gemm_prenorm_layernorm_writes_sum_and_norm(dtype, shape):
+    # Pre-norm layers (ModernBERT): one launch leaves the residual stream
+    # sum = y + a w^T + b in y and LN(sum) (weight only) in a second buffer.
+    M, N, K = shape
+    rng = np.random.default_rng(M + N + K + 1)
+    a = rng.standard_normal((M, K), np.float32)
+    w = rng.standard_normal((N, K), np.float32) * np.float32(1 / np.sqrt(K))
+    bias = rng.standard_normal(N).astype(np.float32)
+    y_in = rng.standard_normal((M, N)).astype(np.float32) * 3
+    ln_w = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    ln_b = np.zeros(N, np.float32)
+    total, got = runtime.gemm_ln_dual_check(dtype, a, w, bias, y_in, ln_w, ln_b, 1e-5)
+    v = ref_gemm(dtype, 2, a, w, bias, y_in)
+    assert rel_err(total, v) < (8e-3 if dtype == BF16 else 1.5e-3)
+    mean = v.mean(1, keepdims=True)
+    var = ((v - mean) ** 2).mean(1, keepdims=True)
+    want = (v - mean) / np.sqrt(var + 1e-5) * ln_w + ln_b
+    assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
+
+
 @pytest.mark.parametrize("epi", [0, 1, 2, 3])
 def test_ffma_gemm_f32_is_one_chain_over_k(epi):
     M, N, K = 150, 160, 200

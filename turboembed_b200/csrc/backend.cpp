@@ -199,8 +199,9 @@ struct Session {
     bool upload_pending = false;
     // GEMM operand maps over x, xn, ctx, ffn (box rows 128)
     CUtensorMap map_x{}, map_xn{}, map_ctx{}, map_ffn{}, map_qkv{}, map_qkv64{};
-    // TMA store maps of the GEMM outputs x, qkv and ffn ([32 x 32] boxes)
-    CUtensorMap out_x{}, out_qkv{}, out_ffn{};
+    // TMA store maps of the GEMM outputs x, qkv and ffn ([32 x 32] boxes),
+    // and of xn (pre-norm models)
+    CUtensorMap out_x{}, out_qkv{}, out_ffn{}, out_xn{};
     // the written state
     bool written = false;
     int tokens = 0, batch = 0, n_vectors = 0, n_attn = 0, n_attn2 = 0, max_len = 0;
@@ -213,6 +214,9 @@ struct Session {
     // (EPI_RESIDUAL_LN), unless the environment sets TB_LNFUSE=0 (an A/B
     // switch, read at session open).
     bool fuse_ln = false;
+    // Pre-norm layers (ModernBERT) fold the LayerNorm that follows each
+    // residual GEMM into it: the GEMM writes x and xn = LN(x) (same switch).
+    bool fuse_ln_pre = false;
     bool exact_tf32 = false;  // F32 sessions: GEMMs on kind::tf32 x3 (else FFMA)
     uint64_t h2d_bytes = 0;
     std::vector<int32_t> row_start, row_len;
@@ -776,7 +780,10 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
     s->cap_vectors = std::max(s->max_batch, s->max_ranges);
     {
         const char *v = getenv("TB_LNFUSE");
-        s->fuse_ln = !m->modern && dt != Dt::F32 && !(v && v[0] == '0') && gemm_ln_fusable(dt, m->hidden);
+        const bool on = dt != Dt::F32 && !(v && v[0] == '0') && gemm_ln_fusable(dt, m->hidden);
+        s->fuse_ln = on && !m->modern;
+        s->fuse_ln_pre = on && m->modern && gemm_ln_dual_takes(m->hidden, m->hidden) &&
+                         gemm_ln_dual_takes(m->hidden, m->inter);
     }
     const int qt = attention_queries(s.get());
     s->max_attn_items = (int)(cap / qt) + s->max_batch + 1;
@@ -827,6 +834,7 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         if (e == cudaSuccess) e = make_store_map(dt, s->x, rows, h, h, &s->out_x);
         if (e == cudaSuccess) e = make_store_map(dt, s->qkv, rows, 3 * h, 3 * h, &s->out_qkv);
         if (e == cudaSuccess) e = make_store_map(dt, s->ffn, rows, I, I, &s->out_ffn);
+        if (e == cudaSuccess && m->modern) e = make_store_map(dt, s->xn, rows, h, h, &s->out_xn);
     }
     if (e == cudaSuccess && dt == Dt::F32) {
         e = make_operand_map_f32((const float *)s->x, rows, h, h, &s->map_x);
@@ -1038,7 +1046,7 @@ template <class F> cudaError_t timed(Session *s, int kind, double flops, F launc
 // One GEMM of the layer loop: the tensor-core kernel on F16/BF16 sessions,
 // the FFMA kernel on F32 ones.
 cudaError_t linear_launch(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi,
-                          int M, const CUtensorMap *out_map) {
+                          int M, const CUtensorMap *out_map, const CUtensorMap *out2_map) {
     if (s->dt == Dt::F32) {
         Epilogue e2 = epi;
         if (epi.kind == EPI_ROPE) e2.kind = EPI_STORE;
@@ -1059,13 +1067,18 @@ cudaError_t linear_launch(Session *s, const CUtensorMap *amap, const void *a, co
         maps.out = *out_map;
         maps.has_out = true;
     }
+    if (out2_map) {
+        maps.out2 = *out2_map;
+        maps.has_out2 = true;
+    }
     return gemm_tc(s->dt, maps, M, L.n, L.k, epi, s->ctx->sms, s->ctx->fault_dev, s->ctx->stream);
 }
 
-// out_map: the output's TMA store map, or null for direct stores.
+// out_map: the output's TMA store map, or null for direct stores; out2_map:
+// Epilogue::out2's (pre-norm fused LayerNorm).
 cudaError_t linear(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi, int M,
-                   const CUtensorMap *out_map = nullptr) {
-    return timed(s, 0, 2.0 * M * L.n * L.k, [&] { return linear_launch(s, amap, a, L, epi, M, out_map); });
+                   const CUtensorMap *out_map = nullptr, const CUtensorMap *out2_map = nullptr) {
+    return timed(s, 0, 2.0 * M * L.n * L.k, [&] { return linear_launch(s, amap, a, L, epi, M, out_map, out2_map); });
 }
 
 // Block k of a tapped range write: the ranges pooled from layer l's states
@@ -1156,6 +1169,7 @@ cudaError_t encode(Session *s) {
     });
     if (e != cudaSuccess) return e;
     const size_t half_tab = (size_t)m->positions * m->rope_pairs;
+    bool xn_ready = false;  // xn already holds this layer's attention pre-norm (fused into the last GEMM)
     for (int l = 0; l < s->layers_run; ++l) {
         const LayerWeights &L = ws.layers[l];
         const bool global = m->global_every == 0 || l % m->global_every == 0;
@@ -1163,8 +1177,9 @@ cudaError_t encode(Session *s) {
         const void *src = s->x;
         const CUtensorMap *src_map = &s->map_x;
         if (l > 0) {
-            if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->xn, L.ln1_w, nullptr, T, h, m->eps, st); })) !=
-                cudaSuccess)
+            if (!xn_ready &&
+                (e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->xn, L.ln1_w, nullptr, T, h, m->eps, st); })) !=
+                    cudaSuccess)
                 return e;
             src = s->xn;
             src_map = &s->map_xn;
@@ -1176,21 +1191,37 @@ cudaError_t encode(Session *s) {
         if ((e = attention(global ? -1 : m->window)) != cudaSuccess) return e;
         Epilogue o;
         o.kind = EPI_RESIDUAL, o.out = s->x, o.ldo = h;
-        if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
-        if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->xn, L.ln2_w, nullptr, T, h, m->eps, st); })) !=
-            cudaSuccess)
-            return e;
+        if (s->fuse_ln_pre) {
+            // x += ctx W_o^T + b and xn = LN_mlp(x) in one launch.
+            o.kind = EPI_RESIDUAL_LN, o.ln_w = L.ln2_w, o.ln_eps = (float)m->eps, o.out2 = s->xn, o.ldo2 = h;
+            if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x, &s->out_xn)) != cudaSuccess) return e;
+        } else {
+            if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
+            if ((e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->xn, L.ln2_w, nullptr, T, h, m->eps, st); })) !=
+                cudaSuccess)
+                return e;
+        }
         Epilogue g;
         g.kind = EPI_GATED, g.out = s->ffn, g.ldo = I, g.act = m->act;
         if ((e = linear(s, &s->map_xn, s->xn, L.ffn_in, g, T, &s->out_ffn)) != cudaSuccess) return e;
         Epilogue f2;
         f2.kind = EPI_RESIDUAL, f2.out = s->x, f2.ldo = h;
-        if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) return e;
         // A tap before the last layer reads the layer's states through the
-        // final norm, the scale the final states are on.
-        if (s->taps > 1 && l + 1 < s->layers_run && l >= s->layers_run - s->taps) {
-            if ((e = layer_norm(dt, s->x, s->xn, m->final_w, nullptr, T, h, m->eps, st)) != cudaSuccess) return e;
-            if ((e = pool_tap(s, l, s->xn)) != cudaSuccess) return e;
+        // final norm, the scale the final states are on (into ctx, free
+        // until the next attention: xn may hold the next layer's pre-norm).
+        const bool tap = s->taps > 1 && l + 1 < s->layers_run && l >= s->layers_run - s->taps;
+        xn_ready = s->fuse_ln_pre && l + 1 < s->layers_run;
+        if (xn_ready) {
+            // x += ffn W_2^T + b and xn = LN_attn(x) of the next layer in one launch.
+            f2.kind = EPI_RESIDUAL_LN, f2.ln_w = ws.layers[l + 1].ln1_w, f2.ln_eps = (float)m->eps, f2.out2 = s->xn,
+            f2.ldo2 = h;
+            if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x, &s->out_xn)) != cudaSuccess) return e;
+        } else if ((e = linear(s, &s->map_ffn, s->ffn, L.ffn_out, f2, T, &s->out_x)) != cudaSuccess) {
+            return e;
+        }
+        if (tap) {
+            if ((e = layer_norm(dt, s->x, s->ctxb, m->final_w, nullptr, T, h, m->eps, st)) != cudaSuccess) return e;
+            if ((e = pool_tap(s, l, s->ctxb)) != cudaSuccess) return e;
         }
     }
     (void)es;

@@ -34,6 +34,7 @@ namespace tb {
 namespace {
 
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
+constexpr int LN_STAGED_MAX_K = 1280;  // fused LayerNorm GEMMs with the staged residual (K up to this)
 using namespace tc;
 
 // LNS > 0: the fused residual + LayerNorm epilogue over rows of N = 256 LNS
@@ -380,8 +381,13 @@ struct LnStep {
 template <class T, int COLS, int LNS, int PARTS, bool RS, class Release>
 __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
                                                  bool row_ok, int col_base, const uint4 *res, StoreStage &ss,
-                                                 const CUtensorMap *out_map, const LnStep &L, volatile int *abort_flag,
-                                                 int *fault, Release release) {
+                                                 const CUtensorMap *out_map, const CUtensorMap *out2_map,
+                                                 const LnStep &L, volatile int *abort_flag, int *fault,
+                                                 Release release) {
+    // RS with out2 (pre-norm layers): pass 1 also leaves v in the staged
+    // tile, which goes to out (the residual stream) as one store group;
+    // pass 2's normalised rows then go to out2.
+    const bool dual = RS && e.out2 != nullptr;
     const int lane = threadIdx.x & 31;
     float v[32];
     // Pass 1: v = accumulator + bias + residual, written back to TMEM (pass
@@ -415,6 +421,18 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
                 v[8 * i + 2 * j + 1] += f.y;
             }
         }
+        if (dual) {
+            // v back where this lane's residual came from.
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint4 u;
+                u.x = pack2<T>(v[8 * i + 0], v[8 * i + 1]);
+                u.y = pack2<T>(v[8 * i + 2], v[8 * i + 3]);
+                u.z = pack2<T>(v[8 * i + 4], v[8 * i + 5]);
+                u.w = pack2<T>(v[8 * i + 6], v[8 * i + 7]);
+                *reinterpret_cast<uint4 *>(ss.buf + (c / 32) * 2048 + lane * 64 + ((i ^ ((lane >> 1) & 3)) << 4)) = u;
+            }
+        }
         tmem_st32(tbase + c, v);
         if (c == 0) k = v[0];
 #pragma unroll
@@ -422,6 +440,15 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
             const float d = v[i] - k;
             s1 += d;
             s2 = fmaf(d, d, s2);
+        }
+    }
+    if (dual) {
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+            for (int j = 0; j < COLS / 32; ++j) tma_store_2d(out_map, smem_u32(ss.buf + j * 2048), col_base + 32 * j, ss.row0);
+            tma_store_commit();
         }
     }
     const float mean_p = k + s1 / (float)COLS;
@@ -452,6 +479,10 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
     const float inv = 1.0f / sqrtf(M2 / (float)(PARTS * COLS) + e.ln_eps);
     // Pass 2: normalise and store, 64 columns a step.
     static_assert(COLS % 64 == 0, "the LayerNorm epilogue stores 64 columns a step");
+    if (dual) {
+        if (lane == 0) tma_store_wait_read<0>();  // v has left the staged tile
+        __syncwarp();
+    }
 #pragma unroll 1
     for (int c = 0; c < COLS; c += 64) {
         uint32_t raw[2][32];
@@ -501,7 +532,8 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
         __syncwarp();
         if (lane == 0) {
 #pragma unroll
-            for (int j = 0; j < COLS / 32; ++j) tma_store_2d(out_map, smem_u32(ss.buf + j * 2048), col_base + 32 * j, ss.row0);
+            for (int j = 0; j < COLS / 32; ++j)
+                tma_store_2d(dual ? out2_map : out_map, smem_u32(ss.buf + j * 2048), col_base + 32 * j, ss.row0);
             tma_store_commit();
         }
     }
@@ -521,8 +553,8 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
 template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false>
 __global__ void __launch_bounds__(128 + 128 * EPI_WG, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
-               const __grid_constant__ CUtensorMap tout, int use_tma_store, int M, int N, int K, Epilogue e,
-               int *fault) {
+               const __grid_constant__ CUtensorMap tout, const __grid_constant__ CUtensorMap tout2, int use_tma_store,
+               int M, int N, int K, Epilogue e, int *fault) {
     static_assert(LNS == 0 || (PAIR && BN == 256), "the fused LayerNorm runs on 256-column CTA pairs");
     static_assert(!RS || (LNS > 0 && BN / EPI_WG == 128), "staged residual rows: LayerNorm tiles of 128 columns a warp");
     using C = Cfg<BN, PAIR, LNS, EPI_WG, RS>;
@@ -747,7 +779,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                 LnStep L{lnw_s, lnb_s, stats0 + qb * (C::PARTS * 32 * 8), stats_s + qb * (C::PARTS * 32),
                          sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * EPI_WG + part, lane == 0 && part == 0};
                 if (!epilogue_ln_tile<T, COLS, LNS, C::PARTS, RS>(e, bias_s, tbase, row, row_ok, col_base, res, ss,
-                                                                  &tout, L, abort_flag, fault, release))
+                                                                  &tout, &tout2, L, abort_flag, fault, release))
                     break;
                 if constexpr (RS)
                     if (lane == 0 && tile + units < tiles) {
@@ -855,15 +887,17 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
         attr[1].val.clusterDim.z = 1;
         cfg.numAttrs = 2;
     }
-    return counted(cudaLaunchKernelEx(&cfg, kern, maps.a, maps.w, maps.out, maps.has_out ? 1 : 0, M, N, K, e, fault));
+    return counted(
+        cudaLaunchKernelEx(&cfg, kern, maps.a, maps.w, maps.out, maps.out2, maps.has_out ? 1 : 0, M, N, K, e, fault));
 }
 
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     if (e.kind == EPI_RESIDUAL_LN) {
-        // Short mainloops (K up to 1024: attention-out) are bound by the
-        // epilogue: they take the staged residual rows and 4 stages.
-        if (N == 768 && K <= 1024 && maps.has_out)
+        // Short mainloops (K up to 1280: attention-out, and the gated
+        // models' FFN-out) are bound by the epilogue: they take the staged
+        // residual rows and 4 stages.
+        if (N == 768 && K <= LN_STAGED_MAX_K && maps.has_out)
             return launch<T, 256, LN_EPI_WG, true, 3, -1, true>(maps, M, N, K, e, sms, fault, s);
         if (N == 768) return launch<T, 256, LN_EPI_WG, true, 3>(maps, M, N, K, e, sms, fault, s);
         if (N == 1024) return launch<T, 256, LN_EPI_WG, true, 4>(maps, M, N, K, e, sms, fault, s);
@@ -919,6 +953,8 @@ cudaError_t make_store_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+bool gemm_ln_dual_takes(int n, int k) { return n == 768 && k <= LN_STAGED_MAX_K; }
+
 bool gemm_ln_fusable(Dt dt, int n) {
     // 1024-column rows take clusters of 8, of which too few fit the GPCs:
     // measured slower than the separate LayerNorm, so only 768 is fused.
@@ -935,6 +971,8 @@ cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilog
     if (epi.kind == EPI_ROPE && (epi.head_dim > 64 || 64 % epi.head_dim != 0)) return cudaErrorNotSupported;
     if (epi.bias && N > Cfg<256, false>::MAX_BIAS) return cudaErrorNotSupported;
     if (maps.pair && maps.bn != 256) return cudaErrorNotSupported;
+    if (epi.out2 && (epi.kind != EPI_RESIDUAL_LN || !gemm_ln_dual_takes(N, K) || !maps.has_out || !maps.has_out2))
+        return cudaErrorNotSupported;
     if (epi.kind == EPI_RESIDUAL_LN && (!maps.pair || !epi.ln_w || (N != 768 && N != 1024)))
         return cudaErrorNotSupported;
     if (dt == Dt::F16) return dispatch<__half>(maps, M, N, K, epi, sms, fault, s);

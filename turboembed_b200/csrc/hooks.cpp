@@ -180,10 +180,12 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t vari
 // The fused residual + LayerNorm GEMM (EPI_RESIDUAL_LN) on N = 768 or
 // 1024 columns: y = LN(y_in + a w^T + bias) * ln_w + ln_b, operands narrowed
 // to dtype as turbo_b200_gemm_check does.
-extern "C" TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K,
-                                                      const float *a, const float *w, const float *bias,
-                                                      const float *y_in, const float *ln_w, const float *ln_b,
-                                                      float eps, float *y_out, turbo_error *err) {
+namespace {
+// ln_out null: y_out = the LayerNorm; else y_out = the sum and ln_out = its
+// LayerNorm (the pre-norm form, Epilogue::out2).
+int32_t gemm_ln_run(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K, const float *a, const float *w,
+                    const float *bias, const float *y_in, const float *ln_w, const float *ln_b, float eps,
+                    float *y_out, float *ln_out, turbo_error *err) {
     Dt dt;
     if (!dt_of(dtype, &dt) || dt == Dt::F32) return hook_fail(err, TURBO_E_INVALID_ENUM, "dtype", cudaSuccess);
     Dev dv;
@@ -209,7 +211,16 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M
     TcMaps maps;
     maps.bn = 256;
     maps.pair = true;
-    e = make_operand_map(dt, da, M, K, K, 128, &maps.a);
+    void *d2 = nullptr;
+    if (ln_out) {
+        d2 = dv.get((size_t)M * N * 2);  // F16 / BF16
+        if (!d2) return hook_fail(err, TURBO_E_RUNTIME, "gemm_ln_check setup", cudaErrorMemoryAllocation);
+        ep.out2 = d2;
+        ep.ldo2 = (int64_t)N;
+        e = make_store_map(dt, d2, M, N, N, &maps.out2);
+        maps.has_out2 = true;
+    }
+    if (e == cudaSuccess) e = make_operand_map(dt, da, M, K, K, 128, &maps.a);
     if (e == cudaSuccess) e = make_operand_map(dt, dw, N, K, K, 128, &maps.w);
     if (e == cudaSuccess) e = make_store_map(dt, dy, M, N, N, &maps.out);
     maps.has_out = true;
@@ -222,8 +233,27 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M
     cudaMemcpy(&f, fault, 4, cudaMemcpyDeviceToHost);
     if (f) return hook_fail(err, TURBO_E_RUNTIME, "gemm_ln_check: the kernel's fault word is set", cudaSuccess);
     widen_host(dt, dy, y_out, (size_t)M * N);
+    if (ln_out) widen_host(dt, d2, ln_out, (size_t)M * N);
     if (err) err->code = 0, err->message[0] = 0;
     return TURBO_OK;
+}
+}  // namespace
+
+extern "C" TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K,
+                                                      const float *a, const float *w, const float *bias,
+                                                      const float *y_in, const float *ln_w, const float *ln_b,
+                                                      float eps, float *y_out, turbo_error *err) {
+    return gemm_ln_run(dtype, M, N, K, a, w, bias, y_in, ln_w, ln_b, eps, y_out, nullptr, err);
+}
+
+// The pre-norm form (N = 768, K up to 1280): sum = y_in + a w^T + bias
+// (narrowed to dtype) and ln = LN(sum) * ln_w + ln_b from one launch.
+extern "C" TB_EXPORT int32_t turbo_b200_gemm_ln_dual_check(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K,
+                                                           const float *a, const float *w, const float *bias,
+                                                           const float *y_in, const float *ln_w, const float *ln_b,
+                                                           float eps, float *sum_out, float *ln_out,
+                                                           turbo_error *err) {
+    return gemm_ln_run(dtype, M, N, K, a, w, bias, y_in, ln_w, ln_b, eps, sum_out, ln_out, err);
 }
 
 namespace {

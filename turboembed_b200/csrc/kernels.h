@@ -38,6 +38,11 @@ struct Epilogue {
     // EPI_RESIDUAL_LN: the LayerNorm's weight and bias [N] F32 and epsilon.
     const float *ln_w = nullptr, *ln_b = nullptr;
     float ln_eps = 0.0f;
+    // EPI_RESIDUAL_LN of pre-norm layers: the sum y + acc + b stays in out
+    // (the residual stream) and its LayerNorm goes to out2 (the next
+    // product's input), row stride ldo2.
+    void *out2 = nullptr;
+    int64_t ldo2 = 0;
 };
 
 // The packed batch of one run, in device memory: each packed token's id,
@@ -105,10 +110,10 @@ cudaError_t gemm_simt(Dt dt, const void *a, int64_t lda, const void *w, int M, i
 // out (with has_out) is a map over the output made by make_store_map: the
 // store, GELU and residual epilogues then write through TMA stores.
 struct TcMaps {
-    CUtensorMap a, w, out;
+    CUtensorMap a, w, out, out2;  // out2: Epilogue::out2's store map
     int bn = 256;
     bool pair = false;
-    bool has_out = false;
+    bool has_out = false, has_out2 = false;
 };
 // A TMA map for GEMM outputs: [32 x 32] boxes, 64-byte swizzle.
 cudaError_t make_store_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
@@ -130,6 +135,9 @@ cudaError_t gemm_tf32(const CUtensorMap &a_map, const CUtensorMap &w_map, int M,
 // Whether EPI_RESIDUAL_LN runs for rows of n columns at dt: n = 768 or 1024
 // and the device fits at least one cluster of n / 128 CTAs.
 bool gemm_ln_fusable(Dt dt, int n);
+// Whether EPI_RESIDUAL_LN with out2 (sum and LayerNorm both written) takes
+// an n x k product: n = 768, k up to 1280 (the staged-residual kernel).
+bool gemm_ln_dual_takes(int n, int k);
 
 // Attention within each row and head, Q/K/V read from qkv [tokens, 3h],
 // context written to ctx [tokens, h]. window < 0: whole row; else query i

@@ -303,6 +303,24 @@ def gemm_ln_check(dtype, a, w, bias, y_in, ln_w, ln_b, eps):
     return out
 
 
+def gemm_ln_dual_check(dtype, a, w, bias, y_in, ln_w, ln_b, eps):
+    """turbo_b200_gemm_ln_dual_check: (sum, LN(sum) * ln_w + ln_b) with
+    sum = y_in + a w^T + bias, from the pre-norm fused GEMM (N = 768)."""
+    lib = library()
+    f = lib.turbo_b200_gemm_ln_dual_check
+    f.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32] + [C.c_void_p] * 6 + [
+        C.c_float, C.c_void_p, C.c_void_p, C.POINTER(abi.turbo_error)]
+    arrs = [np.ascontiguousarray(x, np.float32) for x in (a, w, bias, y_in, ln_w, ln_b)]
+    M, K = arrs[0].shape
+    N = arrs[1].shape[0]
+    total = np.zeros((M, N), np.float32)
+    out = np.zeros((M, N), np.float32)
+    err = abi.new_error()
+    _check(f(dtype, M, N, K, *[_ptr(x) for x in arrs], eps, _ptr(total), _ptr(out), C.byref(err)), err,
+           "gemm_ln_dual_check")
+    return total, out
+
+
 def attention_check(dtype, variant, lens, qkv, live, heads, head_dim, window=-1):
     lib = library()
     lens = np.ascontiguousarray(lens, np.int32)
