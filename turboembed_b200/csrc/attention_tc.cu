@@ -21,10 +21,11 @@
 // buffers each, the next chunk's while this one is in use:
 //   warps 0..3, 4..7  two softmax warpgroups, one per 128-query tile
 //                     (S in TMEM columns 0..63 / 64..127, O in 128..191 /
-//                     192..255, P in its own shared-memory tile);
-//   warp 8, lane 0    every MMA: S of a tile's next chunk as soon as its
-//                     softmax holds the current S in registers and the K
-//                     chunk is in, P V as soon as P is written;
+//                     192..255; P written back over its chunk's S columns
+//                     as packed pairs, the A operand of P V read from TMEM);
+//   warp 8, lane 0    every MMA: a tile's P V as soon as its softmax has
+//                     written P, then the tile's next S into the same
+//                     columns (in issue order, after P V has read P);
 //   warp 9, lane 0    every TMA load (Q of both tiles, K and V chunks) into
 //                     buffers the MMAs have released (tcgen05.commit).
 // attn_tc_kernel (sliding-window layers, and the allocation-free entry
@@ -57,7 +58,7 @@ constexpr int P_BYTES = QT * KT * 2;  // 16 KB
 constexpr int SMEM = Q_BYTES + 2 * KV_BYTES + P_BYTES + 256 + 1024;
 constexpr int CTAS_PER_SM = 4;
 constexpr int KB2 = 3;  // attn_tc2's K buffers (V has 2)
-constexpr int SMEM2 = 2 * Q_BYTES + 2 * P_BYTES + (KB2 + 2) * KV_BYTES + 256 + 1024;
+constexpr int SMEM2 = 2 * Q_BYTES + (KB2 + 2) * KV_BYTES + 256 + 1024;  // P lives in TMEM
 constexpr int CTAS_PER_SM2 = 2;
 constexpr float RESCALE = 8.0f;  // log2 units
 
@@ -132,7 +133,11 @@ struct SoftBars {
 // warp's TMEM lanes at the tile's S columns; O sits o_off columns further.
 // r is the thread's query row in the tile; rowp its 128-byte row of the
 // tile's P operand. Returns false when the kernel must stop.
-template <class T>
+// PT (attn_tc2): P goes into TMEM over the chunk's own S columns (the A
+// operand of P V, read from TMEM), so S is not released early and nothing
+// waits for the previous P V: when S(j) is complete, the commit that
+// signalled it also covers P V(j - 1), issued before it.
+template <class T, bool PT = false>
 __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo, int khi, int window, int head,
                                              T *__restrict__ ctx, int h, const uint8_t *__restrict__ live,
                                              float scale_log2, uint32_t lane_base, uint32_t o_off, uint8_t *rowp, int r,
@@ -172,8 +177,10 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo
 #pragma unroll
             for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
         }
-        tc_fence_before();
-        mbar_arrive(b.sf);
+        if constexpr (!PT) {
+            tc_fence_before();
+            mbar_arrive(b.sf);
+        }
         // Invalid keys (masked, past the row, outside the window) become
         // -inf; the row max of the valid raw scores (the scale is positive,
         // so it is applied once after).
@@ -197,7 +204,7 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo
         float mx = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
         mx = mx == -INFINITY ? mx : mx * scale_log2;
         // P smem and O are free once the previous chunk's P V is done.
-        if (j > 0) {
+        if (!PT && j > 0) {
             if (!mbar_wait(b.o, (g - 1) & 1, abort_flag, fault)) return false;
             tc_fence_after();
         }
@@ -242,19 +249,30 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo
         float rs, rs1;
         upk2(add2(add2(s4[0], s4[1]), add2(s4[2], s4[3])), rs, rs1);
         rs += rs1;
+        if constexpr (PT) {
+            // P as 32 columns of packed pairs over this chunk's S columns
+            // (packed in place: pair i reads sv[2i], sv[2i + 1], i <= 2i).
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-            uint4 w;
-            w.x = pack2<T>(sv[8 * cc + 0], sv[8 * cc + 1]);
-            w.y = pack2<T>(sv[8 * cc + 2], sv[8 * cc + 3]);
-            w.z = pack2<T>(sv[8 * cc + 4], sv[8 * cc + 5]);
-            w.w = pack2<T>(sv[8 * cc + 6], sv[8 * cc + 7]);
-            *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
+            for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(pack2<T>(sv[2 * i], sv[2 * i + 1]));
+            tmem_st32(lane_base, sv);  // waits for the store
+            l += rs;
+            tc_fence_before();
+            mbar_arrive(b.p);
+        } else {
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                uint4 w;
+                w.x = pack2<T>(sv[8 * cc + 0], sv[8 * cc + 1]);
+                w.y = pack2<T>(sv[8 * cc + 2], sv[8 * cc + 3]);
+                w.z = pack2<T>(sv[8 * cc + 4], sv[8 * cc + 5]);
+                w.w = pack2<T>(sv[8 * cc + 6], sv[8 * cc + 7]);
+                *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
+            }
+            l += rs;
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(b.p);
         }
-        l += rs;
-        fence_async_smem();
-        tc_fence_before();
-        mbar_arrive(b.p);
     }
     if (!mbar_wait(b.o, (g - 1) & 1, abort_flag, fault)) return false;
     tc_fence_after();
@@ -443,7 +461,7 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 float scale_log2, int *fault) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sQ = smem, *sP = sQ + 2 * Q_BYTES, *sK = sP + 2 * P_BYTES, *sV = sK + KB2 * KV_BYTES;
+    uint8_t *sQ = smem, *sK = sQ + 2 * Q_BYTES, *sV = sK + KB2 * KV_BYTES;
     uint8_t *bars = sV + 2 * KV_BYTES;
     // Barriers: Q in, Q free, K in [3], K free [3], V in [2], V free [2],
     // then per tile t the four SoftBars.
@@ -541,13 +559,15 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         }
     } else if (warp == 8) {
         if (lane == 0) {
-            // MMAs. Per chunk: S of both tiles' next chunk as soon as each
-            // softmax holds its current S and the next K is in (then a
-            // commit releases K's buffer), P V of each tile as soon as its P
-            // is written (then V's buffer). A unit's Q buffer is released
-            // after its last S.
+            // MMAs. Per chunk and tile: P V (A = P from the tile's S columns
+            // in TMEM) as soon as the softmax has written P, then the
+            // tile's next S into the same columns; the tensor pipe runs a
+            // thread's MMAs in order, so S(j + 1) overwrites P(j) only after
+            // P V(j) has read it, and S(j + 1)'s commit covers P V(j). K's
+            // buffer is released once both tiles' S of the chunk are
+            // issued, V's once both P V are, Q's after the unit's last S.
             const uint32_t ids = idesc(fmt, KT, false), idpv = idesc(fmt, D, true);
-            const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sP);
+            const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV);
             const SoftBars tb0 = tile_bars(0), tb1 = tile_bars(1);
             uint32_t c = 0, qn = 0, g0 = 0, g1 = 0;  // chunks; units; each tile's chunks
             bool ok = true;
@@ -561,52 +581,44 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 umma_commit(t ? tb1.s : tb0.s);
             };
             auto issue_pv = [&](int t, uint32_t vb, bool acc) {
-                const uint32_t p = ap + t * P_BYTES, v = av + vb * KV_BYTES;
+                const uint32_t v = av + vb * KV_BYTES;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < KT / 16; ++kk)
-                    umma_f16(tmem + 128 + t * 64, smem_desc(p) + (uint64_t)(kk * 2), smem_desc(v + kk * 16 * 128), idpv,
-                             (acc || kk) ? 1u : 0u);
+                    // A = P [128 q x 64 keys] in TMEM, 8 columns (16 keys) a
+                    // step; B = V [64 keys x 64 d] MN-major, 16 keys a step.
+                    umma_f16_ts(tmem + 128 + t * 64, tmem + t * 64 + kk * 8, smem_desc(v + kk * 16 * 128), idpv,
+                                (acc || kk) ? 1u : 0u);
                 umma_commit(t ? tb1.o : tb0.o);
             };
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++qn) {
                 const AttnItem it = items[u / heads];
                 const bool two = it.q0 + QT < it.len;
                 const int nch = (it.len + KT - 1) / KT;
-                // The unit's first S: Q and K in, each softmax done with its
-                // previous S.
+                // The unit's first S: Q and K in (each tile's S columns are
+                // free: its last P V was issued before).
                 if (!(ok = mbar_wait(bar_q, qn & 1, abort_flag, fault))) break;
                 if (!(ok = mbar_wait(bar_k + 8 * (c % KB2), (c / KB2) & 1, abort_flag, fault))) break;
-                if (g0 > 0 && !(ok = mbar_wait(tb0.sf, (g0 - 1) & 1, abort_flag, fault))) break;
                 issue_s(0, c % KB2);
-                if (two) {
-                    if (g1 > 0 && !(ok = mbar_wait(tb1.sf, (g1 - 1) & 1, abort_flag, fault))) break;
-                    issue_s(1, c % KB2);
-                }
+                if (two) issue_s(1, c % KB2);
                 umma_commit(bar_kf + 8 * (c % KB2));
+                if (nch == 1) umma_commit(bar_qf);
                 for (int j = 0; j < nch && ok; ++j, ++c, ++g0, g1 += two ? 1 : 0) {
-                    if (j + 1 < nch) {
-                        const uint32_t kb = (c + 1) % KB2;
-                        if (!(ok = mbar_wait(bar_k + 8 * kb, ((c + 1) / KB2) & 1, abort_flag, fault))) break;
-                        if (!(ok = mbar_wait(tb0.sf, g0 & 1, abort_flag, fault))) break;
-                        issue_s(0, kb);
-                        if (two) {
-                            if (!(ok = mbar_wait(tb1.sf, g1 & 1, abort_flag, fault))) break;
-                            issue_s(1, kb);
-                        }
-                        umma_commit(bar_kf + 8 * kb);
-                    } else {
-                        umma_commit(bar_qf);
-                    }
-                    const uint32_t vb = c & 1;
+                    const uint32_t vb = c & 1, kb = (c + 1) % KB2;
+                    const bool more = j + 1 < nch;
                     if (!(ok = mbar_wait(bar_v + 8 * vb, (c >> 1) & 1, abort_flag, fault))) break;
+                    if (more && !(ok = mbar_wait(bar_k + 8 * kb, ((c + 1) / KB2) & 1, abort_flag, fault))) break;
                     if (!(ok = mbar_wait(tb0.p, g0 & 1, abort_flag, fault))) break;
                     issue_pv(0, vb, j > 0);
+                    if (more) issue_s(0, kb);
                     if (two) {
                         if (!(ok = mbar_wait(tb1.p, g1 & 1, abort_flag, fault))) break;
                         issue_pv(1, vb, j > 0);
+                        if (more) issue_s(1, kb);
                     }
                     umma_commit(bar_vf + 8 * vb);
+                    if (more) umma_commit(bar_kf + 8 * kb);
+                    if (j + 2 == nch) umma_commit(bar_qf);
                 }
             }
         }
@@ -621,8 +633,8 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             const AttnItem it = items[u / heads];
             const int q0 = it.q0 + t * QT;
             if (q0 >= it.len) continue;  // a unit with one tile
-            if (!softmax_tile<T>(it, q0, 0, it.len, -1, u % heads, ctx, h, live, scale_log2, lane_base, 128,
-                                 sP + t * P_BYTES + r * 128, r, sb, g, abort_flag, fault))
+            if (!softmax_tile<T, true>(it, q0, 0, it.len, -1, u % heads, ctx, h, live, scale_log2, lane_base, 128,
+                                       nullptr, r, sb, g, abort_flag, fault))
                 break;
         }
     }
