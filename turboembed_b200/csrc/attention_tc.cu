@@ -15,10 +15,10 @@
 // buffer with the 128-byte swizzle.
 //
 // attn_tc2_kernel (full attention, the encoder's global layers): persistent
-// CTAs, two per SM (about 98 KB shared memory, 256 TMEM columns each), 320
+// CTAs, two per SM (about 100 KB shared memory, 256 TMEM columns each), 320
 // threads, looping over units (row, 256-query pair of tiles, head). Both
-// tiles read the same keys, so K and V are loaded once for the two, into two
-// buffers each, the next chunk's while this one is in use:
+// tiles read the same keys, so K and V are loaded once for the two, into four
+// buffers each, up to four chunks ahead:
 //   warps 0..3, 4..7  two softmax warpgroups, one per 128-query tile
 //                     (S in TMEM columns 0..63 / 64..127, O in 128..191 /
 //                     192..255; P written back over its chunk's S columns
@@ -57,8 +57,8 @@ constexpr int KV_BYTES = KT * D * 2;  // 8 KB
 constexpr int P_BYTES = QT * KT * 2;  // 16 KB
 constexpr int SMEM = Q_BYTES + 2 * KV_BYTES + P_BYTES + 256 + 1024;
 constexpr int CTAS_PER_SM = 4;
-constexpr int KB2 = 3;  // attn_tc2's K buffers (V has 2)
-constexpr int SMEM2 = 2 * Q_BYTES + (KB2 + 2) * KV_BYTES + 256 + 1024;  // P lives in TMEM
+constexpr int KB2 = 4, VB2 = 4;  // attn_tc2's K and V buffers (loads run up to 4 chunks ahead)
+constexpr int SMEM2 = 2 * Q_BYTES + (KB2 + VB2) * KV_BYTES + 256 + 1024;  // P lives in TMEM
 constexpr int CTAS_PER_SM2 = 2;
 constexpr float RESCALE = 8.0f;  // log2 units
 
@@ -462,17 +462,19 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sQ = smem, *sK = sQ + 2 * Q_BYTES, *sV = sK + KB2 * KV_BYTES;
-    uint8_t *bars = sV + 2 * KV_BYTES;
-    // Barriers: Q in, Q free, K in [3], K free [3], V in [2], V free [2],
-    // then per tile t the four SoftBars.
+    uint8_t *bars = sV + VB2 * KV_BYTES;
+    // Barriers: Q in, Q free, K in [KB2], K free [KB2], V in [VB2], V free
+    // [VB2], then per tile t the four SoftBars (224 bytes of the 256).
+    static_assert(16 + 16 * (KB2 + VB2) + 64 + 16 <= 256, "attn_tc2's barriers fit their 256 bytes");
     const uint32_t b0 = smem_u32(bars);
-    const uint32_t bar_q = b0, bar_qf = b0 + 8, bar_k = b0 + 16, bar_kf = b0 + 40, bar_v = b0 + 64, bar_vf = b0 + 80;
+    const uint32_t bar_q = b0, bar_qf = b0 + 8, bar_k = b0 + 16, bar_kf = bar_k + 8 * KB2, bar_v = bar_kf + 8 * KB2,
+                   bar_vf = bar_v + 8 * VB2;
     auto tile_bars = [&](int t) {
-        const uint32_t x = b0 + 96 + 32 * t;
+        const uint32_t x = bar_vf + 8 * VB2 + 32 * t;
         return SoftBars{x, x + 8, x + 16, x + 24};
     };
-    uint32_t *tmem_slot = (uint32_t *)(bars + 160);
-    volatile int *abort_flag = (volatile int *)(bars + 168);
+    uint32_t *tmem_slot = (uint32_t *)(bars + 16 + 16 * (KB2 + VB2) + 64);
+    volatile int *abort_flag = (volatile int *)(bars + 16 + 16 * (KB2 + VB2) + 72);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = n_items * heads;
@@ -484,9 +486,11 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             mbar_init(bar_k + 8 * i, 1);
             mbar_init(bar_kf + 8 * i, 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < VB2; ++i) {
             mbar_init(bar_v + 8 * i, 1);
             mbar_init(bar_vf + 8 * i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             const SoftBars tb = tile_bars(i);
             mbar_init(tb.s, 1);
             mbar_init(tb.sf, 128);
@@ -512,9 +516,10 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     if (warp == 9) {
         if (lane == 0) {
             // Loads. Chunk c (counted over this CTA's units) uses K buffer
-            // c % 3, free once the S of chunk c - 3 are done, and V buffer
-            // c & 1, free once the P V of chunk c - 2 are; the K stream runs
-            // one chunk ahead of the V stream (S comes before P V).
+            // c % KB2, free once the S of chunk c - KB2 are done, and V
+            // buffer c % VB2, free once the P V of chunk c - VB2 are; the K
+            // stream runs one chunk ahead of the V stream (S comes before
+            // P V).
             struct Unit {
                 int start, q0, len, col, nch;
             };
@@ -532,8 +537,8 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 ++kc;
             };
             auto load_v = [&](const Unit &n, int j) {
-                const uint32_t b = vc & 1;
-                if (vc >= 2 && !(ok = mbar_wait(bar_vf + 8 * b, ((vc - 2) >> 1) & 1, abort_flag, fault))) return;
+                const uint32_t b = vc % VB2;
+                if (vc >= VB2 && !(ok = mbar_wait(bar_vf + 8 * b, ((vc - VB2) / VB2) & 1, abort_flag, fault))) return;
                 mbar_expect_tx(bar_v + 8 * b, KV_BYTES);
                 tma_load_2d(smem_u32(sV + b * KV_BYTES), &tkv, 2 * h + n.col, n.start + j * KT, bar_v + 8 * b);
                 ++vc;
@@ -604,9 +609,9 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                 umma_commit(bar_kf + 8 * (c % KB2));
                 if (nch == 1) umma_commit(bar_qf);
                 for (int j = 0; j < nch && ok; ++j, ++c, ++g0, g1 += two ? 1 : 0) {
-                    const uint32_t vb = c & 1, kb = (c + 1) % KB2;
+                    const uint32_t vb = c % VB2, kb = (c + 1) % KB2;
                     const bool more = j + 1 < nch;
-                    if (!(ok = mbar_wait(bar_v + 8 * vb, (c >> 1) & 1, abort_flag, fault))) break;
+                    if (!(ok = mbar_wait(bar_v + 8 * vb, (c / VB2) & 1, abort_flag, fault))) break;
                     if (more && !(ok = mbar_wait(bar_k + 8 * kb, ((c + 1) / KB2) & 1, abort_flag, fault))) break;
                     if (!(ok = mbar_wait(tb0.p, g0 & 1, abort_flag, fault))) break;
                     issue_pv(0, vb, j > 0);
