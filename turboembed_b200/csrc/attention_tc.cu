@@ -55,7 +55,7 @@ constexpr int QT = 128, KT = 64, D = 64;
 constexpr int Q_BYTES = QT * D * 2;   // 16 KB
 constexpr int KV_BYTES = KT * D * 2;  // 8 KB
 constexpr int P_BYTES = QT * KT * 2;  // 16 KB
-constexpr int SMEM = Q_BYTES + 2 * KV_BYTES + P_BYTES + 256 + 1024;
+constexpr int SMEM = Q_BYTES + 4 * KV_BYTES + 256 + 1024;  // Q, K [2], V [2]; P lives in TMEM
 constexpr int CTAS_PER_SM = 4;
 constexpr int KB2 = 4, VB2 = 4;  // attn_tc2's K and V buffers (loads run up to 4 chunks ahead)
 constexpr int SMEM2 = 2 * Q_BYTES + (KB2 + VB2) * KV_BYTES + 256 + 1024;  // P lives in TMEM
@@ -309,10 +309,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                int window, float scale_log2, int *fault) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *sQ = smem, *sP = smem + Q_BYTES, *sK = sP + P_BYTES, *sV = sK + KV_BYTES;
-    uint8_t *bars = sV + KV_BYTES;
-    const uint32_t bar_q = smem_u32(bars), bar_k = bar_q + 8, bar_v = bar_q + 16, bar_s = bar_q + 24;
-    const uint32_t bar_p = bar_q + 32, bar_o = bar_q + 40, bar_sf = bar_q + 48;
+    uint8_t *sQ = smem, *sK = smem + Q_BYTES, *sV = sK + 2 * KV_BYTES;
+    uint8_t *bars = sV + 2 * KV_BYTES;
+    // Q in, K in [2], V in [2], S done, P written, P V done.
+    const uint32_t bar_q = smem_u32(bars), bar_k = bar_q + 8, bar_v = bar_q + 24, bar_s = bar_q + 40;
+    const uint32_t bar_p = bar_q + 48, bar_o = bar_q + 56;
     uint32_t *tmem_slot = (uint32_t *)(bars + 64);
     volatile int *abort_flag = (volatile int *)(bars + 72);
 
@@ -321,12 +322,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 
     if (threadIdx.x == 0) {
         mbar_init(bar_q, 1);
-        mbar_init(bar_k, 1);
-        mbar_init(bar_v, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar_k + 8 * i, 1);
+            mbar_init(bar_v + 8 * i, 1);
+        }
         mbar_init(bar_s, 1);
         mbar_init(bar_p, 128);
         mbar_init(bar_o, 1);
-        mbar_init(bar_sf, 128);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
@@ -345,14 +347,23 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 
     if (warp == 4) {
         if (lane == 0) {
+            // Loads and MMAs. Chunk y (counted over this CTA's units) uses
+            // K and V buffer y & 1. P V(y) takes A = P from the S columns
+            // in TMEM and S(y + 1) follows it into the same columns (in
+            // issue order). When P(y) arrives, S(y) and P V(y - 1) are done
+            // (the commit the softmax waited on covers both): K(y + 1) can
+            // go into buffer (y + 1) & 1 once S(y) is issued, V(y + 1) once
+            // P(y) is in, each a whole chunk ahead. The next unit's Q goes
+            // in once this unit's last S is done.
             const uint32_t ids = idesc(fmt, KT, false), idpv = idesc(fmt, D, true);
-            const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV), ap = smem_u32(sP);
+            const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK), av = smem_u32(sV);
             // A unit's TMA coordinates, read once: first key row, query row,
-            // head column, chunk count.
+            // head column, chunk count (0: past the last unit).
             struct Unit {
                 int row0, qrow, col, nch;
             };
             auto unit_of = [&](int u) {
+                if (u >= units) return Unit{0, 0, 0, 0};
                 const AttnItem it = items[u / heads];
                 int klo, khi;
                 key_range(it.len, it.q0, window, klo, khi);
@@ -362,85 +373,88 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 mbar_expect_tx(bar_q, Q_BYTES);
                 tma_load_2d(aq, &tq, n.col, n.qrow, bar_q);
             };
-            auto load_k = [&](const Unit &n, int j) {
-                mbar_expect_tx(bar_k, KV_BYTES);
-                tma_load_2d(ak, &tkv, h + n.col, n.row0 + j * KT, bar_k);
+            auto load_kv = [&](const Unit &n, int j, uint32_t y, bool k) {
+                const uint32_t b = y & 1, bar = (k ? bar_k : bar_v) + 8 * b;
+                mbar_expect_tx(bar, KV_BYTES);
+                tma_load_2d((k ? ak : av) + b * KV_BYTES, &tkv, (k ? h : 2 * h) + n.col, n.row0 + j * KT, bar);
             };
-            auto load_v = [&](const Unit &n, int j) {
-                mbar_expect_tx(bar_v, KV_BYTES);
-                tma_load_2d(av, &tkv, 2 * h + n.col, n.row0 + j * KT, bar_v);
-            };
-            auto issue_s = [&]() {
+            auto issue_s = [&](uint32_t kb) {
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(tmem, smem_desc(aq) + (uint64_t)(kk * 2), smem_desc(ak) + (uint64_t)(kk * 2), ids,
-                             kk > 0 ? 1u : 0u);
+                    umma_f16(tmem, smem_desc(aq) + (uint64_t)(kk * 2), smem_desc(ak + kb * KV_BYTES) + (uint64_t)(kk * 2),
+                             ids, kk > 0 ? 1u : 0u);
                 umma_commit(bar_s);
             };
-            uint32_t g = 0, qc = 0;  // chunks and units done so far
-            bool ok = true;
+            auto issue_pv = [&](uint32_t vb, bool acc) {
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < KT / 16; ++kk)
+                    // A = P [128 q x 64 keys] in TMEM, 8 columns (16 keys) a
+                    // step; B = V [64 keys x 64 d] MN-major, 16 keys a step.
+                    umma_f16_ts(tmem + 64, tmem + kk * 8, smem_desc(av + vb * KV_BYTES + kk * 16 * 128), idpv,
+                                (acc || kk) ? 1u : 0u);
+                umma_commit(bar_o);
+            };
+            const int grid = (int)gridDim.x;
             int u = blockIdx.x;
-            Unit cur = u < units ? unit_of(u) : Unit{0, 0, 0, 0};
+            Unit cur = unit_of(u), nxt = unit_of(u + grid);
+            // K or V of the chunk after (this unit, chunk j), stream chunk
+            // y + 1: this unit's next chunk, or the next unit's first.
+            auto load_after = [&](int j, uint32_t y, bool k) {
+                if (j + 1 < cur.nch) load_kv(cur, j + 1, y + 1, k);
+                else if (nxt.nch > 0) load_kv(nxt, 0, y + 1, k);
+            };
+            uint32_t y = 0, qn = 0;  // chunks and units done so far
+            bool ok = true;
             if (u < units) {
                 load_q(cur);
-                load_k(cur, 0);
-                load_v(cur, 0);
+                load_kv(cur, 0, 0, true);
+                load_kv(cur, 0, 0, false);
+                load_after(0, 0, true);
+                load_after(0, 0, false);
             }
-            for (; u < units && ok; u += gridDim.x, ++qc) {
-                const int next = u + gridDim.x;
-                const Unit nxt = next < units ? unit_of(next) : Unit{0, 0, 0, 0};
-                if (!(ok = mbar_wait(bar_q, qc & 1, abort_flag, fault))) break;
-                // The softmax has S of the previous chunk in registers.
-                if (g > 0 && !(ok = mbar_wait(bar_sf, (g - 1) & 1, abort_flag, fault))) break;
-                if (!(ok = mbar_wait(bar_k, g & 1, abort_flag, fault))) break;
-                issue_s();
-                for (int j = 0; j < cur.nch && ok; ++j, ++g) {
-                    const uint32_t par = g & 1;
-                    // S done: K (and, after the last chunk, Q) are free.
-                    if (!(ok = mbar_wait(bar_s, par, abort_flag, fault))) break;
-                    if (j + 1 < cur.nch) load_k(cur, j + 1);
-                    else if (next < units) {
-                        load_q(nxt);
-                        load_k(nxt, 0);
-                    }
-                    // The next S as soon as the softmax holds this one: it
-                    // runs while the softmax works on this chunk.
+            for (; u < units && ok; u += grid, ++qn) {
+                if (!(ok = mbar_wait(bar_q, qn & 1, abort_flag, fault))) break;
+                if (!(ok = mbar_wait(bar_k + 8 * (y & 1), (y >> 1) & 1, abort_flag, fault))) break;
+                issue_s(y & 1);
+                if (y >= 1) load_after(0, y, true);  // buffer (y + 1) & 1: S(y - 1) is done (P(y - 1) came)
+                if (cur.nch == 1) {
+                    if (!(ok = mbar_wait(bar_s, y & 1, abort_flag, fault))) break;
+                    if (nxt.nch > 0) load_q(nxt);
+                }
+                for (int j = 0; j < cur.nch && ok; ++j, ++y) {
+                    if (!(ok = mbar_wait(bar_p, y & 1, abort_flag, fault))) break;
+                    if (y >= 1) load_after(j, y, false);  // buffer (y + 1) & 1: P V(y - 1) is done
+                    if (!(ok = mbar_wait(bar_v + 8 * (y & 1), (y >> 1) & 1, abort_flag, fault))) break;
+                    issue_pv(y & 1, j > 0);
                     if (j + 1 < cur.nch) {
-                        if (!(ok = mbar_wait(bar_sf, par, abort_flag, fault))) break;
-                        if (!(ok = mbar_wait(bar_k, (g + 1) & 1, abort_flag, fault))) break;
-                        issue_s();
+                        if (!(ok = mbar_wait(bar_k + 8 * ((y + 1) & 1), ((y + 1) >> 1) & 1, abort_flag, fault))) break;
+                        issue_s((y + 1) & 1);
+                        load_after(j + 1, y + 1, true);  // buffer y & 1: S(y) is done (P(y) came)
+                        if (j + 2 == cur.nch) {
+                            // The unit's last S: once it is done, Q is free.
+                            if (!(ok = mbar_wait(bar_s, (y + 1) & 1, abort_flag, fault))) break;
+                            if (nxt.nch > 0) load_q(nxt);
+                        }
                     }
-                    // P written (O rescaled) by the softmax; V loaded.
-                    if (!(ok = mbar_wait(bar_p, par, abort_flag, fault))) break;
-                    if (!(ok = mbar_wait(bar_v, par, abort_flag, fault))) break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < KT / 16; ++kk)
-                        // A = P [128 q x 64 keys] K-major; B = V [64 keys x 64 d] MN-major, 16 keys a step.
-                        umma_f16(tmem + 64, smem_desc(ap) + (uint64_t)(kk * 2), smem_desc(av + kk * 16 * 128), idpv,
-                                 (j | kk) ? 1u : 0u);
-                    umma_commit(bar_o);
-                    // P V done: V and P are free.
-                    if (!(ok = mbar_wait(bar_o, par, abort_flag, fault))) break;
-                    if (j + 1 < cur.nch) load_v(cur, j + 1);
-                    else if (next < units) load_v(nxt, 0);
                 }
                 cur = nxt;
+                nxt = unit_of(u + 2 * grid);
             }
         }
     } else {
         // Softmax: thread r = query row r = TMEM lane r.
         const int r = threadIdx.x;
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        const SoftBars sb{bar_s, bar_sf, bar_p, bar_o};
+        const SoftBars sb{bar_s, 0u, bar_p, bar_o};  // no S release: P goes over S in TMEM
         uint32_t g = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
             const AttnItem it = items[u / heads];
             int klo, khi;
             key_range(it.len, it.q0, window, klo, khi);
-            if (!softmax_tile<T>(it, it.q0, klo, khi, window, u % heads, ctx, h, live, scale_log2, lane_base, 64,
-                                 sP + r * 128, r, sb, g, abort_flag, fault))
+            if (!softmax_tile<T, true>(it, it.q0, klo, khi, window, u % heads, ctx, h, live, scale_log2, lane_base,
+                                       64, nullptr, r, sb, g, abort_flag, fault))
                 break;
         }
     }
