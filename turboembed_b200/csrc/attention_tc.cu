@@ -100,9 +100,10 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float 
     y0 = x0 >= -126.0f ? __int_as_float(__float_as_int(p0) + (__float_as_int(r0) << 23)) : 0.0f;
     y1 = x1 >= -126.0f ? __int_as_float(__float_as_int(p1) + (__float_as_int(r1) << 23)) : 0.0f;
 }
-// Which pairs of a 64-key chunk take the polynomial: one in four, so the
-// MUFU and the FMA pipe share the exponentials.
-__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (pair & 3) == 3; }
+// Which pairs of a 64-key chunk take the polynomial: one in eight, so the
+// MUFU and the FMA pipe share the exponentials (one in four and none both
+// measured slower: the polynomial costs issue slots, the MUFU queue fills).
+__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (pair & 7) == 7; }
 
 // Instruction descriptors of kind::f16 with F32 accumulators, M = 128.
 __host__ __device__ constexpr uint32_t idesc(uint32_t fmt, int n, bool b_mn_major) {
