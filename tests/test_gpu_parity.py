@@ -182,6 +182,24 @@ def test_bf16_model_runs_in_bf16(ctx):
     m.release()
 
 
+@pytest.mark.parametrize("lens_range", [(80, 300), (1100, 1300)])
+def test_xlmr_large_shape_in_bf16(ctx, lens_range):
+    # Hidden 1024, 16 heads, FFN 4096 (config 5's model) at BF16: the
+    # separate LayerNorm of 1024-column rows (weights in shared memory), the
+    # one-tile and (rows past 1,024) the two-tile attention kernels.
+    d = models.synthetic("xlmr-large", 4, dtype=abi.TURBO_DTYPE_BF16, layers=2)
+    lo, hi = lens_range
+    ids, mask, lens = models.rows_long(6, 2, lo, hi, hi, 5, 250001)
+    m = ctx.load(d)
+    s = m.session(2, hi, MODEL)
+    assert s.compute_dtype == abi.TURBO_DTYPE_BF16
+    got = s.embed(ids, mask)
+    want = oracle.encode(d, ids, mask)
+    check(got, want, MODEL, "xlm-r large shape, 2 layers")
+    s.release()
+    m.release()
+
+
 @pytest.mark.parametrize("precision", [EXACT, FASTEST])
 def test_modernbert_long_rows_local_and_global_layers(ctx, precision):
     d = models.synthetic("modernbert-base", 3, layers=3)

@@ -171,23 +171,35 @@ __global__ void __launch_bounds__(256) ln_vec_kernel(const T *__restrict__ src, 
 // The F16/BF16 LayerNorm: as ln_vec_kernel (the same sums in the same
 // order, so the same bits), with each lane's weights and biases held in
 // registers for all its rows (its columns never change) and the next row's
-// loads issued before this row's arithmetic. Two blocks an SM.
-template <class T, int CPL>
+// loads issued before this row's arithmetic. Two blocks an SM. SW (rows of
+// more than 768 columns, whose weights would not fit the registers): the
+// weights in shared memory, read as 16-byte vectors.
+template <class T, int CPL, bool SW = false>
 __global__ void __launch_bounds__(256, 2) ln_reg_kernel(const T *__restrict__ src, T *dst,
                                                         const float *__restrict__ ln_w,
                                                         const float *__restrict__ ln_b, int tokens, int h, float eps) {
     using V = Vec<T>;
     constexpr int N = V::N;
+    static_assert(N % 4 == 0, "16-byte vectors of F32 weights");
     const int lane = threadIdx.x & 31;
     const int chunks = h / N;
-    float w[CPL][N], b[CPL][N];
+    __shared__ __align__(16) float wb_s[SW ? 2 * 1024 : 4];
+    float w[SW ? 1 : CPL][N], b[SW ? 1 : CPL][N];
+    if constexpr (SW) {
+        for (int i = threadIdx.x; i < h; i += blockDim.x) {
+            wb_s[i] = ln_w[i];
+            wb_s[1024 + i] = ln_b ? ln_b[i] : 0.0f;
+        }
+        __syncthreads();
+    } else {
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-        const int c = lane + 32 * i;
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-            w[i][j] = c < chunks ? ln_w[c * N + j] : 0.0f;
-            b[i][j] = c < chunks && ln_b ? ln_b[c * N + j] : 0.0f;
+            for (int j = 0; j < N; ++j) {
+                w[i][j] = c < chunks ? ln_w[c * N + j] : 0.0f;
+                b[i][j] = c < chunks && ln_b ? ln_b[c * N + j] : 0.0f;
+            }
         }
     }
     pdl_wait();
@@ -229,8 +241,21 @@ __global__ void __launch_bounds__(256, 2) ln_reg_kernel(const T *__restrict__ sr
             const int c = lane + 32 * i;
             if (c < chunks) {
                 float o[N];
+                if constexpr (SW) {
+                    const float4 *w4 = reinterpret_cast<const float4 *>(wb_s + c * N);
+                    const float4 *b4 = reinterpret_cast<const float4 *>(wb_s + 1024 + c * N);
 #pragma unroll
-                for (int j = 0; j < N; ++j) o[j] = (float)((cur[i][j] - mean) * inv) * w[i][j] + b[i][j];
+                    for (int q = 0; q < N / 4; ++q) {
+                        const float4 ww = w4[q], bb = b4[q];
+                        o[4 * q] = (float)((cur[i][4 * q] - mean) * inv) * ww.x + bb.x;
+                        o[4 * q + 1] = (float)((cur[i][4 * q + 1] - mean) * inv) * ww.y + bb.y;
+                        o[4 * q + 2] = (float)((cur[i][4 * q + 2] - mean) * inv) * ww.z + bb.z;
+                        o[4 * q + 3] = (float)((cur[i][4 * q + 3] - mean) * inv) * ww.w + bb.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < N; ++j) o[j] = (float)((cur[i][j] - mean) * inv) * w[i][j] + b[i][j];
+                }
                 V::store(out + c * N, o);
             }
         }
@@ -399,7 +424,8 @@ cudaError_t ln_launch(const void *src, void *dst, const float *w, const float *b
         if (cpl <= 1) return launch_pdl(ln_reg_kernel<T, 1>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
         if (cpl <= 2) return launch_pdl(ln_reg_kernel<T, 2>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
         if (cpl <= 3) return launch_pdl(ln_reg_kernel<T, 3>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
-        // Wider rows would spill their weights: the shared-memory kernel.
+        // Wider rows (up to 1024 columns) keep their weights in shared memory.
+        if (cpl <= 4 && h <= 1024) return launch_pdl(ln_reg_kernel<T, 4, true>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
     }
     // Resident blocks only (3 of 256 threads an SM at 78 registers), each
     // warp streaming rows.
