@@ -54,7 +54,6 @@ using namespace tc;
 constexpr int QT = 128, KT = 64, D = 64;
 constexpr int Q_BYTES = QT * D * 2;   // 16 KB
 constexpr int KV_BYTES = KT * D * 2;  // 8 KB
-constexpr int P_BYTES = QT * KT * 2;  // 16 KB
 constexpr int SMEM = Q_BYTES + 4 * KV_BYTES + 256 + 1024;  // Q, K [2], V [2]; P lives in TMEM
 constexpr int CTAS_PER_SM = 4;
 constexpr int KB2 = 4, VB2 = 4;  // attn_tc2's K and V buffers (loads run up to 4 chunks ahead)
@@ -121,27 +120,25 @@ __device__ __forceinline__ void key_range(int len, int q0, int window, int &klo,
     }
 }
 
-// The four barriers between one softmax warpgroup and the MMA issuer: S
-// done (commit), S held in registers (128 arrivals), P written (128
-// arrivals), P V done (commit).
+// The three barriers between one softmax warpgroup and the MMA issuer: S
+// done (commit), P written (128 arrivals), P V done (commit).
 struct SoftBars {
-    uint32_t s, sf, p, o;
+    uint32_t s, p, o;
 };
 
 // One softmax warpgroup's pass over one 128-query tile at q0 of item `it`:
 // chunks of keys [klo, khi); `g` counts this warpgroup's chunks (barrier
 // phases) and advances by the tile's chunk count. lane_base addresses this
 // warp's TMEM lanes at the tile's S columns; O sits o_off columns further.
-// r is the thread's query row in the tile; rowp its 128-byte row of the
-// tile's P operand. Returns false when the kernel must stop.
-// PT (attn_tc2): P goes into TMEM over the chunk's own S columns (the A
-// operand of P V, read from TMEM), so S is not released early and nothing
-// waits for the previous P V: when S(j) is complete, the commit that
-// signalled it also covers P V(j - 1), issued before it.
-template <class T, bool PT = false>
+// r is the thread's query row in the tile. Returns false when the kernel
+// must stop. P goes into TMEM over the chunk's own S columns (the A operand
+// of P V, read from TMEM), so nothing waits for the previous P V: when S(j)
+// is complete, the commit that signalled it also covers P V(j - 1), which
+// the MMA thread issued before it.
+template <class T>
 __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo, int khi, int window, int head,
                                              T *__restrict__ ctx, int h, const uint8_t *__restrict__ live,
-                                             float scale_log2, uint32_t lane_base, uint32_t o_off, uint8_t *rowp, int r,
+                                             float scale_log2, uint32_t lane_base, uint32_t o_off, int r,
                                              const SoftBars &b, uint32_t &g, volatile int *abort_flag, int *fault) {
     const int lane = threadIdx.x & 31;
     const int nch = (khi - klo + KT - 1) / KT;
@@ -178,10 +175,6 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo
 #pragma unroll
             for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
         }
-        if constexpr (!PT) {
-            tc_fence_before();
-            mbar_arrive(b.sf);
-        }
         // Invalid keys (masked, past the row, outside the window) become
         // -inf; the row max of the valid raw scores (the scale is positive,
         // so it is applied once after).
@@ -204,11 +197,6 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo
         for (int k = 0; k < 4; ++k) m4[k] = fmaxf(m4[k], sv[60 + k]);
         float mx = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
         mx = mx == -INFINITY ? mx : mx * scale_log2;
-        // P smem and O are free once the previous chunk's P V is done.
-        if (!PT && j > 0) {
-            if (!mbar_wait(b.o, (g - 1) & 1, abort_flag, fault)) return false;
-            tc_fence_after();
-        }
         // A row whose max passed m_ref by more than RESCALE moves m_ref; the
         // warp rescales O in TMEM (warp-wide, factor 1 for the rows that
         // keep theirs) when any of its rows moved.
@@ -250,30 +238,14 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int q0, int klo
         float rs, rs1;
         upk2(add2(add2(s4[0], s4[1]), add2(s4[2], s4[3])), rs, rs1);
         rs += rs1;
-        if constexpr (PT) {
-            // P as 32 columns of packed pairs over this chunk's S columns
-            // (packed in place: pair i reads sv[2i], sv[2i + 1], i <= 2i).
+        // P as 32 columns of packed pairs over this chunk's S columns
+        // (packed in place: pair i reads sv[2i], sv[2i + 1], i <= 2i).
 #pragma unroll
-            for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(pack2<T>(sv[2 * i], sv[2 * i + 1]));
-            tmem_st32(lane_base, sv);  // waits for the store
-            l += rs;
-            tc_fence_before();
-            mbar_arrive(b.p);
-        } else {
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                uint4 w;
-                w.x = pack2<T>(sv[8 * cc + 0], sv[8 * cc + 1]);
-                w.y = pack2<T>(sv[8 * cc + 2], sv[8 * cc + 3]);
-                w.z = pack2<T>(sv[8 * cc + 4], sv[8 * cc + 5]);
-                w.w = pack2<T>(sv[8 * cc + 6], sv[8 * cc + 7]);
-                *reinterpret_cast<uint4 *>(rowp + ((cc ^ (r & 7)) << 4)) = w;
-            }
-            l += rs;
-            fence_async_smem();
-            tc_fence_before();
-            mbar_arrive(b.p);
-        }
+        for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(pack2<T>(sv[2 * i], sv[2 * i + 1]));
+        tmem_st32(lane_base, sv);  // waits for the store
+        l += rs;
+        tc_fence_before();
+        mbar_arrive(b.p);
     }
     if (!mbar_wait(b.o, (g - 1) & 1, abort_flag, fault)) return false;
     tc_fence_after();
@@ -448,14 +420,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         // Softmax: thread r = query row r = TMEM lane r.
         const int r = threadIdx.x;
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        const SoftBars sb{bar_s, 0u, bar_p, bar_o};  // no S release: P goes over S in TMEM
+        const SoftBars sb{bar_s, bar_p, bar_o};
         uint32_t g = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
             const AttnItem it = items[u / heads];
             int klo, khi;
             key_range(it.len, it.q0, window, klo, khi);
-            if (!softmax_tile<T, true>(it, it.q0, klo, khi, window, u % heads, ctx, h, live, scale_log2, lane_base,
-                                       64, nullptr, r, sb, g, abort_flag, fault))
+            if (!softmax_tile<T>(it, it.q0, klo, khi, window, u % heads, ctx, h, live, scale_log2, lane_base, 64, r,
+                                 sb, g, abort_flag, fault))
                 break;
         }
     }
@@ -486,7 +458,7 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                    bar_vf = bar_v + 8 * VB2;
     auto tile_bars = [&](int t) {
         const uint32_t x = bar_vf + 8 * VB2 + 32 * t;
-        return SoftBars{x, x + 8, x + 16, x + 24};
+        return SoftBars{x, x + 8, x + 16};
     };
     uint32_t *tmem_slot = (uint32_t *)(bars + 16 + 16 * (KB2 + VB2) + 64);
     volatile int *abort_flag = (volatile int *)(bars + 16 + 16 * (KB2 + VB2) + 72);
@@ -508,7 +480,6 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         for (int i = 0; i < 2; ++i) {
             const SoftBars tb = tile_bars(i);
             mbar_init(tb.s, 1);
-            mbar_init(tb.sf, 128);
             mbar_init(tb.p, 128);
             mbar_init(tb.o, 1);
         }
@@ -653,8 +624,8 @@ attn_tc2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
             const AttnItem it = items[u / heads];
             const int q0 = it.q0 + t * QT;
             if (q0 >= it.len) continue;  // a unit with one tile
-            if (!softmax_tile<T, true>(it, q0, 0, it.len, -1, u % heads, ctx, h, live, scale_log2, lane_base, 128,
-                                       nullptr, r, sb, g, abort_flag, fault))
+            if (!softmax_tile<T>(it, q0, 0, it.len, -1, u % heads, ctx, h, live, scale_log2, lane_base, 128, r, sb, g,
+                                 abort_flag, fault))
                 break;
         }
     }
