@@ -151,6 +151,25 @@ def test_tcgen05_gemm_prenorm_layernorm_writes_sum_and_norm(dtype, shape):
     assert rel_err(got, want) < (1.2e-2 if dtype == BF16 else 2e-3)
 
 
+@pytest.mark.parametrize("variant", [0, 1])
+def test_gated_product_saturates_at_the_f16_maximum(variant):
+    # A gated middle past the F16 range stores +-65504, not infinity (the
+    # reference's gated epilogue, core/cuda/rotary.cuh:31-46); below it the
+    # products are the narrowed operands' (tensor-core kernel 0, FFMA 1).
+    M, N, K = 300, 512, 256
+    rng = np.random.default_rng(4242)
+    a = rng.standard_normal((M, K), np.float32) * 4
+    w = rng.standard_normal((N, K), np.float32) * np.float32(40 / np.sqrt(K))
+    bias = np.zeros(N, np.float32)
+    got = runtime.gemm_check(F16, variant, 3, a, w, bias, None)
+    want = ref_gemm(F16, 3, a, w, bias, None)
+    big = np.abs(want) > 65504 * 1.01
+    assert big.sum() > 100 and np.isfinite(got).all()
+    assert np.array_equal(got[big], np.sign(want[big]) * 65504)
+    small = np.abs(want) < 65504 * 0.99
+    assert np.abs(got[small] - want[small]).max() <= 2e-3 * 65504
+
+
 @pytest.mark.parametrize("epi", [0, 1, 2, 3])
 def test_ffma_gemm_f32_is_one_chain_over_k(epi):
     M, N, K = 150, 160, 200

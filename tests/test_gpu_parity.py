@@ -73,6 +73,11 @@ def test_tiny_xlmr_position_offset(ctx, precision):
     s = m.session(8, 64, precision)
     got = s.embed(a["ids"], a["mask"])
     check(got, a["embeddings"], precision, "tiny-xlmr vs transformers")
+    if precision == EXACT:
+        # The reference's EXACT bound against arithmetic in F64
+        # (core/tests/cuda_runs.rs:68): |got - w| <= 1e-5 (1 + |w|).
+        want = a["embeddings"].astype(np.float64)
+        assert np.all(np.abs(got - want) <= 1e-5 * (1 + np.abs(want))), np.abs(got - want).max()
     s.release()
     m.release()
 
@@ -178,6 +183,43 @@ def test_bf16_model_runs_in_bf16(ctx):
     got = s.embed(ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
     want = oracle.encode(d, ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
     check(got, want, MODEL, "bf16 rerank body")
+    s.release()
+    m.release()
+
+
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_one_long_row_among_many_short_ones(ctx, precision):
+    # Packing stress: a 500-token row with forty rows of 1..11 tokens (the
+    # reference's cuda_kernels.rs case), CLS pooling, against the oracle.
+    d = models.synthetic("bert-base", 1, layers=2)
+    rng = np.random.default_rng(5)
+    lens = np.array([500] + list(rng.integers(1, 12, size=40)))
+    ids = np.zeros((len(lens), 512), np.int32)
+    mask = np.zeros_like(ids)
+    for r, n in enumerate(lens):
+        ids[r, :n] = rng.integers(1000, 30000, size=n)
+        ids[r, 0] = 101
+        mask[r, :n] = 1
+    m = ctx.load(d)
+    s = m.session(len(lens), 512, precision)
+    got = s.embed(ids, mask, pooling=abi.TURBO_POOLING_CLS)
+    want = oracle.encode(d, ids, mask, pooling=abi.TURBO_POOLING_CLS)
+    check(got, want, precision, "one long row, many short")
+    s.release()
+    m.release()
+
+
+def test_f32_attention_past_4096_keys(ctx):
+    # EXACT attention over a 4,500-token row (ModernBERT's first layer is
+    # global): the F32 sums past 4,096 keys (the reference's
+    # cuda_rotary.rs:381 case), against the oracle.
+    d = models.synthetic("modernbert-base", 7, layers=1)
+    ids, mask, lens = models.rows_long(11, 1, 4500, 4500, 4500, 100, 50367)
+    m = ctx.load(d)
+    s = m.session(1, 4500, EXACT)
+    got = s.embed(ids, mask)
+    want = oracle.encode(d, ids, mask)
+    check(got, want, EXACT, "modernbert EXACT, 4,500 keys")
     s.release()
     m.release()
 

@@ -1,6 +1,7 @@
 // common.cuh -- element types, conversions and warp reductions shared by the
 // B200 kernels. Everything here is sm_100a device code or plain host code.
 #pragma once
+#include <type_traits>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -182,6 +183,15 @@ __device__ __forceinline__ void gelu_erf_fast2(float &x0, float &x1) {
     upk2(fma2(pk2(-1.0f, -1.0f), mul2(p, pk2(e0, e1)), pk2(1.0f, 1.0f)), a0, a1);
     const uint64_t hx = mul2(pk2(x0, x1), pk2(0.5f, 0.5f));
     upk2(fma2(hx, pk2(copysignf(a0, x0), copysignf(a1, x1)), hx), x0, x1);
+}
+
+// The gated product act(gate) * up as an F16 output stores it: saturated at
+// +-65504 instead of rounding to infinity (a NaN stays NaN), as the
+// reference CUDA backend's gated epilogue does (core/cuda/rotary.cuh:31-46);
+// other output types keep the product.
+template <class T> __device__ __forceinline__ float gated_out(float v) {
+    if constexpr (std::is_same<T, __half>::value) return v > 65504.0f ? 65504.0f : (v < -65504.0f ? -65504.0f : v);
+    return v;
 }
 
 // GELU in its tanh form, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),

@@ -279,8 +279,8 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                     } else {
                         gelu_erf_fast2(g0, g1);
                     }
-                    o[hh * 16 + i] = g0 * u0;
-                    o[hh * 16 + i + 1] = g1 * u1;
+                    o[hh * 16 + i] = gated_out<T>(g0 * u0);
+                    o[hh * 16 + i + 1] = gated_out<T>(g1 * u1);
                 }
             stage_store32<T>(o, col / 2, ss, out_map);
             continue;
@@ -317,8 +317,8 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                     } else {
                         gelu_erf_fast2(g0, g1);
                     }
-                    o[i] = g0 * v[2 * i + 1];
-                    o[i + 1] = g1 * v[2 * i + 3];
+                    o[i] = gated_out<T>(g0 * v[2 * i + 1]);
+                    o[i + 1] = gated_out<T>(g1 * v[2 * i + 3]);
                 }
                 store_n<T, 16>((T *)e.out + (int64_t)row * e.ldo + col / 2, o);
                 continue;
