@@ -209,6 +209,32 @@ def test_one_long_row_among_many_short_ones(ctx, precision):
     m.release()
 
 
+@pytest.mark.parametrize("name,vocab", [("bert-base", 30522), ("modernbert-base", 50368)])
+@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+def test_left_padded_rows_stay_finite_and_match(ctx, name, vocab, precision):
+    # Rows whose first tokens are padding (mask 0): masked keys inside the
+    # packed row, mean pooling over the live ones (and for BERT CLS, which
+    # reads column 0 whatever its mask), as the reference's awkward rows.
+    d = models.synthetic(name, 12, layers=2)
+    rng = np.random.default_rng(12)
+    lens = np.array([60, 130, 17, 90])
+    pads = np.array([5, 0, 9, 40])
+    ids = np.zeros((len(lens), 160), np.int32)
+    mask = np.zeros_like(ids)
+    for r, (n, p) in enumerate(zip(lens, pads)):
+        ids[r, p:p + n] = rng.integers(1000, vocab - 1, size=n)
+        mask[r, p:p + n] = 1
+    m = ctx.load(d)
+    s = m.session(len(lens), 160, precision)
+    poolings = [abi.TURBO_POOLING_MEAN] + ([abi.TURBO_POOLING_CLS] if name == "bert-base" else [])
+    for pooling in poolings:
+        got = s.embed(ids, mask, pooling=pooling)
+        assert np.isfinite(got).all()
+        check(got, oracle.encode(d, ids, mask, pooling=pooling), precision, f"left-padded {name}")
+    s.release()
+    m.release()
+
+
 def test_f32_attention_past_4096_keys(ctx):
     # EXACT attention over a 4,500-token row (ModernBERT's first layer is
     # global): the F32 sums past 4,096 keys (the reference's
