@@ -74,6 +74,14 @@ TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t variant, uint32
  * cluster of N / 256 CTA pairs exchanging row statistics):
  * y_out = LN(y_in + a w^T + bias) * ln_w + ln_b with LayerNorm epsilon eps,
  * host F32 operands narrowed to dtype (F16 or BF16), y_out widened back. */
+/* embed_write for rows already in device memory (ids, mask and types
+ * [batch, row_stride] i32 device pointers; types may be NULL): the same
+ * checks and the same plan as embed_write, built on the device, so nothing
+ * crosses PCIe but 20 bytes of sizes. No ranges or taps. The reference's
+ * CUDA backend refuses device rows (core/cuda/backend.cpp:3367-3368). */
+TB_EXPORT int32_t turbo_b200_embed_write_device(void *session, const turbo_backend_embed_rows *rows,
+                                                turbo_error *err);
+
 TB_EXPORT int32_t turbo_b200_gemm_ln_check(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K, const float *a,
                                            const float *w, const float *bias, const float *y_in, const float *ln_w,
                                            const float *ln_b, float eps, float *y_out, turbo_error *err);

@@ -220,6 +220,9 @@ struct Session {
     bool exact_tf32 = false;  // F32 sessions: GEMMs on kind::tf32 x3 (else FFMA)
     uint64_t h2d_bytes = 0;
     std::vector<int32_t> row_start, row_len;
+    // Packing rows that are in device memory (turbo_b200_embed_write_device):
+    // the device scratch (6 x max_batch + 8 i32) and the counts read back.
+    int32_t *pack_dev = nullptr, *pack_counts = nullptr;
     // Device time of the last run (events on the context's stream), and,
     // when profiling, of each GEMM and attention launch in it.
     cudaEvent_t run0 = nullptr, run1 = nullptr;
@@ -236,9 +239,10 @@ struct Session {
     ~Session() {
         DeviceScope ds(ctx->device);
         for (void *p : {x, xn, qkv, ctxb, ffn, (void *)plan_dev, (void *)head_wt, (void *)head_bp, (void *)head_wc,
-                        (void *)head_scores})
+                        (void *)head_scores, (void *)pack_dev})
             cudaFree(p);
         if (plan_host) cudaFreeHost(plan_host);
+        if (pack_counts) cudaFreeHost(pack_counts);
         if (uploaded) cudaEventDestroy(uploaded);
         if (run0) cudaEventDestroy(run0);
         if (run1) cudaEventDestroy(run1);
@@ -810,6 +814,8 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
     if (e == cudaSuccess) e = alloc(&s->ffn, rows * I * es);
     if (e == cudaSuccess) e = alloc((void **)&s->plan_dev, s->lay.total);
     if (e == cudaSuccess) e = cudaHostAlloc((void **)&s->plan_host, s->lay.total, cudaHostAllocDefault);
+    if (e == cudaSuccess) e = alloc((void **)&s->pack_dev, (6 * (size_t)s->max_batch + 8) * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaHostAlloc((void **)&s->pack_counts, 8 * sizeof(int32_t), cudaHostAllocDefault);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->uploaded, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreate(&s->run0);
     if (e == cudaSuccess) e = cudaEventCreate(&s->run1);
@@ -1029,6 +1035,61 @@ int32_t tb_embed_write_ranges(void *p, const turbo_backend_embed_rows *r, const 
                               uint32_t count, turbo_error *err) {
     if (count == 0) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "count of 0 ranges");
     return write_rows((Session *)p, r, ranges, count, err);
+}
+
+// Rows in device memory: the same checks and plan as write_rows (no ranges
+// or taps), the plan built on the device (pack_rows_device) and its sizes
+// read back (20 bytes, the only copy).
+int32_t write_rows_device(Session *s, const turbo_backend_embed_rows *r, turbo_error *err) {
+    s->written = false;
+    if (r->batch == 0 || r->seq == 0 || !r->ids || !r->mask)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "rows need batch, seq, ids and mask");
+    if ((int)r->batch > s->max_batch || (int)r->seq > s->max_seq)
+        return fail(err, TURBO_E_CAPACITY, 0, "batch %u x seq %u over the session's %d x %d", r->batch, r->seq,
+                    s->max_batch, s->max_seq);
+    if (r->taps > 1 || r->tap_alone) return fail(err, TURBO_E_UNSUPPORTED_OPTION, 9, "taps take host rows");
+    if (r->head) return fail(err, TURBO_E_UNSUPPORTED_OPTION, 0, "a token head is not built");
+    const int h = s->m->hidden;
+    const uint32_t od = r->output_dim ? r->output_dim : (uint32_t)h;
+    if (od > (uint32_t)h) return fail(err, TURBO_E_INVALID_ARGUMENT, 6, "output_dim %u over hidden %d", od, h);
+    const uint32_t stride = r->row_stride ? r->row_stride : r->seq;
+    Context *c = s->ctx;
+    DeviceScope ds(c->device);
+    DeviceRows dr;
+    dr.ids = r->ids, dr.mask = r->mask, dr.types = r->types;
+    dr.batch = (int)r->batch, dr.seq = (int)r->seq, dr.stride = (int)stride;
+    dr.pool_mode = r->pooling == TURBO_POOLING_CLS ? 1 : (r->pooling == TURBO_POOLING_LAST ? 2 : 0);
+    DevicePlan dp;
+    dp.qt = attention_queries(s), dp.q2 = ATTN_TC2_QUERIES, dp.allow_pairs = s->max_attn2_items > 0;
+    const size_t B = (size_t)s->max_batch;
+    dp.len = s->pack_dev, dp.start = dp.len + B, dp.holes = dp.start + B, dp.item0 = dp.holes + B;
+    dp.item2 = dp.item0 + B, dp.order = dp.item2 + B, dp.counts = dp.order + B;
+    uint8_t *D = s->plan_dev;
+    dp.tok_id = (int32_t *)(D + s->lay.tok_id), dp.tok_type = (int32_t *)(D + s->lay.tok_type);
+    dp.tok_pos = (int32_t *)(D + s->lay.tok_pos), dp.tok_live = D + s->lay.tok_live;
+    dp.attn = (AttnItem *)(D + s->lay.attn), dp.attn2 = (AttnItem *)(D + s->lay.attn2);
+    dp.pool = (PoolItem *)(D + s->lay.pool);
+    CK(pack_rows_device(dr, dp, c->stream), "embed_write_device");
+    CK(cudaMemcpyAsync(s->pack_counts, dp.counts, 5 * sizeof(int32_t), cudaMemcpyDeviceToHost, c->stream),
+       "embed_write_device");
+    CK(cudaStreamSynchronize(c->stream), "embed_write_device");
+    const int32_t *k = s->pack_counts;
+    if (k[4]) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "mask row %d has no 1: a row needs a token", k[4] - 1);
+    const uint32_t L = (uint32_t)s->m->layers;
+    s->h2d_bytes = 0;
+    s->tokens = k[0];
+    s->batch = (int)r->batch;
+    s->n_vectors = (int)r->batch;
+    s->n_attn = k[1];
+    s->n_attn2 = k[2];
+    s->max_len = k[3];
+    s->normalize = r->normalize;
+    s->output_dim = od;
+    s->taps = 1;
+    s->layers_run = (int)L;
+    s->written = true;
+    ok(err);
+    return TURBO_OK;
 }
 
 // With profiling on, an event pair around a launch (kind 0 GEMM, 1 attention).
@@ -1429,6 +1490,14 @@ TB_EXPORT const char *turbo_cuda_arch_label(void) { return "b200"; }
 TB_EXPORT uint64_t turbo_b200_kernel_launches(void) { return launch_counter().load(); }
 
 TB_EXPORT const turbo_backend *turbo_b200_backend(void) { return &turbo_cuda_backend; }
+
+TB_EXPORT int32_t turbo_b200_embed_write_device(void *session, const turbo_backend_embed_rows *rows,
+                                                turbo_error *err) {
+    return guarded(err, [&]() -> int32_t {
+        if (!session || !rows) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "a session and rows are required");
+        return write_rows_device((Session *)session, rows, err);
+    });
+}
 
 TB_EXPORT int32_t turbo_b200_session_set_head(void *session, const float *pooler_w, const float *pooler_b,
                                               const float *cls_w, float cls_b, turbo_error *err) {

@@ -71,6 +71,29 @@ struct AttnItem {
     int32_t start, len, q0, holes;
 };
 
+// Rows already in device memory ([batch, stride] i32; types may be null)
+// and how each row pools: 0 the mean over its live tokens, 1 column 0
+// (CLS), 2 its last token.
+struct DeviceRows {
+    const int32_t *ids = nullptr, *mask = nullptr, *types = nullptr;
+    int batch = 0, seq = 0, stride = 0, pool_mode = 0;
+};
+// The session's plan arrays (device) and the packing scratch: len, start,
+// holes, item0, item2, order [max_batch] each, counts [5] = tokens,
+// attention items, two-tile items, longest row, first empty row + 1.
+struct DevicePlan {
+    int qt = 0, q2 = 0, allow_pairs = 0;
+    int32_t *len = nullptr, *start = nullptr, *holes = nullptr, *item0 = nullptr, *item2 = nullptr,
+            *order = nullptr, *counts = nullptr;
+    int32_t *tok_id = nullptr, *tok_type = nullptr, *tok_pos = nullptr;
+    uint8_t *tok_live = nullptr;
+    AttnItem *attn = nullptr, *attn2 = nullptr;
+    PoolItem *pool = nullptr;
+};
+// The plan embed_write builds on the host, built on the device from rows in
+// device memory (devrows.cu); counts then tell the host its sizes.
+cudaError_t pack_rows_device(const DeviceRows &r, const DevicePlan &p, cudaStream_t s);
+
 // dst[i] = src[i] narrowed from F32 to F16 or BF16 (round to nearest even).
 cudaError_t narrow(Dt dt, const float *src, void *dst, int64_t n, cudaStream_t s);
 

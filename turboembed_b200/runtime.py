@@ -204,6 +204,22 @@ class Session:
         _check(self.t.embed_write(self.h, C.byref(r), C.byref(err)), err, "embed_write")
         self._out_dim, self._count = r.output_dim, r.batch
 
+    def write_device(self, ids_ptr, mask_ptr, types_ptr, batch, seq, pooling=abi.TURBO_POOLING_MEAN,
+                     normalize=abi.TURBO_NORMALIZE_L2, output_dim=0):
+        """turbo_b200_embed_write_device: rows already in device memory
+        ([batch, seq] i32 at the given device addresses; types may be 0)."""
+        lib = library()
+        f = lib.turbo_b200_embed_write_device
+        f.argtypes = [C.c_void_p, C.POINTER(abi.turbo_backend_embed_rows), C.POINTER(abi.turbo_error)]
+        i32 = C.POINTER(C.c_int32)
+        r = abi.turbo_backend_embed_rows(C.sizeof(abi.turbo_backend_embed_rows), batch, seq, seq,
+                                         C.cast(C.c_void_p(ids_ptr), i32), C.cast(C.c_void_p(mask_ptr), i32),
+                                         C.cast(C.c_void_p(types_ptr), i32) if types_ptr else None, pooling,
+                                         normalize, output_dim or self.hidden, 0, 0, 0)
+        err = abi.new_error()
+        _check(f(self.h, C.byref(r), C.byref(err)), err, "embed_write_device")
+        self._out_dim, self._count = r.output_dim, r.batch
+
     def write_ranges(self, ids, mask, ranges, types=None, normalize=abi.TURBO_NORMALIZE_L2, output_dim=0, taps=0,
                      tap_alone=0):
         """embed_write_ranges; taps T > 1 pools each range from each of the
