@@ -18,6 +18,9 @@ the encoder (and, for c3, the rerank head) over one batch.
   e2e    the same metric through the C table with host buffers: each step is
          embed_write (host rows, packing, H2D) + session_run + buffer_read
          (D2H of the vectors, or of the scores for c3), wall-clock.
+  e2e_device_rows  the same with the rows already in device memory
+         (turbo_b200_embed_write_device: packing on the device, no H2D);
+         row writes only (null for range writes and the device head).
 Under torchrun (N > 1) one seeded global batch of N times the per-GPU rows is
 sharded by cost (longest-processing-time, turboembed_b200/shard.py) and each
 rank runs its rows on its own GPU (weak scaling: no collective on the data
@@ -431,6 +434,29 @@ def main():
     h2d = int(run.h2d_bytes)
     d2h = int(res.nbytes)
 
+    # The same with the rows already in device memory
+    # (turbo_b200_embed_write_device: the plan built on the device, nothing
+    # staged through the host): row writes only.
+    e2e_dev = None
+    if ranges is None and not wl.head:
+        import torch
+        dev = [torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(f"cuda:{local}") if a is not None else None
+               for a in (ids, mask, types)]
+        torch.cuda.synchronize(local)
+        dt_dev = []
+        barrier()
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            sess.write_device(dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr() if dev[2] is not None else 0,
+                              ids.shape[0], ids.shape[1], pooling=wl.pooling, normalize=wl.normalize)
+            run_d = sess.run()
+            res_d = sess.read()
+            if i >= args.warmup:
+                dt_dev.append(time.perf_counter() - t0)
+        barrier()
+        e2e_dev = {"value": tokens_all * args.steps / max_over_ranks(sum(dt_dev)), "unit": "tokens/s",
+                   "h2d_bytes_per_step": int(run_d.h2d_bytes), "d2h_bytes_per_step": int(res_d.nbytes)}
+
     # The optional all-gather of the pooled vectors into one device buffer
     # on every rank (NCCL over NVLink), once, outside the timed steps.
     n_vec = len(ranges) if ranges is not None else len(mine)
@@ -480,6 +506,7 @@ def main():
                          "between_kernels_ms_per_step": (p_run - g_ms - a_ms - o_ms) / 3,
                          "launches_per_step": g_n // 3},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e_device_rows": e2e_dev,
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
