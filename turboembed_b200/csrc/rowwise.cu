@@ -266,6 +266,97 @@ __global__ void __launch_bounds__(256, 2) ln_reg_kernel(const T *__restrict__ sr
     }
 }
 
+// 16-bit rows of up to 1024 columns: as ln_reg_kernel<T, 4, true> (the same
+// sums in the same order, so the same bits), with the row and the prefetched
+// next row kept packed (16 registers each, unpacked for each pass) so that
+// three blocks fit an SM and more rows are in flight.
+template <class T>
+__global__ void __launch_bounds__(256, 3) ln_pk_kernel(const T *__restrict__ src, T *dst, const float *__restrict__ ln_w,
+                                                       const float *__restrict__ ln_b, int tokens, int h, float eps) {
+    constexpr int CPL = 4, N = 8;
+    const int lane = threadIdx.x & 31;
+    const int chunks = h / N;
+    __shared__ __align__(16) float wb_s[2 * 1024];
+    for (int i = threadIdx.x; i < h; i += blockDim.x) {
+        wb_s[i] = ln_w[i];
+        wb_s[1024 + i] = ln_b ? ln_b[i] : 0.0f;
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    uint4 cur[CPL], nxt[CPL];
+    auto load = [&](int tok, uint4 *v) {
+        const uint4 *in = reinterpret_cast<const uint4 *>(src + (int64_t)tok * h);
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            v[i] = c < chunks ? in[c] : make_uint4(0, 0, 0, 0);
+        }
+    };
+    auto unpack = [](const uint4 &u, float *f) {
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 p = unpack2<T>(w[j]);
+            f[2 * j] = p.x, f[2 * j + 1] = p.y;
+        }
+    };
+    if (t < tokens) load(t, cur);
+    for (; t < tokens; t += warps) {
+        if (t + warps < tokens) load(t + warps, nxt);
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i)
+            if (lane + 32 * i < chunks) {
+                float f[N];
+                unpack(cur[i], f);
+#pragma unroll
+                for (int j = 0; j < N; ++j) s += f[j];
+            }
+        const float mean = warp_sum(s) / (float)h;
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i)
+            if (lane + 32 * i < chunks) {
+                float f[N];
+                unpack(cur[i], f);
+#pragma unroll
+                for (int j = 0; j < N; ++j) {
+                    const float d = f[j] - mean;
+                    q += d * d;
+                }
+            }
+        const float inv = 1.0f / sqrt(warp_sum(q) / (float)h + eps);
+        uint4 *out = reinterpret_cast<uint4 *>(dst + (int64_t)t * h);
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+                float f[N];
+                unpack(cur[i], f);
+                const float4 *w4 = reinterpret_cast<const float4 *>(wb_s + c * N);
+                const float4 *b4 = reinterpret_cast<const float4 *>(wb_s + 1024 + c * N);
+                uint32_t o[4];
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) {
+                    const float4 ww = w4[qq], bb = b4[qq];
+                    const float o0 = (float)((f[4 * qq] - mean) * inv) * ww.x + bb.x;
+                    const float o1 = (float)((f[4 * qq + 1] - mean) * inv) * ww.y + bb.y;
+                    const float o2 = (float)((f[4 * qq + 2] - mean) * inv) * ww.z + bb.z;
+                    const float o3 = (float)((f[4 * qq + 3] - mean) * inv) * ww.w + bb.w;
+                    o[2 * qq] = pack2<T>(o0, o1);
+                    o[2 * qq + 1] = pack2<T>(o2, o3);
+                }
+                out[c] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) cur[i] = nxt[i];
+    }
+}
+
 // One block per output vector. Each thread owns columns tid, tid + blockDim,
 // .. of the cut and sums its tokens in column (position) order, as the
 // reference's mean does; L2 in F64 over the block.
@@ -425,7 +516,9 @@ cudaError_t ln_launch(const void *src, void *dst, const float *w, const float *b
         if (cpl <= 2) return launch_pdl(ln_reg_kernel<T, 2>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
         if (cpl <= 3) return launch_pdl(ln_reg_kernel<T, 3>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
         // Wider rows (up to 1024 columns) keep their weights in shared memory.
-        if (cpl <= 4 && h <= 1024) return launch_pdl(ln_reg_kernel<T, 4, true>, g, 256, 0, s, in, out, w, b, tokens, h, fe);
+        if (cpl <= 4 && h <= 1024)
+            return launch_pdl(ln_pk_kernel<T>, std::min(148 * 3, (tokens + 7) / 8), 256, 0, s, in, out, w, b, tokens, h,
+                              fe);
     }
     // Resident blocks only (3 of 256 threads an SM at 78 registers), each
     // warp streaming rows.
