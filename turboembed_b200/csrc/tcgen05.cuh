@@ -209,9 +209,6 @@ __device__ __forceinline__ void cluster_sync() {
 }
 // Two floats into shared memory of a CTA of the cluster (a shared::cluster
 // address); a later release-arrive orders them before the arrival.
-__device__ __forceinline__ void st_cluster_v2(uint32_t cluster_addr, float a, float b) {
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(cluster_addr), "f"(a), "f"(b) : "memory");
-}
 // An asynchronous 8-byte store into a cluster peer's shared memory that
 // completes 8 bytes of transactions on the peer's mbarrier `cluster_bar`
 // (the peer arms it with expect_tx): no fence or wait on the sender.
