@@ -57,8 +57,9 @@ TB_EXPORT uint64_t turbo_b200_kernel_launches(void);
  * and narrowed to dtype (TURBO_DTYPE_F16 / BF16 / F32) first, run through
  * `variant` 0 (the tcgen05 kernel as the backend runs it: CTA pairs when N
  * is a multiple of 256), 1 (the FFMA kernel), 2 (the tcgen05 kernel on
- * single CTAs) or 3 (F32 only: the kind::tf32 kernel with the three-product
- * split, the EXACT tier's), the result
+ * single CTAs), 3 (F32 only: the kind::tf32 kernel with the three-product
+ * split, the EXACT tier's, tiles chosen by shape) or 4 (as 3 on CTA pairs,
+ * 256 x 256 tiles; N a multiple of 256), the result
  * widened back into y_out. epi is 0 store, 1 GELU, 2 residual (y_in holds
  * y's starting values), 3 gated (interleaved gate/up columns; y is
  * [M, N/2]), 4 RoPE on the columns below 2 * (N / 3) with head_dim, pos [M],

@@ -185,7 +185,8 @@ def test_ffma_gemm_f32_is_one_chain_over_k(epi):
     assert np.array_equal(got, runtime.gemm_check(F32, 1, epi, a, w, bias, y_in))
 
 
-@pytest.mark.parametrize("shape", [(150, 256, 200), (2000, 768, 3072), (77, 2304, 768), (513, 1536, 384)])
+@pytest.mark.parametrize("shape", [(150, 256, 200), (2000, 768, 3072), (77, 2304, 768), (513, 1536, 384),
+                                   (20011, 768, 768)])
 @pytest.mark.parametrize("epi", [0, 1, 2, 3])
 def test_tf32x3_gemm_has_f32_accuracy(shape, epi):
     # The EXACT tier's tensor-core GEMM: hi/lo TF32 split, three products,
@@ -202,6 +203,10 @@ def test_tf32x3_gemm_has_f32_accuracy(shape, epi):
     assert np.abs(got - want).max() < 1e-4 * max(1.0, np.abs(want).max())
     simt = runtime.gemm_check(F32, 1, epi, a, w, bias, y_in)
     assert np.abs(got - simt).max() < 1e-4 * max(1.0, np.abs(want).max())
+    # The same on CTA pairs (256 x 256 tiles, cta_group::2), which the EXACT
+    # sessions take for large token counts.
+    pair = runtime.gemm_check(F32, 4, epi, a, w, bias, y_in)
+    assert np.abs(pair - want).max() < 1e-4 * max(1.0, np.abs(want).max())
 
 
 def ref_attention(qkv, lens, live, heads, d, window):

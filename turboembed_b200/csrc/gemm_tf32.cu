@@ -7,16 +7,26 @@
 //   a w = a_hi w_hi + a_hi w_lo + a_lo w_hi   (+ a_lo w_lo, below F32 precision)
 // as three tcgen05.mma kind::tf32 products accumulated in F32 in TMEM.
 //
-// Design (one CTA per SM, persistent over 128 x 128 output tiles, 512
-// threads):
+// Design (persistent, 512 threads a CTA). PAIR = false: one CTA a 128 x 128
+// output tile. PAIR = true: a cluster of two CTAs a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (each CTA loads and splits its own 128 rows of A
+// and 128 rows of W; the leader issues the MMAs for both; each CTA's TMEM
+// holds its 128 rows of the accumulator). The pair does twice the MMA work
+// for each stage a CTA loads and splits.
 //   warp 0        TMA: A [128 x 32] and W [128 x 32] F32 tiles per k-block
 //                 (128-byte swizzle) into the hi halves of a 3-stage ring.
-//   warps 4..7    the split: in each stage hi = x with its low 13 mantissa
-//                 bits cleared (exactly a TF32 value, written back in place)
-//                 and lo = x - hi into the lo halves, same swizzled layout;
-//                 then a proxy fence and an arrival for the MMA.
+//   warps 4..7    the split: in each stage lo = x - hi into the lo halves
+//                 (same swizzled layout), hi = x with its low 13 mantissa
+//                 bits cleared; then a proxy fence and the arrival for the
+//                 MMA (pairs: one a CTA, on the leader's barrier, released
+//                 at cluster scope). hi is not written back: the tensor core
+//                 reads an F32 operand of kind::tf32 by its top 19 bits
+//                 (measured on B200: the products are bit-equal to those of
+//                 operands with the low 13 bits cleared in shared memory,
+//                 over 1.7e7 outputs; a rounding read would put the error
+//                 near 5e-4, which the F64 accuracy tests bound at 1e-4).
 //   warp 1        MMA: per k-block 4 steps of K = 8, three products each.
-//   warp 2        TMEM (2 x 128 columns: two accumulators).
+//   warp 2        TMEM (2 accumulators of 128 or 256 columns).
 //   warps 8..15   epilogue: bias / erf-GELU (erff) / residual / gating in
 //                 F32, 16-byte stores.
 // Waits are bounded (2 s) and end in the fault word, as in gemm_tc.cu.
@@ -30,16 +40,16 @@ namespace {
 
 using namespace tc;
 
-constexpr int TBM = 128, TBN = 128, TBK = 32, STAGES = 3;
+constexpr int TBM = 128, TBK = 32, STAGES = 3;  // TBM: rows of A (and of W) a CTA loads a stage
 constexpr int HALF_BYTES = TBM * TBK * 4;             // 16 KB: one [128 x 32] F32 tile
 constexpr int STAGE_BYTES = 4 * HALF_BYTES;           // A hi, A lo, W hi, W lo
 constexpr int MAX_BIAS = 4096;
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + MAX_BIAS * 4 + 1024;
 
 // kind::tf32 instruction descriptor: F32 accumulator, A and B TF32 (format
-// 2), both K-major, M = 128, N = TBN.
-__host__ __device__ constexpr uint32_t idesc_tf32() {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TBN >> 3) << 17) | ((uint32_t)(TBM >> 4) << 24);
+// 2), both K-major, M x N.
+template <int M, int N> __host__ __device__ constexpr uint32_t idesc_tf32() {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
@@ -48,10 +58,25 @@ __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t
             tmem_d),
         "l"(da), "l"(db), "r"(idesc), "r"(acc));
 }
+__device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                               uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+// Arrival on a cluster peer's barrier that releases this thread's (and, after
+// a CTA barrier, its CTA's) shared-memory writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 
+template <bool PAIR>
 __global__ void __launch_bounds__(512, 1)
 gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
                  Epilogue e, int *fault) {
+    constexpr int TN = PAIR ? 256 : 128;  // output columns a tile (TMEM columns an accumulator)
+    constexpr int TM = PAIR ? 256 : 128;  // output rows a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *bars = smem + STAGES * STAGE_BYTES;
@@ -63,32 +88,43 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
     for (int i = threadIdx.x; i < N && e.bias; i += blockDim.x) bias_s[i] = e.bias[i];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t pr = PAIR ? cluster_rank() : 0;  // this CTA's half of the pair (0: the leader)
+    const bool leader = pr == 0;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(split0 + 8 * s, 128);
+            mbar_init(split0 + 8 * s, PAIR ? 2 : 128);  // pairs: one arrival a CTA; else every split thread
             mbar_init(empty0 + 8 * s, 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, 8);
+            mbar_init(tempty0 + 8 * a, PAIR ? 16 : 8);  // every epilogue warp of the pair
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
     if (warp == 2) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(2u * TBN));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"(2u * TN));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"(2u * TN));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before anyone signals them
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     pdl_wait();
     pdl_trigger();
 
-    const int m_tiles = (M + TBM - 1) / TBM, n_tiles = (N + TBN - 1) / TBN;
+    const int m_tiles = (M + TM - 1) / TM, n_tiles = (N + TN - 1) / TN;
     const int tiles = m_tiles * n_tiles, kblocks = (K + TBK - 1) / TBK;
     auto stage_at = [&](int s) { return smem + s * STAGE_BYTES; };  // A hi | A lo | W hi | W lo
 
@@ -97,8 +133,9 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / n_tiles) * TBM, n0 = (tile % n_tiles) * TBN;
+            for (int tile = unit; tile < tiles && ok; tile += units) {
+                // This CTA's 128 rows of the tile's A rows and of its W rows.
+                const int m0 = (tile / n_tiles) * TM + (int)pr * TBM, n0 = (tile % n_tiles) * TN + (int)pr * TBM;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!(ok = mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, fault))) break;
                     const uint32_t sa = smem_u32(stage_at(stage)), fb = full0 + 8 * stage;
@@ -112,16 +149,26 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
     } else if (warp >= 4 && warp < 8) {
         // The split: lo = x - trunc_tf32(x), for A and W, 16 bytes at a time.
         const int t = threadIdx.x - 128;
+        const uint32_t split_lead = PAIR ? mapa(split0, 0) : split0;
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
+        for (int tile = unit; tile < tiles && ok; tile += units)
             for (int kb = 0; kb < kblocks; ++kb) {
-                if (!(ok = mbar_wait(full0 + 8 * stage, phase, abort_flag, fault))) break;
+                // Pairs: all four warps take the same branch (a failed wait
+                // in one thread ends the split for all), so the barrier of
+                // the four warps below never waits for a thread that left.
+                uint32_t good = mbar_wait(full0 + 8 * stage, phase, abort_flag, fault) ? 1u : 0u;
+                if constexpr (PAIR)
+                    asm volatile("{\n .reg .pred p, q;\n setp.ne.b32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+                                 : "=r"(good)
+                                 : "r"(good)
+                                 : "memory");
+                if (!(ok = good != 0)) break;
                 uint8_t *st = stage_at(stage);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    uint4 *hi = reinterpret_cast<uint4 *>(st + 2 * h * HALF_BYTES);
+                    const uint4 *hi = reinterpret_cast<const uint4 *>(st + 2 * h * HALF_BYTES);
                     uint4 *lo = reinterpret_cast<uint4 *>(st + (2 * h + 1) * HALF_BYTES);
 #pragma unroll 4
                     for (int i = t; i < HALF_BYTES / 16; i += 128) {
@@ -131,30 +178,39 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
                         float r[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            hs[j] = xs[j] & 0xFFFFE000u;  // exactly a TF32 value, however the tensor core reads F32
+                            hs[j] = xs[j] & 0xFFFFE000u;  // hi: the TF32 value the tensor core reads of x
                             r[j] = __fsub_rn(__uint_as_float(xs[j]), __uint_as_float(hs[j]));
                         }
-                        hi[i] = make_uint4(hs[0], hs[1], hs[2], hs[3]);
+
                         lo[i] = make_uint4(__float_as_uint(r[0]), __float_as_uint(r[1]), __float_as_uint(r[2]),
                                            __float_as_uint(r[3]));
                     }
                 }
                 fence_async_smem();  // the lo halves, written by threads, are read by the tensor core
-                mbar_arrive(split0 + 8 * stage);
+                if constexpr (PAIR) {
+                    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four split warps
+                    if (t == 0) mbar_arrive_release_cluster(split_lead + 8 * stage);
+                } else {
+                    mbar_arrive(split0 + 8 * stage);
+                }
                 if (++stage == STAGES) stage = 0, phase ^= 1;
             }
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_tf32();
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_tf32<TM, TN>();
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                if (!(ok = mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, fault))) break;
+            for (int tile = unit; tile < tiles && ok; tile += units) {
+                if (!(ok = PAIR ? mbar_wait_cluster(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, fault)
+                                : mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, fault)))
+                    break;
                 tc_fence_after();
-                const uint32_t d = tmem + acc * TBN;
+                const uint32_t d = tmem + acc * TN;
                 for (int kb = 0; kb < kblocks; ++kb) {
-                    if (!(ok = mbar_wait(split0 + 8 * stage, phase, abort_flag, fault))) break;
+                    if (!(ok = PAIR ? mbar_wait_cluster(split0 + 8 * stage, phase, abort_flag, fault)
+                                    : mbar_wait(split0 + 8 * stage, phase, abort_flag, fault)))
+                        break;
                     tc_fence_after();
                     const uint32_t s = smem_u32(stage_at(stage));
                     const uint64_t ah = smem_desc(s), al = smem_desc(s + HALF_BYTES);
@@ -162,31 +218,40 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
 #pragma unroll
                     for (int kk = 0; kk < TBK / 8; ++kk) {
                         const uint64_t off = (uint64_t)(kk * 8 * 4 / 16);  // 32 bytes a K = 8 step
-                        umma_tf32(d, al + off, wh + off, idesc, (kb | kk) ? 1u : 0u);
-                        umma_tf32(d, ah + off, wl + off, idesc, 1u);
-                        umma_tf32(d, ah + off, wh + off, idesc, 1u);
+                        if constexpr (PAIR) {
+                            umma_tf32_pair(d, al + off, wh + off, idesc, (kb | kk) ? 1u : 0u);
+                            umma_tf32_pair(d, ah + off, wl + off, idesc, 1u);
+                            umma_tf32_pair(d, ah + off, wh + off, idesc, 1u);
+                        } else {
+                            umma_tf32(d, al + off, wh + off, idesc, (kb | kk) ? 1u : 0u);
+                            umma_tf32(d, ah + off, wl + off, idesc, 1u);
+                            umma_tf32(d, ah + off, wh + off, idesc, 1u);
+                        }
                     }
-                    umma_commit(empty0 + 8 * stage);
+                    if constexpr (PAIR) umma_commit_pair(empty0 + 8 * stage);
+                    else umma_commit(empty0 + 8 * stage);
                     if (++stage == STAGES) stage = 0, phase ^= 1;
                 }
                 if (!ok) break;
-                umma_commit(tfull0 + 8 * acc);
+                if constexpr (PAIR) umma_commit_pair(tfull0 + 8 * acc);
+                else umma_commit(tfull0 + 8 * acc);
                 if (++acc == 2) acc = 0, acc_phase ^= 1;
             }
         }
     } else if (warp >= 8) {
         const int ew = warp - 8, quad = warp & 3, part = ew >> 2;
-        constexpr int COLS = TBN / 2;
+        constexpr int COLS = TN / 2;
+        const uint32_t tempty_lead = PAIR ? mapa(tempty0, 0) : tempty0;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            const int m0 = (tile / n_tiles) * TBM, n0 = (tile % n_tiles) * TBN;
+        for (int tile = unit; tile < tiles; tile += units) {
+            const int m0 = (tile / n_tiles) * TM + (int)pr * TBM, n0 = (tile % n_tiles) * TN;
             const int row = m0 + quad * 32 + lane;
             const bool row_ok = row < M;
             const int col_base = n0 + part * COLS;
             if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, fault)) break;
             tc_fence_after();
-            const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + acc * TBN + part * COLS;
+            const uint32_t tbase = tmem + ((uint32_t)(quad * 32) << 16) + acc * TN + part * COLS;
 #pragma unroll 1
             for (int c = 0; c < COLS; c += 32) {
                 float v[32];
@@ -195,7 +260,10 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
                 if (c + 32 >= COLS) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
+                    if (lane == 0) {
+                        if constexpr (PAIR) mbar_arrive_remote(tempty_lead + 8 * acc);
+                        else mbar_arrive(tempty0 + 8 * acc);
+                    }
                 }
                 const int col = col_base + c;
                 if (!row_ok || col >= N) continue;
@@ -234,10 +302,14 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
         }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still signal it
+    else __syncthreads();
     if (warp == 2) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2u * TBN));
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2u * TN));
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2u * TN));
     }
 }
 
@@ -271,18 +343,45 @@ cudaError_t make_operand_map_f32(const float *ptr, uint64_t rows, uint64_t cols,
 }
 
 bool gemm_tf32_takes(int N, int K, const Epilogue &e) {
-    return N % TBN == 0 && K % 4 == 0 && N <= MAX_BIAS && e.kind != EPI_ROPE && e.kind != EPI_RESIDUAL_LN;
+    return N % 128 == 0 && K % 4 == 0 && N <= MAX_BIAS && e.kind != EPI_ROPE && e.kind != EPI_RESIDUAL_LN;
 }
 
 cudaError_t gemm_tf32(const CUtensorMap &a_map, const CUtensorMap &w_map, int M, int N, int K, const Epilogue &epi,
-                      int sms, int *fault, cudaStream_t s) {
+                      int sms, int *fault, cudaStream_t s, int pair) {
     if (M == 0) return cudaSuccess;
     if (!gemm_tf32_takes(N, K, epi)) return cudaErrorNotSupported;
-    cudaError_t err = cudaFuncSetAttribute(gemm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    // CTA pairs (256 x 256 tiles) when N is a multiple of 256 and the pair
+    // tiles fill every pair of SMs at least once; else 128 x 128 tiles.
+    const int pair_tiles = ((M + 255) / 256) * (N / 256);
+    if (pair < 0) pair = N % 256 == 0 && pair_tiles >= sms / 2;
+    if (pair && N % 256 != 0) return cudaErrorNotSupported;
+    if (pair) {
+        auto kern = gemm_tf32_kernel<true>;
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        if (err != cudaSuccess) return err;
+        const int units = pair_tiles < sms / 2 ? pair_tiles : sms / 2;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * units);
+        cfg.blockDim = dim3(512);
+        cfg.dynamicSmemBytes = SMEM;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        return counted(cudaLaunchKernelEx(&cfg, kern, a_map, w_map, M, N, K, epi, fault));
+    }
+    auto kern = gemm_tf32_kernel<false>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (err != cudaSuccess) return err;
-    const int tiles = ((M + TBM - 1) / TBM) * (N / TBN);
+    const int tiles = ((M + TBM - 1) / TBM) * (N / 128);
     const int grid = tiles < sms ? tiles : sms;
-    return launch_pdl(gemm_tf32_kernel, grid, 512, SMEM, s, a_map, w_map, M, N, K, epi, fault);
+    return launch_pdl(kern, grid, 512, SMEM, s, a_map, w_map, M, N, K, epi, fault);
 }
 
 }  // namespace tb

@@ -94,9 +94,12 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t vari
                                                    const float *sin_t, uint32_t positions, turbo_error *err) {
     Dt dt;
     if (!dt_of(dtype, &dt)) return hook_fail(err, TURBO_E_INVALID_ENUM, "dtype", cudaSuccess);
-    if (variant != 1 && variant != 3 && dt == Dt::F32)
+    if (variant > 4) return hook_fail(err, TURBO_E_INVALID_ARGUMENT, "variant", cudaSuccess);
+    if ((variant == 0 || variant == 2) && dt == Dt::F32)
         return hook_fail(err, TURBO_E_UNSUPPORTED, "variants 0 and 2 take F16/BF16", cudaSuccess);
-    if (variant == 3 && dt != Dt::F32) return hook_fail(err, TURBO_E_UNSUPPORTED, "variant 3 takes F32", cudaSuccess);
+    if (variant >= 3 && dt != Dt::F32) return hook_fail(err, TURBO_E_UNSUPPORTED, "variants 3 and 4 take F32", cudaSuccess);
+    if (variant == 4 && N % 256 != 0)
+        return hook_fail(err, TURBO_E_INVALID_ARGUMENT, "variant 4 takes N a multiple of 256", cudaSuccess);
     Dev dv;
     cudaError_t e = cudaSuccess;
     const size_t out_cols = epi == EPI_GATED ? N / 2 : N;
@@ -146,8 +149,9 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t vari
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
         if (e == cudaSuccess) e = gemm_tc(dt, maps, (int)M, (int)N, (int)K, ep, sms, fault, 0);
-    } else if (variant == 3) {
-        // 3: the EXACT tier's kind::tf32 GEMM with the three-product split.
+    } else if (variant == 3 || variant == 4) {
+        // 3: the EXACT tier's kind::tf32 GEMM with the three-product split,
+        // tiles chosen by shape; 4: the same on CTA pairs (N % 256 == 0).
         CUtensorMap am, wm;
         e = make_operand_map_f32((const float *)da, M, K, K, &am);
         if (e == cudaSuccess) e = make_operand_map_f32((const float *)dw, N, K, K, &wm);
@@ -155,7 +159,7 @@ extern "C" TB_EXPORT int32_t turbo_b200_gemm_check(uint32_t dtype, uint32_t vari
         if (epi == EPI_ROPE) e2.kind = EPI_STORE;
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-        if (e == cudaSuccess) e = gemm_tf32(am, wm, (int)M, (int)N, (int)K, e2, sms, fault, 0);
+        if (e == cudaSuccess) e = gemm_tf32(am, wm, (int)M, (int)N, (int)K, e2, sms, fault, 0, variant == 4 ? 1 : -1);
         if (e == cudaSuccess && epi == EPI_ROPE) e = rope_qk(dt, dy, dpos, dcos, dsin, (int)M, (int)(N / 3), (int)head_dim, 0);
     } else {
         if (epi == EPI_ROPE) {

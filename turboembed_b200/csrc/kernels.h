@@ -148,12 +148,14 @@ cudaError_t gemm_tc(Dt dt, const TcMaps &maps, int M, int N, int K, const Epilog
 // The EXACT tier's GEMM on tcgen05 kind::tf32 with the three-product split
 // (F32 operands, F32 accuracy): A [M, K] and W [N, K] through F32 TMA maps
 // ([128 x 32] boxes, make_operand_map_f32); epilogues as gemm_tc's except
-// RoPE and the fused LayerNorm; N a multiple of 128.
+// RoPE and the fused LayerNorm; N a multiple of 128. pair: 1 CTA pairs on
+// 256 x 256 tiles (N a multiple of 256), 0 one CTA a 128 x 128 tile, -1 the
+// choice by shape.
 cudaError_t make_operand_map_f32(const float *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                                  CUtensorMap *out);
 bool gemm_tf32_takes(int N, int K, const Epilogue &e);
 cudaError_t gemm_tf32(const CUtensorMap &a_map, const CUtensorMap &w_map, int M, int N, int K, const Epilogue &epi,
-                      int sms, int *fault, cudaStream_t s);
+                      int sms, int *fault, cudaStream_t s, int pair = -1);
 
 // Whether EPI_RESIDUAL_LN runs for rows of n columns at dt: n = 768 or 1024
 // and the device fits at least one cluster of n / 128 CTAs.
