@@ -108,7 +108,9 @@ TB_EXPORT int32_t turbo_b200_wait_check(uint64_t limit_ns, int32_t *fault_out, i
  * the mask entries, window < 0 for whole rows. variant 0 is the F16/BF16
  * mma.sync kernel, 1 the SIMT kernel (any dtype), 2 the tcgen05 kernel with
  * one 128-query tile a CTA, 3 the tcgen05 kernel with two (whole rows only),
- * the last two for head width 64. ctx_out [tokens, hidden]. */
+ * 4 (F32 only) the EXACT tier's tcgen05 kind::tf32 kernel with the
+ * three-product split (the lo halves of qkv made on the host), the last
+ * three for head width 64. ctx_out [tokens, hidden]. */
 TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, uint32_t batch, const int32_t *lens,
                                              const float *qkv, const uint8_t *live, uint32_t heads,
                                              uint32_t head_dim, int32_t window, float *ctx_out, turbo_error *err);

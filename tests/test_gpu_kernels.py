@@ -314,6 +314,34 @@ def test_f32_attention(case):
     assert np.abs(got - want).max() < 2e-5
 
 
+@pytest.mark.parametrize("case", TC_CASES)
+@pytest.mark.parametrize("holes", [True, False])
+def test_tf32x3_attention_has_f32_accuracy(case, holes):
+    # The EXACT tier's tensor-core attention (kind::tf32, three products for
+    # Q K^T and for P V): to the bound of the FFMA kernel against F64.
+    lens, heads, d, window = case
+    T = sum(lens)
+    rng = np.random.default_rng(T + d + 7)
+    qkv = rng.standard_normal((T, 3 * heads * d)).astype(np.float32)
+    live = (rng.random(T) > 0.15).astype(np.uint8) if holes else np.ones(T, np.uint8)
+    got = runtime.attention_check(F32, 4, lens, qkv, live, heads, d, window)
+    want = ref_attention(qkv, lens, live, heads, d, window)
+    assert np.abs(got - want).max() < 2e-5
+
+
+def test_tf32x3_attention_rescales_when_the_max_grows():
+    lens, heads, d = [400, 70, 700], 2, 64
+    T = sum(lens)
+    rng = np.random.default_rng(98)
+    qkv = rng.standard_normal((T, 3 * heads * d)).astype(np.float32)
+    ramp = np.concatenate([np.linspace(0.2, 6.0, n) for n in lens]).astype(np.float32)
+    qkv[:, heads * d:2 * heads * d] *= ramp[:, None]
+    live = np.ones(T, np.uint8)
+    got = runtime.attention_check(F32, 4, lens, qkv, live, heads, d, -1)
+    want = ref_attention(qkv, lens, live, heads, d, -1)
+    assert np.abs(got - want).max() < 2e-5 * max(1.0, np.abs(want).max())
+
+
 @pytest.mark.parametrize("dtype", [F16, BF16])
 def test_simt_attention_takes_other_head_widths(dtype):
     lens, heads, d = [40, 9, 64], 4, 8

@@ -1,0 +1,493 @@
+// attention_tf32.cu -- the EXACT tier's attention on the 5th-gen tensor
+// cores: F32 operands to F32 accuracy by the three-product split of the
+// EXACT GEMMs (gemm_tf32.cu; Markidis et al., 2018), head width 64.
+//
+// Semantics as attention.cu's F32 kernel (core/src/cpu/kernels/attend.rs:
+// 95-198): a key whose mask entry is 0, past the row's end, or outside a
+// sliding window scores -inf; a query that reads no live key gets a zero
+// context. This is the tensor-core counterpart of attn_f32_kernel.
+//
+// x = hi + lo with hi = x with its low 13 mantissa bits cleared (what the
+// tensor core reads of an F32 operand of kind::tf32) and lo = x - hi. The
+// QKV GEMM's epilogue writes lo of every output into qkv_lo (same layout as
+// qkv), so Q's and K's halves arrive by TMA; V and P are split here:
+//   S  = Q_lo K^T + Q K_lo^T + Q K^T    M 128 x N 64, 8 steps of K = 8
+//   O += P_lo V + P V_lo + P V          M 128 x N 64, 8 steps of K = 8
+// P (F32) is written by the softmax over its chunk's S columns in TMEM and
+// P_lo = P - hi(P) beside it: the A operands of P V, read from TMEM. The
+// lo x lo products are below F32 precision and left out.
+//
+// Operand tiles are [rows x 32] F32 with the 128-byte swizzle (one swizzle
+// row is 32 floats), all K-major: Q [128 x 64] and K [64 keys x 64] arrive
+// as two TMA boxes each along d; the B operand of P V is V transposed, [64 d
+// x 64 keys] as two boxes along the keys, written by a transposer warpgroup
+// that reads V from global memory (and splits it into hi and lo on the way).
+// An MN-major B of kind::tf32 read as V stands, with A in tensor memory,
+// gave no products on B200 (the accumulator stayed zero at N = 32 and 64),
+// so this kernel does not use one.
+//
+// One 128-query tile a CTA (persistent over units (row, tile, head)), one
+// CTA an SM (shared memory: Q and Q_lo 64 KB, two chunk buffers of K, K_lo,
+// V^T, V^T_lo 64 KB each), 288 threads: warps 0..3 the softmax (thread r =
+// query row r = TMEM lane r), warp 4 lane 0 the loads and the MMAs in the
+// order of attention_tc.cu's one-tile kernel, warps 5..8 the transposer.
+// TMEM: S / P in columns 0..63, P_lo in 64..127, O in 128..191. The softmax
+// keeps a reference max per row that moves only when a chunk's max passes
+// it by more than 8 (log2 units), and then rescales O in TMEM and the row
+// sum. Waits are bounded (2 s) and end in the fault word.
+#include <cudaTypedefs.h>
+
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace tb {
+namespace {
+
+using namespace tc;
+
+constexpr int QT = ATTN_TC_QUERIES, KT = 64, D = 64;
+constexpr int Q_BOX = QT * 32 * 4;       // 16 KB: [128 rows x 32 F32]
+constexpr int K_BOX = KT * 32 * 4;       // 8 KB: [64 rows x 32 F32]
+constexpr int Q_BYTES = 2 * Q_BOX;       // a [128 x 64] F32 tile
+constexpr int KV_BYTES = 2 * K_BOX;      // a [64 x 64] F32 tile
+constexpr int BUF_BYTES = 4 * KV_BYTES;  // a chunk: K, K_lo, V^T, V^T_lo
+constexpr int SMEM = 2 * Q_BYTES + 2 * BUF_BYTES + 256 + 1024;
+constexpr float RESCALE = 8.0f;                              // log2 units
+constexpr float SCALE_LOG2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+static_assert(SMEM <= 227 * 1024, "one CTA an SM");
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// kind::tf32 instruction descriptor: F32 accumulator, A and B TF32 (format
+// 2), A K-major, B K-major or MN-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_tf32(int n, bool b_mn_major) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+// A from tensor memory (row r = lane r, one F32 a column).
+__device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                             uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ float tf32_lo(float x) { return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)); }
+
+// Keys [klo, khi) the query tile at q0 of a row of len tokens reads.
+__device__ __forceinline__ void key_range(int len, int q0, int window, int &klo, int &khi) {
+    klo = 0;
+    khi = len;
+    if (window >= 0) {
+        klo = max(0, q0 - window);
+        khi = min(len, q0 + QT - 1 + window + 1);
+    }
+}
+
+// The softmax warpgroup's pass over one tile: chunks of keys [klo, khi); g
+// counts chunks (barrier phases). lane_base addresses this warp's TMEM lanes
+// at column 0. Returns false when the kernel must stop.
+__device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int khi, int window, int head,
+                                             float *__restrict__ ctx, int h, const uint8_t *__restrict__ live,
+                                             uint32_t lane_base, int r, uint32_t bar_s, uint32_t bar_p,
+                                             uint32_t bar_o, uint32_t &g, volatile int *abort_flag, int *fault) {
+    const int lane = threadIdx.x & 31;
+    const int nch = (khi - klo + KT - 1) / KT;
+    const int qi = it.q0 + r;
+    float m_ref = -INFINITY, l = 0.0f;
+    for (int j = 0; j < nch; ++j, ++g) {
+        const int k0 = klo + j * KT;
+        uint32_t km0, km1;
+        if (!it.holes) {
+            const int n0 = khi - k0, n1 = n0 - 32;
+            km0 = n0 >= 32 ? 0xffffffffu : (n0 <= 0 ? 0u : (1u << n0) - 1u);
+            km1 = n1 >= 32 ? 0xffffffffu : (n1 <= 0 ? 0u : (1u << n1) - 1u);
+        } else {
+            int key = k0 + lane;
+            km0 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
+            key += 32;
+            km1 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
+        }
+        const bool full = window < 0 && (km0 & km1) == 0xffffffffu;
+        if (!mbar_wait(bar_s, g & 1, abort_flag, fault)) return false;
+        tc_fence_after();
+        float sv[64];
+        {
+            uint32_t raw[64];
+            __syncwarp();
+            tmem_ld32_async(lane_base, raw);
+            tmem_ld32_async(lane_base + 32, raw + 32);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
+        }
+        if (!full) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                bool valid = (((i < 32) ? km0 : km1) >> (i & 31)) & 1u;
+                if (window >= 0) valid = valid && abs(qi - (k0 + i)) <= window;
+                sv[i] = valid ? sv[i] : -INFINITY;
+            }
+        }
+        float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int i = 4; i < 64; i += 4)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) m4[k] = fmaxf(m4[k], sv[i + k]);
+        float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        mx = mx == -INFINITY ? mx : mx * SCALE_LOG2;
+        const bool move = mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + RESCALE);
+        float f = 1.0f;
+        if (move) {
+            f = m_ref == -INFINITY ? 0.0f : ex2(m_ref - mx);
+            l *= f;
+            m_ref = mx;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, move)) {
+            __syncwarp();
+#pragma unroll 1
+            for (int q = 0; q < 4; ++q) {
+                float o[16];
+                tmem_ld16(lane_base + 128 + q * 16, o);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] *= f;
+                tmem_st16(lane_base + 128 + q * 16, o);
+            }
+        }
+        const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
+        float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            sv[i] = ex2(fmaf(sv[i], SCALE_LOG2, -mu));  // 0 for an invalid key (2^-inf)
+            s4[i & 3] += sv[i];
+        }
+        // P over the chunk's S columns, then P_lo beside it.
+        __syncwarp();
+        tmem_st32(lane_base, sv);
+        tmem_st32(lane_base + 32, sv + 32);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) sv[i] = tf32_lo(sv[i]);
+        tmem_st32(lane_base + 64, sv);
+        tmem_st32(lane_base + 96, sv + 32);
+        l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        tc_fence_before();
+        mbar_arrive(bar_p);
+    }
+    if (!mbar_wait(bar_o, (g - 1) & 1, abort_flag, fault)) return false;
+    tc_fence_after();
+    __syncwarp();
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    float *out = ctx + ((int64_t)it.start + qi) * h + head * D;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        float o[32];
+        tmem_ld32(lane_base + 128 + half * 32, o);
+        if (qi < it.len) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                reinterpret_cast<float4 *>(out)[half * 8 + q] =
+                    make_float4(o[4 * q] * inv, o[4 * q + 1] * inv, o[4 * q + 2] * inv, o[4 * q + 3] * inv);
+        }
+    }
+    tc_fence_before();  // O is read: the next unit's first P V may overwrite it
+    return true;
+}
+
+// The transposer's pass over chunk j of a unit: V rows [k0, k0 + 64) of the
+// head at column col, keys at or past khi written as zeros, into V^T (hi:
+// the values as they are, read by the tensor core as TF32) and V^T_lo, each
+// two K-major boxes [64 d x 32 keys] with the 128-byte swizzle. Thread t of
+// 128 moves two 4 x 4 blocks (4 keys x 4 columns of d): 16-byte loads (a
+// warp reads 8 keys x 64 contiguous bytes) and 16-byte stores of 4 keys of
+// one d (the 8 lanes of a store phase hit 8 distinct 16-byte bank groups).
+__device__ __forceinline__ void transpose_v(const float *__restrict__ qkv, int64_t ld, int start, int k0, int khi,
+                                            int col, uint8_t *vth, uint8_t *vtl, int t) {
+    const int lane = t & 31, w = t >> 5;
+    const int g = (lane >> 3) + 4 * w;  // d columns 4 g .. 4 g + 3
+#pragma unroll
+    for (int itr = 0; itr < 2; ++itr) {
+        const int kq = (lane & 7) + 8 * itr;  // keys 4 kq .. 4 kq + 3 of the chunk
+        float4 v[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int k = k0 + 4 * kq + r;
+            v[r] = k < khi ? *reinterpret_cast<const float4 *>(qkv + (int64_t)(start + k) * ld + col + 4 * g)
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        const int box = kq >> 3, c = kq & 7;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int d = 4 * g + j;
+            float e[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) e[r] = j == 0 ? v[r].x : j == 1 ? v[r].y : j == 2 ? v[r].z : v[r].w;
+            const int off = box * K_BOX + d * 128 + ((c ^ (d & 7)) << 4);
+            *reinterpret_cast<float4 *>(vth + off) = make_float4(e[0], e[1], e[2], e[3]);
+            *reinterpret_cast<float4 *>(vtl + off) = make_float4(tf32_lo(e[0]), tf32_lo(e[1]), tf32_lo(e[2]), tf32_lo(e[3]));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(288, 1)
+attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
+                 const __grid_constant__ CUtensorMap tq_lo, const __grid_constant__ CUtensorMap tkv_lo,
+                 const float *__restrict__ qkv, float *__restrict__ ctx, const uint8_t *__restrict__ live,
+                 const AttnItem *__restrict__ items, int n_items, int heads, int h, int window, int *fault) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sQ = smem, *sBuf = smem + 2 * Q_BYTES;  // Q, Q_lo; then 2 x (K, K_lo, V^T, V^T_lo)
+    uint8_t *bars = sBuf + 2 * BUF_BYTES;
+    // Q in, K in [2], V^T written [2], S done, P written, P V done, V^T
+    // free [2] (the P V that read it is done).
+    const uint32_t bar_q = smem_u32(bars), bar_k = bar_q + 8, bar_v = bar_q + 24, bar_s = bar_q + 40;
+    const uint32_t bar_p = bar_q + 48, bar_o = bar_q + 56, bar_vf = bar_q + 80;
+    uint32_t *tmem_slot = (uint32_t *)(bars + 64);
+    volatile int *abort_flag = (volatile int *)(bars + 72);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int units = n_items * heads;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar_q, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar_k + 8 * i, 1);
+            mbar_init(bar_v + 8 * i, 128);  // every transposer thread
+            mbar_init(bar_vf + 8 * i, 1);
+        }
+        mbar_init(bar_s, 1);
+        mbar_init(bar_p, 128);
+        mbar_init(bar_o, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(256u));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // qkv, qkv_lo and the plan are an earlier kernel's and copy's
+    pdl_trigger();
+
+    if (warp == 4) {
+        if (lane == 0) {
+            // Chunk y (counted over this CTA's units) uses buffer y & 1. P V(y)
+            // reads P from the S columns and S(y + 1) follows it into them (in
+            // issue order). When P(y) arrives, S(y) and P V(y - 1) are done:
+            // K(y + 1) can go into buffer (y + 1) & 1 once S(y) is issued.
+            // V^T(y) comes from the transposer, which refills a buffer once
+            // the P V that read it is done (bar_vf). The next unit's Q goes in
+            // once this unit's last S is done.
+            const uint32_t ids = idesc_tf32(KT, false), idpv = idesc_tf32(D, false);
+            const uint32_t aq = smem_u32(sQ), aql = aq + Q_BYTES, ab = smem_u32(sBuf);
+            struct Unit {
+                int row0, qrow, col, nch;
+            };
+            auto unit_of = [&](int u) {
+                if (u >= units) return Unit{0, 0, 0, 0};
+                const AttnItem it = items[u / heads];
+                int klo, khi;
+                key_range(it.len, it.q0, window, klo, khi);
+                return Unit{it.start + klo, it.start + it.q0, (u % heads) * D, (khi - klo + KT - 1) / KT};
+            };
+            auto load_q = [&](const Unit &n) {
+                mbar_expect_tx(bar_q, 2 * Q_BYTES);
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    tma_load_2d(aq + hf * Q_BOX, &tq, n.col + 32 * hf, n.qrow, bar_q);
+                    tma_load_2d(aql + hf * Q_BOX, &tq_lo, n.col + 32 * hf, n.qrow, bar_q);
+                }
+            };
+            // K of chunk j of unit n into buffer y & 1: hi then lo.
+            auto load_k = [&](const Unit &n, int j, uint32_t y) {
+                const uint32_t b = y & 1, bar = bar_k + 8 * b;
+                const uint32_t dst = ab + b * BUF_BYTES;
+                mbar_expect_tx(bar, 2 * KV_BYTES);
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int x = h + n.col + 32 * hf, yrow = n.row0 + j * KT;
+                    tma_load_2d(dst + hf * K_BOX, &tkv, x, yrow, bar);
+                    tma_load_2d(dst + KV_BYTES + hf * K_BOX, &tkv_lo, x, yrow, bar);
+                }
+            };
+            auto issue_s = [&](uint32_t b) {
+                tc_fence_after();
+                const uint32_t kh = ab + b * BUF_BYTES, kl = kh + KV_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < D / 8; ++kk) {
+                    const uint32_t box = (uint32_t)(kk >> 2);
+                    const uint64_t off = (uint64_t)((kk & 3) * 2);  // 32 bytes a K = 8 step, in 16-byte units
+                    const uint64_t qh = smem_desc(aq + box * Q_BOX) + off, ql = smem_desc(aql + box * Q_BOX) + off;
+                    const uint64_t dkh = smem_desc(kh + box * K_BOX) + off, dkl = smem_desc(kl + box * K_BOX) + off;
+                    umma_tf32(tmem, ql, dkh, ids, kk > 0 ? 1u : 0u);
+                    umma_tf32(tmem, qh, dkl, ids, 1u);
+                    umma_tf32(tmem, qh, dkh, ids, 1u);
+                }
+                umma_commit(bar_s);
+            };
+            auto issue_pv = [&](uint32_t b, bool acc) {
+                tc_fence_after();
+                const uint32_t vh = ab + b * BUF_BYTES + 2 * KV_BYTES, vl = vh + KV_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < KT / 8; ++kk) {
+                    // B = V^T [64 d x 8 keys]; A = P / P_lo columns kk*8 .. kk*8+7.
+                    const uint32_t box = (uint32_t)(kk >> 2);
+                    const uint64_t off = (uint64_t)((kk & 3) * 2);
+                    const uint64_t dvh = smem_desc(vh + box * K_BOX) + off, dvl = smem_desc(vl + box * K_BOX) + off;
+                    umma_tf32_ts(tmem + 128, tmem + 64 + kk * 8, dvh, idpv, (acc || kk) ? 1u : 0u);
+                    umma_tf32_ts(tmem + 128, tmem + kk * 8, dvl, idpv, 1u);
+                    umma_tf32_ts(tmem + 128, tmem + kk * 8, dvh, idpv, 1u);
+                }
+                umma_commit(bar_o);
+                umma_commit(bar_vf + 8 * b);
+            };
+            const int grid = (int)gridDim.x;
+            int u = blockIdx.x;
+            Unit cur = unit_of(u), nxt = unit_of(u + grid);
+            auto load_after = [&](int j, uint32_t y) {
+                if (j + 1 < cur.nch) load_k(cur, j + 1, y + 1);
+                else if (nxt.nch > 0) load_k(nxt, 0, y + 1);
+            };
+            uint32_t y = 0, qn = 0;
+            bool ok = true;
+            if (u < units) {
+                load_q(cur);
+                load_k(cur, 0, 0);
+                load_after(0, 0);
+            }
+            for (; u < units && ok; u += grid, ++qn) {
+                if (!(ok = mbar_wait(bar_q, qn & 1, abort_flag, fault))) break;
+                if (!(ok = mbar_wait(bar_k + 8 * (y & 1), (y >> 1) & 1, abort_flag, fault))) break;
+                issue_s(y & 1);
+                if (y >= 1) load_after(0, y);
+                if (cur.nch == 1) {
+                    if (!(ok = mbar_wait(bar_s, y & 1, abort_flag, fault))) break;
+                    if (nxt.nch > 0) load_q(nxt);
+                }
+                for (int j = 0; j < cur.nch && ok; ++j, ++y) {
+                    if (!(ok = mbar_wait(bar_p, y & 1, abort_flag, fault))) break;
+                    if (!(ok = mbar_wait(bar_v + 8 * (y & 1), (y >> 1) & 1, abort_flag, fault))) break;
+                    issue_pv(y & 1, j > 0);
+                    if (j + 1 < cur.nch) {
+                        if (!(ok = mbar_wait(bar_k + 8 * ((y + 1) & 1), ((y + 1) >> 1) & 1, abort_flag, fault))) break;
+                        issue_s((y + 1) & 1);
+                        load_after(j + 1, y + 1);
+                        if (j + 2 == cur.nch) {
+                            if (!(ok = mbar_wait(bar_s, (y + 1) & 1, abort_flag, fault))) break;
+                            if (nxt.nch > 0) load_q(nxt);
+                        }
+                    }
+                }
+                cur = nxt;
+                nxt = unit_of(u + 2 * grid);
+            }
+        }
+    } else if (warp >= 5) {
+        // The transposer: V^T of chunk y into buffer y & 1 once the P V of
+        // chunk y - 2 (the buffer's last reader) is done.
+        const int t = threadIdx.x - 160;
+        const int64_t ld = 3 * (int64_t)h;
+        uint32_t y = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const AttnItem it = items[u / heads];
+            int klo, khi;
+            key_range(it.len, it.q0, window, klo, khi);
+            const int nch = (khi - klo + KT - 1) / KT, col = 2 * h + (u % heads) * D;
+            for (int j = 0; j < nch; ++j, ++y) {
+                const uint32_t b = y & 1;
+                if (y >= 2 && !(ok = mbar_wait(bar_vf + 8 * b, ((y >> 1) & 1) ^ 1, abort_flag, fault))) break;
+                uint8_t *vth = sBuf + b * BUF_BYTES + 2 * KV_BYTES;
+                transpose_v(qkv, ld, it.start, klo + j * KT, khi, col, vth, vth + KV_BYTES, t);
+                fence_async_smem();  // written by threads, read by the tensor core
+                mbar_arrive(bar_v + 8 * b);
+            }
+        }
+    } else {
+        const int r = threadIdx.x;
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        uint32_t g = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
+            const AttnItem it = items[u / heads];
+            int klo, khi;
+            key_range(it.len, it.q0, window, klo, khi);
+            if (!softmax_tile(it, klo, khi, window, u % heads, ctx, h, live, lane_base, r, bar_s, bar_p, bar_o, g,
+                              abort_flag, fault))
+                break;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }();
+    return fn;
+}
+
+cudaError_t make_map(const float *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows, CUtensorMap *out) {
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    if ((cols * 4) % 16 != 0 || ((uintptr_t)ptr & 15) != 0) return cudaErrorInvalidValue;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 4};
+    cuuint32_t box[2] = {32, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+cudaError_t make_attn_maps_f32(const float *qkv, uint64_t rows, int hidden, AttnMapsF32 *out) {
+    cudaError_t e = make_map(qkv, rows, (uint64_t)3 * hidden, QT, &out->q);
+    if (e == cudaSuccess) e = make_map(qkv, rows, (uint64_t)3 * hidden, KT, &out->kv);
+    return e;
+}
+
+cudaError_t attention_tf32(const AttnMapsF32 &hi, const AttnMapsF32 &lo, const float *qkv, float *ctx,
+                           const uint8_t *tok_live,
+                           const AttnItem *items, int n_items, int heads, int head_dim, int hidden, int window,
+                           int *fault, cudaStream_t s) {
+    if (n_items == 0) return cudaSuccess;
+    if (head_dim != D || hidden % 4 != 0) return cudaErrorNotSupported;  // TMA x: 16-byte multiples
+    cudaError_t e = cudaFuncSetAttribute(attn_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int units = n_items * heads;
+    const int grid = units < sms ? units : sms;
+    return launch_pdl(attn_tf32_kernel, grid, 288, SMEM, s, hi.q, hi.kv, lo.q, lo.kv, qkv, ctx, tok_live, items,
+                      n_items, heads, hidden, window, fault);
+}
+
+}  // namespace tb

@@ -218,6 +218,12 @@ struct Session {
     // residual GEMM into it: the GEMM writes x and xn = LN(x) (same switch).
     bool fuse_ln_pre = false;
     bool exact_tf32 = false;  // F32 sessions: GEMMs on kind::tf32 x3 (else FFMA)
+    // F32 sessions of head width 64 without rotary positions: the QKV GEMM
+    // (kind::tf32) also writes qkv's lo halves into qkv_lo, and attention
+    // runs on kind::tf32 x3 (attention_tf32) through these maps.
+    bool tf32_attn = false;
+    void *qkv_lo = nullptr;
+    AttnMapsF32 attn_hi{}, attn_lo{};
     uint64_t h2d_bytes = 0;
     std::vector<int32_t> row_start, row_len;
     // Packing rows that are in device memory (turbo_b200_embed_write_device):
@@ -238,7 +244,7 @@ struct Session {
 
     ~Session() {
         DeviceScope ds(ctx->device);
-        for (void *p : {x, xn, qkv, ctxb, ffn, (void *)plan_dev, (void *)head_wt, (void *)head_bp, (void *)head_wc,
+        for (void *p : {x, xn, qkv, qkv_lo, ctxb, ffn, (void *)plan_dev, (void *)head_wt, (void *)head_bp, (void *)head_wc,
                         (void *)head_scores, (void *)pack_dev})
             cudaFree(p);
         if (plan_host) cudaFreeHost(plan_host);
@@ -717,11 +723,13 @@ PlanLayout plan_layout(int tokens, int vectors, int attn_items, int attn2_items)
 }
 
 // The session's attention kernel: tcgen05 for head width 64 at F16/BF16,
-// mma.sync for 16 and 32, the SIMT kernel at EXACT and for other widths.
-enum class AttnKind { TC, MMA, SIMT };
+// mma.sync for 16 and 32; at EXACT tcgen05 kind::tf32 (three products) when
+// the session's QKV GEMM writes the lo halves, else the FFMA kernel; SIMT
+// for other widths.
+enum class AttnKind { TC, MMA, SIMT, TF32 };
 AttnKind attention_kind(const Session *s) {
     const int dh = s->m->hidden / s->m->heads;
-    if (s->dt == Dt::F32) return AttnKind::SIMT;
+    if (s->dt == Dt::F32) return s->tf32_attn ? AttnKind::TF32 : AttnKind::SIMT;
     if (dh == 64) return AttnKind::TC;
     return attention_mma_takes(dh) ? AttnKind::MMA : AttnKind::SIMT;
 }
@@ -737,7 +745,8 @@ bool attention_pairs(const Session *s) {
 }
 int attention_queries(const Session *s) {
     switch (attention_kind(s)) {
-    case AttnKind::TC: return ATTN_TC_QUERIES;
+    case AttnKind::TC:
+    case AttnKind::TF32: return ATTN_TC_QUERIES;
     case AttnKind::MMA: return ATTN_MMA_QUERIES;
     default: return ATTN_F32_QUERIES;
     }
@@ -789,6 +798,18 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         s->fuse_ln_pre = on && m->modern && gemm_ln_dual_takes(m->hidden, m->hidden) &&
                          gemm_ln_dual_takes(m->hidden, m->inter);
     }
+    if (dt == Dt::F32) {
+        // The EXACT tier's GEMMs on tcgen05 kind::tf32 with the three-product
+        // split, unless the environment sets TB_EXACT_TF32=0 (then the FFMA
+        // kernel, one F32 chain over k per output); its attention on the
+        // same, unless TB_EXACT_TF32_ATTN=0 (then the FFMA attention).
+        const char *v = getenv("TB_EXACT_TF32");
+        s->exact_tf32 = !(v && v[0] == '0');
+        const char *va = getenv("TB_EXACT_TF32_ATTN");
+        Epilogue store;
+        s->tf32_attn = s->exact_tf32 && !(va && va[0] == '0') && !m->modern && m->hidden / m->heads == 64 &&
+                       gemm_tf32_takes(3 * m->hidden, m->hidden, store);
+    }
     const int qt = attention_queries(s.get());
     s->max_attn_items = (int)(cap / qt) + s->max_batch + 1;
     s->max_attn2_items = attention_pairs(s.get()) ? (int)(cap / ATTN_TC2_QUERIES) + s->max_batch + 1 : 0;
@@ -810,6 +831,7 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
     cudaError_t e = alloc(&s->x, rows * h * es);
     if (e == cudaSuccess && m->modern) e = alloc(&s->xn, rows * h * es);
     if (e == cudaSuccess) e = alloc(&s->qkv, rows * 3 * h * es);
+    if (e == cudaSuccess && s->tf32_attn) e = alloc(&s->qkv_lo, rows * 3 * h * 4);
     if (e == cudaSuccess) e = alloc(&s->ctxb, rows * h * es);
     if (e == cudaSuccess) e = alloc(&s->ffn, rows * I * es);
     if (e == cudaSuccess) e = alloc((void **)&s->plan_dev, s->lay.total);
@@ -847,11 +869,8 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         if (e == cudaSuccess) e = make_operand_map_f32((const float *)s->ctxb, rows, h, h, &s->map_ctx);
         if (e == cudaSuccess) e = make_operand_map_f32((const float *)s->ffn, rows, I, I, &s->map_ffn);
         if (e == cudaSuccess && m->modern) e = make_operand_map_f32((const float *)s->xn, rows, h, h, &s->map_xn);
-        // The EXACT tier's GEMMs on tcgen05 kind::tf32 with the three-product
-        // split, unless the environment sets TB_EXACT_TF32=0 (then the FFMA
-        // kernel, one F32 chain over k per output).
-        const char *v = getenv("TB_EXACT_TF32");
-        s->exact_tf32 = !(v && v[0] == '0');
+        if (e == cudaSuccess && s->tf32_attn) e = make_attn_maps_f32((const float *)s->qkv, rows, h, &s->attn_hi);
+        if (e == cudaSuccess && s->tf32_attn) e = make_attn_maps_f32((const float *)s->qkv_lo, rows, h, &s->attn_lo);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return cuda_fail(err, e, "session_open");
@@ -859,7 +878,10 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         tuning->tuned = TURBO_TUNED_DEFAULT;
         tuning->tune_ms = 0;
         snprintf(tuning->choices, TURBO_CHOICES_LEN, "%s",
-                 dt == Dt::F32 ? "gemm=ffma attention=f32" : "gemm=tcgen05 attention=mma");
+                 dt != Dt::F32       ? "gemm=tcgen05 attention=tcgen05"
+                 : !s->exact_tf32 ? "gemm=ffma attention=f32"
+                 : s->tf32_attn   ? "gemm=tf32x3 attention=tf32x3"
+                                  : "gemm=tf32x3 attention=f32");
         if (tuning->struct_size >= offsetof(turbo_backend_tuning, numerics_used) + 4)
             tuning->numerics_used = tuning->numerics_allowed;
     }
@@ -1178,6 +1200,9 @@ cudaError_t encode(Session *s) {
         if (kind == AttnKind::TC)
             return attention_tc(dt, s->map_qkv, s->map_qkv64, s->ctxb, pk.tok_live, items, s->n_attn, m->heads, dh, h, window,
                                 s->ctx->fault_dev, st);
+        if (kind == AttnKind::TF32)
+            return attention_tf32(s->attn_hi, s->attn_lo, (const float *)s->qkv, (float *)s->ctxb, pk.tok_live, items,
+                                  s->n_attn, m->heads, dh, h, window, s->ctx->fault_dev, st);
         if (kind == AttnKind::SIMT)
             return attention_simt(dt, s->qkv, s->ctxb, pk.tok_live, items, s->n_attn, m->heads, dh, h, window,
                                   s->max_len, st);
@@ -1196,6 +1221,7 @@ cudaError_t encode(Session *s) {
             const LayerWeights &L = ws.layers[l];
             Epilogue q;
             q.kind = EPI_STORE, q.bias = L.qkv.bias, q.out = s->qkv, q.ldo = 3 * h;
+            q.out_lo = (float *)s->qkv_lo;  // null unless the attention is attention_tf32
             if ((e = linear(s, &s->map_x, s->x, L.qkv, q, T, &s->out_qkv)) != cudaSuccess) return e;
             if ((e = attention(-1)) != cudaSuccess) return e;
             Epilogue o;

@@ -71,6 +71,9 @@ __device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_add
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// lo = x - hi(x), hi = x with its low 13 mantissa bits cleared.
+__device__ __forceinline__ float tf32_lo(float x) { return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)); }
+
 template <bool PAIR>
 __global__ void __launch_bounds__(512, 1)
 gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
@@ -297,6 +300,13 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
                 float4 *q = reinterpret_cast<float4 *>(y);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                if (e.out_lo) {
+                    float4 *ql = reinterpret_cast<float4 *>(e.out_lo + (int64_t)row * e.ldo + col);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        ql[i] = make_float4(tf32_lo(v[4 * i]), tf32_lo(v[4 * i + 1]), tf32_lo(v[4 * i + 2]),
+                                            tf32_lo(v[4 * i + 3]));
+                }
             }
             if (++acc == 2) acc = 0, acc_phase ^= 1;
         }

@@ -316,8 +316,10 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
     const int h = (int)(heads * head_dim);
     std::vector<AttnItem> items;
     int T = 0, max_len = 0;
+    if (variant == 4 && (dt != Dt::F32 || head_dim != 64))
+        return hook_fail(err, TURBO_E_UNSUPPORTED, "variant 4 takes F32 at head width 64", cudaSuccess);
     const int qt = variant == 0   ? ATTN_MMA_QUERIES
-                   : variant == 2 ? ATTN_TC_QUERIES
+                   : variant == 2 || variant == 4 ? ATTN_TC_QUERIES
                    : variant == 3 ? ATTN_TC2_QUERIES
                                   : ATTN_F32_QUERIES;
     if (variant == 3 && window >= 0) return hook_fail(err, TURBO_E_INVALID_ARGUMENT, "variant 3 has no window", cudaSuccess);
@@ -349,6 +351,25 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
             e = attention_tc(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, fault, 0);
         if (e == cudaSuccess && variant == 3)
             e = attention_tc2(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, fault, 0);
+    }
+    else if (variant == 4) {
+        // The lo halves the EXACT QKV GEMM writes beside qkv, made here.
+        std::vector<float> lo((size_t)T * 3 * h);
+        for (size_t i = 0; i < lo.size(); ++i) {
+            uint32_t b;
+            memcpy(&b, &qkv[i], 4);
+            b &= 0xFFFFE000u;
+            float hi;
+            memcpy(&hi, &b, 4);
+            lo[i] = qkv[i] - hi;
+        }
+        void *dlo = to_device(dv, dt, lo.data(), lo.size(), &e);
+        AttnMapsF32 mh, ml;
+        if (e == cudaSuccess) e = make_attn_maps_f32((const float *)dq, (uint64_t)T, h, &mh);
+        if (e == cudaSuccess) e = make_attn_maps_f32((const float *)dlo, (uint64_t)T, h, &ml);
+        if (e == cudaSuccess)
+            e = attention_tf32(mh, ml, (const float *)dq, (float *)dc, dl, di, (int)items.size(), (int)heads,
+                               (int)head_dim, h, window, fault, 0);
     }
     else e = attention_simt(dt, dq, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, max_len, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();

@@ -43,6 +43,10 @@ struct Epilogue {
     // product's input), row stride ldo2.
     void *out2 = nullptr;
     int64_t ldo2 = 0;
+    // EPI_STORE of the EXACT tier's tf32 GEMM: also x - hi(x) of each output
+    // (hi = x with the low 13 mantissa bits cleared), same index and stride:
+    // the lo halves attention_tf32 reads.
+    float *out_lo = nullptr;
 };
 
 // The packed batch of one run, in device memory: each packed token's id,
@@ -156,6 +160,20 @@ cudaError_t make_operand_map_f32(const float *ptr, uint64_t rows, uint64_t cols,
 bool gemm_tf32_takes(int N, int K, const Epilogue &e);
 cudaError_t gemm_tf32(const CUtensorMap &a_map, const CUtensorMap &w_map, int M, int N, int K, const Epilogue &epi,
                       int sms, int *fault, cudaStream_t s, int pair = -1);
+
+// The EXACT tier's attention on tcgen05 kind::tf32 with the three-product
+// split (attention_tf32.cu), head width 64: F32 qkv [rows, 3 hidden] and its
+// lo halves (Epilogue::out_lo), each through a pair of TMA maps ([128 x 32]
+// and [64 x 32] boxes), and qkv itself (V is read directly); items of
+// ATTN_TC_QUERIES queries.
+struct AttnMapsF32 {
+    CUtensorMap q, kv;
+};
+cudaError_t make_attn_maps_f32(const float *qkv, uint64_t rows, int hidden, AttnMapsF32 *out);
+cudaError_t attention_tf32(const AttnMapsF32 &hi, const AttnMapsF32 &lo, const float *qkv, float *ctx,
+                           const uint8_t *tok_live,
+                           const AttnItem *items, int n_items, int heads, int head_dim, int hidden, int window,
+                           int *fault, cudaStream_t s);
 
 // Whether EPI_RESIDUAL_LN runs for rows of n columns at dt: n = 768 or 1024
 // and the device fits at least one cluster of n / 128 CTAs.
