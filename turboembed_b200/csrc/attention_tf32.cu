@@ -84,6 +84,23 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, u
         "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
 }
 
+// 32 columns of this warp's 32 TMEM lanes from registers, not waited for
+// (tcgen05.wait::st before anything reads them).
+__device__ __forceinline__ void tmem_st32_issue(uint32_t taddr, const float *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
 __device__ __forceinline__ float tf32_lo(float x) { return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)); }
 
 // Keys [klo, khi) the query tile at q0 of a row of len tokens reads.
@@ -173,14 +190,16 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
             sv[i] = ex2(fmaf(sv[i], SCALE_LOG2, -mu));  // 0 for an invalid key (2^-inf)
             s4[i & 3] += sv[i];
         }
-        // P over the chunk's S columns, then P_lo beside it.
-        __syncwarp();
-        tmem_st32(lane_base, sv);
-        tmem_st32(lane_base + 32, sv + 32);
+        // P over the chunk's S columns and P_lo beside it: four stores, one wait.
+        float lo[64];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) sv[i] = tf32_lo(sv[i]);
-        tmem_st32(lane_base + 64, sv);
-        tmem_st32(lane_base + 96, sv + 32);
+        for (int i = 0; i < 64; ++i) lo[i] = tf32_lo(sv[i]);
+        __syncwarp();
+        tmem_st32_issue(lane_base, sv);
+        tmem_st32_issue(lane_base + 32, sv + 32);
+        tmem_st32_issue(lane_base + 64, lo);
+        tmem_st32_issue(lane_base + 96, lo + 32);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
         tc_fence_before();
         mbar_arrive(bar_p);
