@@ -286,8 +286,15 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows per GPU instead of the config's: a smaller case of the same distribution for profiler "
+                         "captures (the line names it in config.rows_per_gpu_override)")
     args = ap.parse_args()
     wl = WORKLOADS[args.config]
+    if args.rows > 0:
+        import copy
+        wl = copy.copy(wl)
+        wl.per_gpu = args.rows
     if args.impl == "reference":
         return run_reference(args, wl)
     rank, world, local = env_rank()
@@ -492,7 +499,8 @@ def main():
                        "model": f"{wl.model} (random init, seed {wl.seed})", "global_batch": wl.per_gpu * world,
                        "seq_len": wl.seq, "parallelism": f"dp{world}", "live_tokens_per_gpu": live,
                        "vectors_per_gpu": n_vec,
-                       "l2": "no flush: every step streams more than the 126 MB L2 (weights + activations)"},
+                       "l2": "no flush: every step streams more than the 126 MB L2 (weights + activations)",
+                       **({"rows_per_gpu_override": args.rows} if args.rows > 0 else {})},
             "per_gpu_tokens_per_s": value / world,
             "wall_tokens_per_s": tokens_all * args.steps / wall,
             "tensor_frac_whole_step": (gemm_flops_step + attn_flops_step) / (step_ms / 1000) / 1e12 / peak,

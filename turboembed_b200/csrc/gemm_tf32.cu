@@ -18,8 +18,11 @@
 //   warps 4..7    the split: in each stage lo = x - hi into the lo halves
 //                 (same swizzled layout), hi = x with its low 13 mantissa
 //                 bits cleared; then a proxy fence and the arrival for the
-//                 MMA (pairs: one a CTA, on the leader's barrier, released
-//                 at cluster scope). hi is not written back: the tensor core
+//                 MMA (pairs: one a CTA, on the leader's barrier, with the
+//                 default CTA-scope release: the proxy fence orders the lo
+//                 halves for the tensor core, and a cluster-scope release
+//                 would first wait for every store of the CTA in flight,
+//                 measured 18% slower on c2x). hi is not written back: the tensor core
 //                 reads an F32 operand of kind::tf32 by its top 19 bits
 //                 (measured on B200: the products are bit-equal to those of
 //                 operands with the low 13 bits cleared in shared memory,
@@ -65,12 +68,6 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t da, uin
             tmem_d),
         "l"(da), "l"(db), "r"(idesc), "r"(acc));
 }
-// Arrival on a cluster peer's barrier that releases this thread's (and, after
-// a CTA barrier, its CTA's) shared-memory writes at cluster scope.
-__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
 // lo = x - hi(x), hi = x with its low 13 mantissa bits cleared.
 __device__ __forceinline__ float tf32_lo(float x) { return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)); }
 
@@ -192,7 +189,7 @@ gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__
                 fence_async_smem();  // the lo halves, written by threads, are read by the tensor core
                 if constexpr (PAIR) {
                     asm volatile("bar.sync 1, 128;" ::: "memory");  // the four split warps
-                    if (t == 0) mbar_arrive_release_cluster(split_lead + 8 * stage);
+                    if (t == 0) mbar_arrive_remote(split_lead + 8 * stage);
                 } else {
                     mbar_arrive(split0 + 8 * stage);
                 }
