@@ -28,10 +28,13 @@
 //
 // One 128-query tile a CTA (persistent over units (row, tile, head)), one
 // CTA an SM (shared memory: Q and Q_lo 64 KB, two chunk buffers of K, K_lo,
-// V^T, V^T_lo 64 KB each), 288 threads: warps 0..3 the softmax (thread r =
-// query row r = TMEM lane r), warp 4 lane 0 the loads and the MMAs in the
-// order of attention_tc.cu's one-tile kernel, warps 5..8 the transposer.
-// TMEM: S / P in columns 0..63, P_lo in 64..127, O in 128..191. The softmax
+// V^T, V^T_lo 64 KB each), 320 threads: warps 0..3 the softmax (thread r =
+// query row r = TMEM lane r), warp 4 lane 0 the MMAs, warps 5..8 the
+// transposer, warp 9 lane 0 the TMA loads of Q and K. TMEM (512 columns):
+// two S / P buffers (0..63, 64..127), two P_lo buffers (128..191,
+// 192..255), O in 256..319; chunk y uses buffer y & 1, and S(y + 2) is
+// issued right after P V(y), so the tensor core computes the next scores
+// while the softmax works on the current ones. The softmax
 // keeps a reference max per row that moves only when a chunk's max passes
 // it by more than 8 (log2 units), and then rescales O in TMEM and the row
 // sum. Waits are bounded (2 s) and end in the fault word.
@@ -114,8 +117,10 @@ __device__ __forceinline__ void key_range(int len, int q0, int window, int &klo,
 }
 
 // The softmax warpgroup's pass over one tile: chunks of keys [klo, khi); g
-// counts chunks (barrier phases). lane_base addresses this warp's TMEM lanes
-// at column 0. Returns false when the kernel must stop.
+// counts chunks (barrier phases); bar_s, bar_p and bar_o are the first of
+// each pair of per-buffer barriers (chunk g uses buffer g & 1, so that every
+// wait finds the phase before the awaited one complete). lane_base addresses this warp's TMEM lanes at column 0. Returns
+// false when the kernel must stop.
 __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int khi, int window, int head,
                                              float *__restrict__ ctx, int h, const uint8_t *__restrict__ live,
                                              uint32_t lane_base, int r, uint32_t bar_s, uint32_t bar_p,
@@ -138,14 +143,17 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
             km1 = __ballot_sync(0xffffffffu, key < khi && live[it.start + key]);
         }
         const bool full = window < 0 && (km0 & km1) == 0xffffffffu;
-        if (!mbar_wait(bar_s, g & 1, abort_flag, fault)) return false;
+        // Chunk g's buffer: S / P columns sc, P_lo columns 128 + sc. Its S
+        // commit also covers P V(g - 2), the buffer's last reader.
+        const uint32_t sb = g & 1, sc = sb * 64;
+        if (!mbar_wait(bar_s + 8 * sb, (g >> 1) & 1, abort_flag, fault)) return false;
         tc_fence_after();
         float sv[64];
         {
             uint32_t raw[64];
             __syncwarp();
-            tmem_ld32_async(lane_base, raw);
-            tmem_ld32_async(lane_base + 32, raw + 32);
+            tmem_ld32_async(lane_base + sc, raw);
+            tmem_ld32_async(lane_base + sc + 32, raw + 32);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 64; ++i) sv[i] = __uint_as_float(raw[i]);
@@ -173,14 +181,18 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
             m_ref = mx;
         }
         if (j > 0 && __any_sync(0xffffffffu, move)) {
+            // O holds P V(g - 1) once it is done (S(g)'s commit covers only
+            // P V(g - 2)).
+            if (!mbar_wait(bar_o + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, abort_flag, fault)) return false;
+            tc_fence_after();
             __syncwarp();
 #pragma unroll 1
             for (int q = 0; q < 4; ++q) {
                 float o[16];
-                tmem_ld16(lane_base + 128 + q * 16, o);
+                tmem_ld16(lane_base + 256 + q * 16, o);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) o[i] *= f;
-                tmem_st16(lane_base + 128 + q * 16, o);
+                tmem_st16(lane_base + 256 + q * 16, o);
             }
         }
         const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
@@ -195,16 +207,18 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
 #pragma unroll
         for (int i = 0; i < 64; ++i) lo[i] = tf32_lo(sv[i]);
         __syncwarp();
-        tmem_st32_issue(lane_base, sv);
-        tmem_st32_issue(lane_base + 32, sv + 32);
-        tmem_st32_issue(lane_base + 64, lo);
-        tmem_st32_issue(lane_base + 96, lo + 32);
+        tmem_st32_issue(lane_base + sc, sv);
+        tmem_st32_issue(lane_base + sc + 32, sv + 32);
+        tmem_st32_issue(lane_base + 128 + sc, lo);
+        tmem_st32_issue(lane_base + 128 + sc + 32, lo + 32);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
         tc_fence_before();
-        mbar_arrive(bar_p);
+        mbar_arrive(bar_p + 8 * sb);
     }
-    if (!mbar_wait(bar_o, (g - 1) & 1, abort_flag, fault)) return false;
+    // P V(g - 1), the unit's last, is done (its buffer's barrier: the use
+    // before, P V(g - 3), is covered by S(g - 1)'s commit).
+    if (!mbar_wait(bar_o + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, abort_flag, fault)) return false;
     tc_fence_after();
     __syncwarp();
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
@@ -212,7 +226,7 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
         float o[32];
-        tmem_ld32(lane_base + 128 + half * 32, o);
+        tmem_ld32(lane_base + 256 + half * 32, o);
         if (qi < it.len) {
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -224,27 +238,37 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
     return true;
 }
 
-// The transposer's pass over chunk j of a unit: V rows [k0, k0 + 64) of the
-// head at column col, keys at or past khi written as zeros, into V^T (hi:
+// The transposer's pass over one chunk: V rows [k0, k0 + 64) of the head at
+// column col, keys at or past khi taken as zeros (load_v), into V^T (hi:
 // the values as they are, read by the tensor core as TF32) and V^T_lo, each
-// two K-major boxes [64 d x 32 keys] with the 128-byte swizzle. Thread t of
-// 128 moves two 4 x 4 blocks (4 keys x 4 columns of d): 16-byte loads (a
-// warp reads 8 keys x 64 contiguous bytes) and 16-byte stores of 4 keys of
-// one d (the 8 lanes of a store phase hit 8 distinct 16-byte bank groups).
-__device__ __forceinline__ void transpose_v(const float *__restrict__ qkv, int64_t ld, int start, int k0, int khi,
-                                            int col, uint8_t *vth, uint8_t *vtl, int t) {
+// two K-major boxes [64 d x 32 keys] with the 128-byte swizzle (store_vt).
+// Thread t of 128 moves two 4 x 4 blocks (4 keys x 4 columns of d): 16-byte
+// loads (a warp reads 8 keys x 64 contiguous bytes) and 16-byte stores of 4
+// keys of one d (the 8 lanes of a store phase hit 8 distinct 16-byte bank
+// groups). The loads of the next chunk are issued before this chunk is
+// stored, so two chunks' loads are in flight.
+__device__ __forceinline__ void load_v(const float *__restrict__ qkv, int64_t ld, int start, int k0, int khi, int col,
+                                       int t, float4 (&v)[8]) {
     const int lane = t & 31, w = t >> 5;
     const int g = (lane >> 3) + 4 * w;  // d columns 4 g .. 4 g + 3
 #pragma unroll
     for (int itr = 0; itr < 2; ++itr) {
         const int kq = (lane & 7) + 8 * itr;  // keys 4 kq .. 4 kq + 3 of the chunk
-        float4 v[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int k = k0 + 4 * kq + r;
-            v[r] = k < khi ? *reinterpret_cast<const float4 *>(qkv + (int64_t)(start + k) * ld + col + 4 * g)
-                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            v[4 * itr + r] = k < khi ? *reinterpret_cast<const float4 *>(qkv + (int64_t)(start + k) * ld + col + 4 * g)
+                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
+    }
+}
+__device__ __forceinline__ void store_vt(const float4 (&vv)[8], uint8_t *vth, uint8_t *vtl, int t) {
+    const int lane = t & 31, w = t >> 5;
+    const int g = (lane >> 3) + 4 * w;
+#pragma unroll
+    for (int itr = 0; itr < 2; ++itr) {
+        const int kq = (lane & 7) + 8 * itr;
+        const float4 *v = vv + 4 * itr;
         const int box = kq >> 3, c = kq & 7;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -259,7 +283,7 @@ __device__ __forceinline__ void transpose_v(const float *__restrict__ qkv, int64
     }
 }
 
-__global__ void __launch_bounds__(288, 1)
+__global__ void __launch_bounds__(320, 1)
 attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
                  const __grid_constant__ CUtensorMap tq_lo, const __grid_constant__ CUtensorMap tkv_lo,
                  const float *__restrict__ qkv, float *__restrict__ ctx, const uint8_t *__restrict__ live,
@@ -268,33 +292,36 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sQ = smem, *sBuf = smem + 2 * Q_BYTES;  // Q, Q_lo; then 2 x (K, K_lo, V^T, V^T_lo)
     uint8_t *bars = sBuf + 2 * BUF_BYTES;
-    // Q in, K in [2], V^T written [2], S done, P written, P V done, V^T
-    // free [2] (the P V that read it is done).
-    const uint32_t bar_q = smem_u32(bars), bar_k = bar_q + 8, bar_v = bar_q + 24, bar_s = bar_q + 40;
-    const uint32_t bar_p = bar_q + 48, bar_o = bar_q + 56, bar_vf = bar_q + 80;
-    uint32_t *tmem_slot = (uint32_t *)(bars + 64);
-    volatile int *abort_flag = (volatile int *)(bars + 72);
+    // Q in, Q free (the unit's last S is done), and per buffer: K in, K
+    // free, V^T written, V^T free (the P V that read it is done), S done, P
+    // written, P V done.
+    const uint32_t bar_q = smem_u32(bars), bar_qf = bar_q + 8, bar_k = bar_q + 16, bar_kf = bar_q + 32;
+    const uint32_t bar_v = bar_q + 48, bar_vf = bar_q + 64, bar_s = bar_q + 80, bar_p = bar_q + 96, bar_o = bar_q + 112;
+    uint32_t *tmem_slot = (uint32_t *)(bars + 128);
+    volatile int *abort_flag = (volatile int *)(bars + 136);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int units = n_items * heads;
 
     if (threadIdx.x == 0) {
         mbar_init(bar_q, 1);
+        mbar_init(bar_qf, 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar_k + 8 * i, 1);
+            mbar_init(bar_kf + 8 * i, 1);
             mbar_init(bar_v + 8 * i, 128);  // every transposer thread
             mbar_init(bar_vf + 8 * i, 1);
+            mbar_init(bar_s + 8 * i, 1);
+            mbar_init(bar_p + 8 * i, 128);
+            mbar_init(bar_o + 8 * i, 1);
         }
-        mbar_init(bar_s, 1);
-        mbar_init(bar_p, 128);
-        mbar_init(bar_o, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
     if (warp == 4) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(256u));
+                     "r"(512u));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     __syncthreads();
@@ -303,48 +330,39 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     pdl_wait();  // qkv, qkv_lo and the plan are an earlier kernel's and copy's
     pdl_trigger();
 
+    // This CTA's chunks in order: unit u = blockIdx.x + k * gridDim.x, chunk j
+    // of its nch. Every role walks the same sequence.
+    struct Cur {
+        int u, j, nch;
+    };
+    auto nch_of = [&](int u) -> int {
+        if (u >= units) return 0;
+        const AttnItem it = items[u / heads];
+        int klo, khi;
+        key_range(it.len, it.q0, window, klo, khi);
+        return (khi - klo + KT - 1) / KT;
+    };
+    auto advance = [&](Cur &c) {
+        if (++c.j >= c.nch) c.u += (int)gridDim.x, c.j = 0, c.nch = nch_of(c.u);
+    };
     if (warp == 4) {
         if (lane == 0) {
-            // Chunk y (counted over this CTA's units) uses buffer y & 1. P V(y)
-            // reads P from the S columns and S(y + 1) follows it into them (in
-            // issue order). When P(y) arrives, S(y) and P V(y - 1) are done:
-            // K(y + 1) can go into buffer (y + 1) & 1 once S(y) is issued.
-            // V^T(y) comes from the transposer, which refills a buffer once
-            // the P V that read it is done (bar_vf). The next unit's Q goes in
-            // once this unit's last S is done.
+            // The MMAs, in order S(0), S(1), then per chunk y: P V(y) once
+            // P(y) and V^T(y) are in, and S(y + 2) into the buffer P V(y)
+            // has just read (in issue order) once K(y + 2) (and, for a
+            // unit's first chunk, its Q) is in. Each S commits its buffer's
+            // S barrier and frees its K buffer; a unit's last S frees Q.
             const uint32_t ids = idesc_tf32(KT, false), idpv = idesc_tf32(D, false);
             const uint32_t aq = smem_u32(sQ), aql = aq + Q_BYTES, ab = smem_u32(sBuf);
-            struct Unit {
-                int row0, qrow, col, nch;
-            };
-            auto unit_of = [&](int u) {
-                if (u >= units) return Unit{0, 0, 0, 0};
-                const AttnItem it = items[u / heads];
-                int klo, khi;
-                key_range(it.len, it.q0, window, klo, khi);
-                return Unit{it.start + klo, it.start + it.q0, (u % heads) * D, (khi - klo + KT - 1) / KT};
-            };
-            auto load_q = [&](const Unit &n) {
-                mbar_expect_tx(bar_q, 2 * Q_BYTES);
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    tma_load_2d(aq + hf * Q_BOX, &tq, n.col + 32 * hf, n.qrow, bar_q);
-                    tma_load_2d(aql + hf * Q_BOX, &tq_lo, n.col + 32 * hf, n.qrow, bar_q);
+            Cur sc{(int)blockIdx.x, 0, nch_of(blockIdx.x)}, pc = sc;
+            uint32_t zs = 0, y = 0, qn = 0;  // S issued, P V issued, units begun
+            auto issue_s_next = [&]() -> bool {
+                const uint32_t b = zs & 1;
+                if (sc.j == 0) {
+                    if (!mbar_wait(bar_q, qn & 1, abort_flag, fault)) return false;
+                    ++qn;
                 }
-            };
-            // K of chunk j of unit n into buffer y & 1: hi then lo.
-            auto load_k = [&](const Unit &n, int j, uint32_t y) {
-                const uint32_t b = y & 1, bar = bar_k + 8 * b;
-                const uint32_t dst = ab + b * BUF_BYTES;
-                mbar_expect_tx(bar, 2 * KV_BYTES);
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int x = h + n.col + 32 * hf, yrow = n.row0 + j * KT;
-                    tma_load_2d(dst + hf * K_BOX, &tkv, x, yrow, bar);
-                    tma_load_2d(dst + KV_BYTES + hf * K_BOX, &tkv_lo, x, yrow, bar);
-                }
-            };
-            auto issue_s = [&](uint32_t b) {
+                if (!mbar_wait(bar_k + 8 * b, (zs >> 1) & 1, abort_flag, fault)) return false;
                 tc_fence_after();
                 const uint32_t kh = ab + b * BUF_BYTES, kl = kh + KV_BYTES;
 #pragma unroll
@@ -353,89 +371,108 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                     const uint64_t off = (uint64_t)((kk & 3) * 2);  // 32 bytes a K = 8 step, in 16-byte units
                     const uint64_t qh = smem_desc(aq + box * Q_BOX) + off, ql = smem_desc(aql + box * Q_BOX) + off;
                     const uint64_t dkh = smem_desc(kh + box * K_BOX) + off, dkl = smem_desc(kl + box * K_BOX) + off;
-                    umma_tf32(tmem, ql, dkh, ids, kk > 0 ? 1u : 0u);
-                    umma_tf32(tmem, qh, dkl, ids, 1u);
-                    umma_tf32(tmem, qh, dkh, ids, 1u);
+                    umma_tf32(tmem + b * 64, ql, dkh, ids, kk > 0 ? 1u : 0u);
+                    umma_tf32(tmem + b * 64, qh, dkl, ids, 1u);
+                    umma_tf32(tmem + b * 64, qh, dkh, ids, 1u);
                 }
-                umma_commit(bar_s);
+                umma_commit(bar_s + 8 * b);
+                umma_commit(bar_kf + 8 * b);
+                if (sc.j + 1 == sc.nch) umma_commit(bar_qf);
+                ++zs;
+                advance(sc);
+                return true;
             };
-            auto issue_pv = [&](uint32_t b, bool acc) {
+            bool ok = true;
+            for (int i = 0; i < 2 && ok && sc.u < units; ++i) ok = issue_s_next();
+            while (ok && pc.u < units) {
+                const uint32_t b = y & 1;
+                if (!(ok = mbar_wait(bar_p + 8 * b, (y >> 1) & 1, abort_flag, fault))) break;
+                if (!(ok = mbar_wait(bar_v + 8 * b, (y >> 1) & 1, abort_flag, fault))) break;
                 tc_fence_after();
                 const uint32_t vh = ab + b * BUF_BYTES + 2 * KV_BYTES, vl = vh + KV_BYTES;
+                const uint32_t pa = tmem + b * 64, pl = tmem + 128 + b * 64;
 #pragma unroll
                 for (int kk = 0; kk < KT / 8; ++kk) {
                     // B = V^T [64 d x 8 keys]; A = P / P_lo columns kk*8 .. kk*8+7.
                     const uint32_t box = (uint32_t)(kk >> 2);
                     const uint64_t off = (uint64_t)((kk & 3) * 2);
                     const uint64_t dvh = smem_desc(vh + box * K_BOX) + off, dvl = smem_desc(vl + box * K_BOX) + off;
-                    umma_tf32_ts(tmem + 128, tmem + 64 + kk * 8, dvh, idpv, (acc || kk) ? 1u : 0u);
-                    umma_tf32_ts(tmem + 128, tmem + kk * 8, dvl, idpv, 1u);
-                    umma_tf32_ts(tmem + 128, tmem + kk * 8, dvh, idpv, 1u);
+                    umma_tf32_ts(tmem + 256, pl + kk * 8, dvh, idpv, (pc.j > 0 || kk) ? 1u : 0u);
+                    umma_tf32_ts(tmem + 256, pa + kk * 8, dvl, idpv, 1u);
+                    umma_tf32_ts(tmem + 256, pa + kk * 8, dvh, idpv, 1u);
                 }
-                umma_commit(bar_o);
+                umma_commit(bar_o + 8 * b);
                 umma_commit(bar_vf + 8 * b);
-            };
-            const int grid = (int)gridDim.x;
-            int u = blockIdx.x;
-            Unit cur = unit_of(u), nxt = unit_of(u + grid);
-            auto load_after = [&](int j, uint32_t y) {
-                if (j + 1 < cur.nch) load_k(cur, j + 1, y + 1);
-                else if (nxt.nch > 0) load_k(nxt, 0, y + 1);
-            };
-            uint32_t y = 0, qn = 0;
-            bool ok = true;
-            if (u < units) {
-                load_q(cur);
-                load_k(cur, 0, 0);
-                load_after(0, 0);
-            }
-            for (; u < units && ok; u += grid, ++qn) {
-                if (!(ok = mbar_wait(bar_q, qn & 1, abort_flag, fault))) break;
-                if (!(ok = mbar_wait(bar_k + 8 * (y & 1), (y >> 1) & 1, abort_flag, fault))) break;
-                issue_s(y & 1);
-                if (y >= 1) load_after(0, y);
-                if (cur.nch == 1) {
-                    if (!(ok = mbar_wait(bar_s, y & 1, abort_flag, fault))) break;
-                    if (nxt.nch > 0) load_q(nxt);
-                }
-                for (int j = 0; j < cur.nch && ok; ++j, ++y) {
-                    if (!(ok = mbar_wait(bar_p, y & 1, abort_flag, fault))) break;
-                    if (!(ok = mbar_wait(bar_v + 8 * (y & 1), (y >> 1) & 1, abort_flag, fault))) break;
-                    issue_pv(y & 1, j > 0);
-                    if (j + 1 < cur.nch) {
-                        if (!(ok = mbar_wait(bar_k + 8 * ((y + 1) & 1), ((y + 1) >> 1) & 1, abort_flag, fault))) break;
-                        issue_s((y + 1) & 1);
-                        load_after(j + 1, y + 1);
-                        if (j + 2 == cur.nch) {
-                            if (!(ok = mbar_wait(bar_s, (y + 1) & 1, abort_flag, fault))) break;
-                            if (nxt.nch > 0) load_q(nxt);
-                        }
-                    }
-                }
-                cur = nxt;
-                nxt = unit_of(u + 2 * grid);
+                ++y;
+                advance(pc);
+                if (sc.u < units) ok = issue_s_next();
             }
         }
-    } else if (warp >= 5) {
+    } else if (warp == 9) {
+        if (lane == 0) {
+            // TMA: a unit's Q (hi and lo) once the previous unit's last S is
+            // done, each chunk's K (hi and lo) once the S two chunks back,
+            // which read its buffer, is done.
+            const uint32_t aq = smem_u32(sQ), aql = aq + Q_BYTES, ab = smem_u32(sBuf);
+            Cur c{(int)blockIdx.x, 0, nch_of(blockIdx.x)};
+            uint32_t z = 0, qn = 0;
+            while (c.u < units) {
+                const AttnItem it = items[c.u / heads];
+                int klo, khi;
+                key_range(it.len, it.q0, window, klo, khi);
+                const int col = (c.u % heads) * D;
+                if (c.j == 0) {
+                    if (qn >= 1 && !mbar_wait(bar_qf, (qn - 1) & 1, abort_flag, fault)) break;
+                    mbar_expect_tx(bar_q, 2 * Q_BYTES);
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        tma_load_2d(aq + hf * Q_BOX, &tq, col + 32 * hf, it.start + it.q0, bar_q);
+                        tma_load_2d(aql + hf * Q_BOX, &tq_lo, col + 32 * hf, it.start + it.q0, bar_q);
+                    }
+                    ++qn;
+                }
+                const uint32_t b = z & 1;
+                if (z >= 2 && !mbar_wait(bar_kf + 8 * b, ((z >> 1) & 1) ^ 1, abort_flag, fault)) break;
+                mbar_expect_tx(bar_k + 8 * b, 2 * KV_BYTES);
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int x = h + col + 32 * hf, yrow = it.start + klo + c.j * KT;
+                    tma_load_2d(ab + b * BUF_BYTES + hf * K_BOX, &tkv, x, yrow, bar_k + 8 * b);
+                    tma_load_2d(ab + b * BUF_BYTES + KV_BYTES + hf * K_BOX, &tkv_lo, x, yrow, bar_k + 8 * b);
+                }
+                ++z;
+                advance(c);
+            }
+        }
+    } else if (warp >= 5 && warp <= 8) {
         // The transposer: V^T of chunk y into buffer y & 1 once the P V of
-        // chunk y - 2 (the buffer's last reader) is done.
+        // chunk y - 2 (the buffer's last reader) is done; chunk y + 1's loads
+        // are in flight meanwhile.
         const int t = threadIdx.x - 160;
         const int64_t ld = 3 * (int64_t)h;
-        uint32_t y = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-            const AttnItem it = items[u / heads];
+        auto load_chunk = [&](const Cur &c, float4 (&v)[8]) {
+            const AttnItem it = items[c.u / heads];
             int klo, khi;
             key_range(it.len, it.q0, window, klo, khi);
-            const int nch = (khi - klo + KT - 1) / KT, col = 2 * h + (u % heads) * D;
-            for (int j = 0; j < nch; ++j, ++y) {
-                const uint32_t b = y & 1;
-                if (y >= 2 && !(ok = mbar_wait(bar_vf + 8 * b, ((y >> 1) & 1) ^ 1, abort_flag, fault))) break;
-                uint8_t *vth = sBuf + b * BUF_BYTES + 2 * KV_BYTES;
-                transpose_v(qkv, ld, it.start, klo + j * KT, khi, col, vth, vth + KV_BYTES, t);
-                fence_async_smem();  // written by threads, read by the tensor core
-                mbar_arrive(bar_v + 8 * b);
-            }
+            load_v(qkv, ld, it.start, klo + c.j * KT, khi, 2 * h + (c.u % heads) * D, t, v);
+        };
+        Cur c{(int)blockIdx.x, 0, nch_of(blockIdx.x)};
+        float4 cur[8];
+        if (c.u < units) load_chunk(c, cur);
+        for (uint32_t y = 0; c.u < units; ++y) {
+            Cur n = c;
+            advance(n);
+            float4 nx[8];
+            if (n.u < units) load_chunk(n, nx);
+            const uint32_t b = y & 1;
+            if (y >= 2 && !mbar_wait(bar_vf + 8 * b, ((y >> 1) & 1) ^ 1, abort_flag, fault)) break;
+            uint8_t *vth = sBuf + b * BUF_BYTES + 2 * KV_BYTES;
+            store_vt(cur, vth, vth + KV_BYTES, t);
+            fence_async_smem();  // written by threads, read by the tensor core
+            mbar_arrive(bar_v + 8 * b);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) cur[i] = nx[i];
+            c = n;
         }
     } else {
         const int r = threadIdx.x;
@@ -454,7 +491,7 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     __syncthreads();
     if (warp == 4) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u));
     }
 }
 
@@ -505,7 +542,7 @@ cudaError_t attention_tf32(const AttnMapsF32 &hi, const AttnMapsF32 &lo, const f
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int units = n_items * heads;
     const int grid = units < sms ? units : sms;
-    return launch_pdl(attn_tf32_kernel, grid, 288, SMEM, s, hi.q, hi.kv, lo.q, lo.kv, qkv, ctx, tok_live, items,
+    return launch_pdl(attn_tf32_kernel, grid, 320, SMEM, s, hi.q, hi.kv, lo.q, lo.kv, qkv, ctx, tok_live, items,
                       n_items, heads, hidden, window, fault);
 }
 
