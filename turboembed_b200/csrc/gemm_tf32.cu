@@ -22,12 +22,13 @@
 //                 default CTA-scope release: the proxy fence orders the lo
 //                 halves for the tensor core, and a cluster-scope release
 //                 would first wait for every store of the CTA in flight,
-//                 measured 18% slower on c2x). hi is not written back: the tensor core
-//                 reads an F32 operand of kind::tf32 by its top 19 bits
-//                 (measured on B200: the products are bit-equal to those of
-//                 operands with the low 13 bits cleared in shared memory,
-//                 over 1.7e7 outputs; a rounding read would put the error
-//                 near 5e-4, which the F64 accuracy tests bound at 1e-4).
+//                 measured 18% slower on c2x). hi is not written back: the
+//                 tensor core reads an F32 operand of kind::tf32 by its top
+//                 19 bits (measured on B200: the products are bit-equal to
+//                 those of operands with the low 13 bits cleared in shared
+//                 memory, over 1.7e7 outputs; a rounding read would put the
+//                 error near 5e-4, which the F64 accuracy tests bound at
+//                 1e-4).
 //   warp 1        MMA: per k-block 4 steps of K = 8, three products each.
 //   warp 2        TMEM (2 accumulators of 128 or 256 columns).
 //   warps 8..15   epilogue: bias / erf-GELU (erff) / residual / gating in
