@@ -270,6 +270,11 @@ typedef struct turbo_token_range {
 #define TURBO_NUMERIC_TF32           2
 #define TURBO_NUMERIC_F16_F32ACC     4
 #define TURBO_NUMERIC_F16_CHUNKACC   8
+/* Appended by the B200 backend, which computes BF16 models in BF16 where the
+ * reference widens them to F32: BF16 operands, F32 sums. The core's table
+ * allows it nowhere until a decision adds it; a session that is not allowed
+ * it computes in F32 (or F16 at FASTEST). */
+#define TURBO_NUMERIC_BF16_F32ACC   16
 
 typedef struct turbo_backend_tuning {
     uint32_t    struct_size;

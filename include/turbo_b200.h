@@ -115,7 +115,7 @@ TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, u
                                              const float *qkv, const uint8_t *live, uint32_t heads,
                                              uint32_t head_dim, int32_t window, float *ctx_out, turbo_error *err);
 
-/* The cross-encoder head on the device (SURVEY-listed next step after the
+/* The cross-encoder head on the device (the step after the
  * reference's host head, core/src/session/rerank.rs:170-188): set_head
  * uploads a pooler (W_p [h, h] row-major and b_p [h], or NULL for none) and
  * a one-logit classifier (w_c [h], b_c) to the session once; head_scores
@@ -133,8 +133,8 @@ TB_EXPORT int32_t turbo_b200_session_head_scores(void *session, uint32_t n, floa
  * in another framework's memory pool or arena, serving loops that must not
  * pay for an allocation, runtimes that forbid allocation after start-up):
  * they pass their own device buffers and get the tensor-core attention
- * alone. qkv is [tokens, 3 * heads * head_dim] (16-byte aligned), ctx
- * [tokens, heads * head_dim], live [tokens] the mask entries, all device
+ * alone. qkv is [tokens, 3 * heads * head_dim], ctx [tokens, heads *
+ * head_dim] (both 16-byte aligned), live [tokens] the mask entries, all device
  * memory of the current device; lens [batch] (host) the rows' token counts,
  * packed one after another; window < 0 for whole rows. F16 or BF16, head
  * width 64. Asynchronous on `stream` (NULL: the default stream); when

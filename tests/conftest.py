@@ -10,6 +10,32 @@ sys.path.insert(0, str(ROOT))
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
+from turboembed_b200 import abi  # noqa: E402
+
+EXACT, FASTEST, MODEL = abi.TURBO_PRECISION_EXACT, abi.TURBO_PRECISION_FASTEST, abi.TURBO_PRECISION_MODEL
+# Tiers beyond the core's own table (core/src/tuning.rs:23-36), as a core
+# would hand them once a decision widens it: EXACT with TURBO_NUMERIC_TF32
+# allowed beside F32 FMAs (the 3xTF32 tensor-core kernels; the table alone
+# runs the FFMA kernels), and MODEL / FASTEST with BF16 operands allowed
+# (BF16 models computed in BF16; the table alone widens them to F32 at
+# MODEL and narrows them to F16 at FASTEST).
+EXACT_TF32 = (EXACT, abi.TURBO_NUMERIC_F32_FMA | abi.TURBO_NUMERIC_TF32)
+MODEL_BF16 = (MODEL, abi.TURBO_NUMERIC_F32_FMA | abi.TURBO_NUMERIC_BF16_F32ACC)
+
+
+def precision_of(tier):
+    """The TURBO_PRECISION_* of a tier (a precision, or (precision, numerics))."""
+    return tier[0] if isinstance(tier, tuple) else tier
+
+
+def open_session(model, max_batch, max_seq, tier, **kw):
+    """model.session at a tier: the core's numerics for a bare precision,
+    the tier's own for a (precision, numerics) pair."""
+    if isinstance(tier, tuple):
+        return model.session(max_batch, max_seq, tier[0], numerics=tier[1], **kw)
+    return model.session(max_batch, max_seq, tier, **kw)
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA kernels through the C ABI)")
 

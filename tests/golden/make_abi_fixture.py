@@ -37,5 +37,7 @@ def probe(include_dir, header):
 
 
 if __name__ == "__main__":
-    inc = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/include")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_abi_fixture.py <reference include directory>  (holding turbo/turbo.h)")
+    inc = Path(sys.argv[1])
     print(json.dumps(probe(inc, "turbo/turbo_backend.h"), indent=1, sort_keys=True))

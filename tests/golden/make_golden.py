@@ -187,7 +187,9 @@ def quantize_table(ref):
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference checkout>  (the directory holding testdata/)")
+    ref = Path(sys.argv[1])
     tiny_bert(ref)
     tiny_modernbert(ref)
     tiny_xlmr()

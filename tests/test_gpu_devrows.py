@@ -78,3 +78,42 @@ def test_device_rows_refuse_an_empty_row(ctx):
     assert e.value.code == abi.TURBO_E_INVALID_ARGUMENT
     s.release()
     m.release()
+
+
+@pytest.mark.parametrize("bad", ["id_past_vocab", "negative_id", "type_past_types"])
+def test_device_rows_refuse_ids_and_types_out_of_range(ctx, bad):
+    # Host rows arrive checked by the core (core/src/session/tokens.rs:343);
+    # device rows are checked on the device and refused by the host before
+    # any run: the gather never reads past its tables.
+    import torch
+    d = models.synthetic("minilm", 0, layers=1)
+    ids = np.full((3, 16), 1000, np.int32)
+    mask = np.ones((3, 16), np.int32)
+    types = np.zeros((3, 16), np.int32)
+    if bad == "id_past_vocab":
+        ids[2, 5] = 30522
+    elif bad == "negative_id":
+        ids[1, 0] = -1
+    else:
+        types[2, 3] = 2
+    m = ctx.load(d)
+    s = m.session(3, 16, FASTEST)
+    di, dm, dt = (torch.from_numpy(x).cuda() for x in (ids, mask, types))
+    torch.cuda.synchronize()
+    with pytest.raises(runtime.TurboError) as e:
+        s.write_device(di.data_ptr(), dm.data_ptr(), dt.data_ptr(), 3, 16)
+    assert e.value.code == abi.TURBO_E_INVALID_ARGUMENT and "row" in e.value.message
+    with pytest.raises(runtime.TurboError) as e:
+        s.run()  # nothing was written
+    assert e.value.code == abi.TURBO_E_INVALID_STATE
+    # The same session takes good rows afterwards.
+    ids[ids < 0] = 1000
+    ids[ids >= 30522] = 1000
+    types[:] = 0
+    di, dt = torch.from_numpy(ids).cuda(), torch.from_numpy(types).cuda()
+    torch.cuda.synchronize()
+    s.write_device(di.data_ptr(), dm.data_ptr(), dt.data_ptr(), 3, 16)
+    s.run()
+    assert np.isfinite(s.read()).all()
+    s.release()
+    m.release()

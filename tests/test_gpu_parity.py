@@ -9,13 +9,12 @@ core/tests/cuda_runs.rs:67-74): EXACT (F32) cosine >= 0.9999 and max-abs
 import numpy as np
 import pytest
 
-from conftest import cosine, load_golden, mask_from_lengths, rerank_rows
+from conftest import (EXACT, EXACT_TF32, FASTEST, MODEL, MODEL_BF16, cosine, load_golden, mask_from_lengths,
+                      open_session, precision_of, rerank_rows)
 from oracle import oracle
 from turboembed_b200 import abi, models, runtime
 
 pytestmark = pytest.mark.gpu
-
-EXACT, FASTEST, MODEL = abi.TURBO_PRECISION_EXACT, abi.TURBO_PRECISION_FASTEST, abi.TURBO_PRECISION_MODEL
 
 
 @pytest.fixture(scope="module")
@@ -31,19 +30,19 @@ def check(got, want, precision, note=""):
     cos = cosine(got, want).min()
     mad = np.abs(got - want).max()
     print(f"{note} cos={cos:.7f} max_abs={mad:.3e}")
-    if precision == EXACT:
+    if precision_of(precision) == EXACT:
         assert cos >= 0.9999 and mad <= 1e-4, (cos, mad)
     else:
         assert cos >= 0.999, (cos, mad)
     return cos, mad
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST, MODEL])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST, MODEL])
 def test_tiny_bert_reference_cases(ctx, precision):
     a, meta = load_golden("tiny_bert")
     d = models.bert_desc(a, meta)
     m = ctx.load(d)
-    s = m.session(16, 64, precision)
+    s = open_session(m, 16, 64, precision)
     mask = mask_from_lengths(a["lengths"], 64)
     got = s.embed(a["ids"], mask)
     check(got, a["embeddings"], precision, "tiny-bert vs upstream")
@@ -52,12 +51,12 @@ def test_tiny_bert_reference_cases(ctx, precision):
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_tiny_modernbert_reference_cases(ctx, precision):
     a, meta = load_golden("tiny_modernbert")
     d = models.modernbert_desc(a, meta)
     m = ctx.load(d)
-    s = m.session(9, 64, precision)
+    s = open_session(m, 9, 64, precision)
     mask = mask_from_lengths(a["lengths"], 64)
     got = s.embed(a["ids"], mask, normalize=abi.TURBO_NORMALIZE_NONE)
     check(got, a["embeddings"], precision, "tiny-modernbert vs upstream")
@@ -65,15 +64,15 @@ def test_tiny_modernbert_reference_cases(ctx, precision):
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_tiny_xlmr_position_offset(ctx, precision):
     a, meta = load_golden("tiny_xlmr")
     d = models.bert_desc(a, meta)
     m = ctx.load(d)
-    s = m.session(8, 64, precision)
+    s = open_session(m, 8, 64, precision)
     got = s.embed(a["ids"], a["mask"])
     check(got, a["embeddings"], precision, "tiny-xlmr vs transformers")
-    if precision == EXACT:
+    if precision_of(precision) == EXACT:
         # The reference's EXACT bound against arithmetic in F64
         # (core/tests/cuda_runs.rs:68): |got - w| <= 1e-5 (1 + |w|).
         want = a["embeddings"].astype(np.float64)
@@ -82,12 +81,12 @@ def test_tiny_xlmr_position_offset(ctx, precision):
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_rerank_scores(ctx, precision):
     a, meta = load_golden("tiny_bert")
     d = models.bert_desc(a, meta)
     m = ctx.load(d)
-    s = m.session(8, 32, precision, task=abi.TURBO_TASK_RERANK)
+    s = open_session(m, 8, 32, precision, task=abi.TURBO_TASK_RERANK)
     ids, types, mask, pair, z = rerank_rows()
     cls = s.embed(ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
     sc = oracle.rerank_head(cls, z["pooler_w"], z["pooler_b"], z["cls_w"], z["cls_b"])
@@ -95,17 +94,17 @@ def test_rerank_scores(ctx, precision):
     for i, p in enumerate(pair):
         scores[p] = max(scores[p], sc[i])
     ref = z["scores"].ravel()
-    bound = 1e-4 if precision == EXACT else 1e-2 * np.abs(ref).max()  # cuda_rerank.rs:29, :144
+    bound = 1e-4 if precision_of(precision) == EXACT else 1e-2 * np.abs(ref).max()  # cuda_rerank.rs:29, :144
     assert np.abs(scores - ref).max() < bound
     s.release()
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_rerank_scores_with_the_device_head(ctx, precision):
     a, meta = load_golden("tiny_bert")
     m = ctx.load(models.bert_desc(a, meta))
-    s = m.session(8, 32, precision, task=abi.TURBO_TASK_RERANK)
+    s = open_session(m, 8, 32, precision, task=abi.TURBO_TASK_RERANK)
     ids, types, mask, pair, z = rerank_rows()
     s.set_head(z["cls_w"], z["cls_b"], z["pooler_w"], z["pooler_b"])
     s.write(ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
@@ -117,20 +116,20 @@ def test_rerank_scores_with_the_device_head(ctx, precision):
     for i, p in enumerate(pair):
         scores[p] = max(scores[p], sc[i])
     ref = z["scores"].ravel()
-    bound = 1e-4 if precision == EXACT else 1e-2 * np.abs(ref).max()
+    bound = 1e-4 if precision_of(precision) == EXACT else 1e-2 * np.abs(ref).max()
     assert np.abs(scores - ref).max() < bound
     s.release()
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 @pytest.mark.parametrize("pooling", [abi.TURBO_POOLING_MEAN, abi.TURBO_POOLING_CLS, abi.TURBO_POOLING_LAST])
 def test_poolings_and_cut_vs_oracle(ctx, precision, pooling):
     d = models.synthetic("minilm", 0, layers=2)
     ids, mask, lens = models.rows_bert(5, 6, 16, 128, 128)
     mask[1, 5] = 0  # a hole: a masked key inside the row
     m = ctx.load(d)
-    s = m.session(8, 128, precision)
+    s = open_session(m, 8, 128, precision)
     for od, norm in [(0, abi.TURBO_NORMALIZE_L2), (128, abi.TURBO_NORMALIZE_L2), (384, abi.TURBO_NORMALIZE_NONE)]:
         got = s.embed(ids, mask, pooling=pooling, normalize=norm, output_dim=od)
         want = oracle.encode(d, ids, mask, pooling=pooling, normalize=norm, output_dim=od)
@@ -139,13 +138,13 @@ def test_poolings_and_cut_vs_oracle(ctx, precision, pooling):
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_ranges_vs_oracle_and_whole_row_equals_row_mean(ctx, precision):
     d = models.synthetic("minilm", 0, layers=2)
     ids, mask, lens = models.rows_bert(6, 5, 40, 128, 128)
     ranges = models.ranges_tiling(7, lens, 8, 40)
     m = ctx.load(d)
-    s = m.session(8, 128, precision, max_ranges=len(ranges) + 8)
+    s = open_session(m, 8, 128, precision, max_ranges=len(ranges) + 8)
     s.write_ranges(ids, mask, ranges)
     s.run()
     got = s.read()
@@ -161,12 +160,12 @@ def test_ranges_vs_oracle_and_whole_row_equals_row_mean(ctx, precision):
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_bert_base_shape_vs_oracle(ctx, precision):
     d = models.synthetic("bert-base", 1, layers=2)
     ids, mask, lens = models.rows_bert(11, 6, 64, 512, 512)
     m = ctx.load(d)
-    s = m.session(8, 512, precision)
+    s = open_session(m, 8, 512, precision)
     got = s.embed(ids, mask, pooling=abi.TURBO_POOLING_CLS)
     want = oracle.encode(d, ids, mask, pooling=abi.TURBO_POOLING_CLS)
     check(got, want, precision, "bert-base 2 layers")
@@ -178,8 +177,8 @@ def test_bf16_model_runs_in_bf16(ctx):
     d = models.synthetic("bert-base", 2, dtype=abi.TURBO_DTYPE_BF16, layers=2)
     ids, mask, types, lens = models.rows_rerank(3, 4, seq=512)
     m = ctx.load(d)
-    s = m.session(4, 512, MODEL, task=abi.TURBO_TASK_RERANK)
-    assert s.compute_dtype == abi.TURBO_DTYPE_BF16
+    s = open_session(m, 4, 512, MODEL_BF16, task=abi.TURBO_TASK_RERANK)
+    assert s.compute_dtype == abi.TURBO_DTYPE_BF16 and s.numerics_used == abi.TURBO_NUMERIC_BF16_F32ACC
     got = s.embed(ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
     want = oracle.encode(d, ids, mask, types, pooling=abi.TURBO_POOLING_CLS, normalize=abi.TURBO_NORMALIZE_NONE)
     check(got, want, MODEL, "bf16 rerank body")
@@ -187,7 +186,7 @@ def test_bf16_model_runs_in_bf16(ctx):
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_one_long_row_among_many_short_ones(ctx, precision):
     # Packing stress: a 500-token row with forty rows of 1..11 tokens (the
     # reference's cuda_kernels.rs case), CLS pooling, against the oracle.
@@ -201,7 +200,7 @@ def test_one_long_row_among_many_short_ones(ctx, precision):
         ids[r, 0] = 101
         mask[r, :n] = 1
     m = ctx.load(d)
-    s = m.session(len(lens), 512, precision)
+    s = open_session(m, len(lens), 512, precision)
     got = s.embed(ids, mask, pooling=abi.TURBO_POOLING_CLS)
     want = oracle.encode(d, ids, mask, pooling=abi.TURBO_POOLING_CLS)
     check(got, want, precision, "one long row, many short")
@@ -210,7 +209,7 @@ def test_one_long_row_among_many_short_ones(ctx, precision):
 
 
 @pytest.mark.parametrize("name,vocab", [("bert-base", 30522), ("modernbert-base", 50368)])
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_left_padded_rows_stay_finite_and_match(ctx, name, vocab, precision):
     # Rows whose first tokens are padding (mask 0): masked keys inside the
     # packed row, mean pooling over the live ones (and for BERT CLS, which
@@ -225,7 +224,7 @@ def test_left_padded_rows_stay_finite_and_match(ctx, name, vocab, precision):
         ids[r, p:p + n] = rng.integers(1000, vocab - 1, size=n)
         mask[r, p:p + n] = 1
     m = ctx.load(d)
-    s = m.session(len(lens), 160, precision)
+    s = open_session(m, len(lens), 160, precision)
     poolings = [abi.TURBO_POOLING_MEAN] + ([abi.TURBO_POOLING_CLS] if name == "bert-base" else [])
     for pooling in poolings:
         got = s.embed(ids, mask, pooling=pooling)
@@ -235,14 +234,15 @@ def test_left_padded_rows_stay_finite_and_match(ctx, name, vocab, precision):
     m.release()
 
 
-def test_f32_attention_past_4096_keys(ctx):
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32])
+def test_f32_attention_past_4096_keys(ctx, precision):
     # EXACT attention over a 4,500-token row (ModernBERT's first layer is
     # global): the F32 sums past 4,096 keys (the reference's
     # cuda_rotary.rs:381 case), against the oracle.
     d = models.synthetic("modernbert-base", 7, layers=1)
     ids, mask, lens = models.rows_long(11, 1, 4500, 4500, 4500, 100, 50367)
     m = ctx.load(d)
-    s = m.session(1, 4500, EXACT)
+    s = open_session(m, 1, 4500, precision)
     got = s.embed(ids, mask)
     want = oracle.encode(d, ids, mask)
     check(got, want, EXACT, "modernbert EXACT, 4,500 keys")
@@ -259,7 +259,7 @@ def test_xlmr_large_shape_in_bf16(ctx, lens_range):
     lo, hi = lens_range
     ids, mask, lens = models.rows_long(6, 2, lo, hi, hi, 5, 250001)
     m = ctx.load(d)
-    s = m.session(2, hi, MODEL)
+    s = open_session(m, 2, hi, MODEL_BF16)
     assert s.compute_dtype == abi.TURBO_DTYPE_BF16
     got = s.embed(ids, mask)
     want = oracle.encode(d, ids, mask)
@@ -268,12 +268,12 @@ def test_xlmr_large_shape_in_bf16(ctx, lens_range):
     m.release()
 
 
-@pytest.mark.parametrize("precision", [EXACT, FASTEST])
+@pytest.mark.parametrize("precision", [EXACT, EXACT_TF32, FASTEST])
 def test_modernbert_long_rows_local_and_global_layers(ctx, precision):
     d = models.synthetic("modernbert-base", 3, layers=3)
     ids, mask, lens = models.rows_long(4, 2, 200, 700, 700, 100, 50367)
     m = ctx.load(d)
-    s = m.session(2, 700, precision)
+    s = open_session(m, 2, 700, precision)
     got = s.embed(ids, mask)
     want = oracle.encode(d, ids, mask)
     check(got, want, precision, "modernbert 3 layers")
@@ -288,7 +288,7 @@ def test_modernbert_rows_past_1024_take_the_two_tile_kernel(ctx, precision):
     d = models.synthetic("modernbert-base", 5, layers=3)
     ids, mask, lens = models.rows_long(6, 2, 1100, 1400, 1400, 100, 50367)
     m = ctx.load(d)
-    s = m.session(2, 1400, precision)
+    s = open_session(m, 2, 1400, precision)
     got = s.embed(ids, mask)
     want = oracle.encode(d, ids, mask)
     check(got, want, precision, "modernbert 3 layers, long rows")

@@ -5,13 +5,15 @@ buffers; the kernel's scratch lives in the library's fixed device array.
 
 Checked through the C ABI against the existing entry point
 (turbo_b200_attention_check, which allocates its own buffers) on the same
-data, two calls in a row, within the tests' tolerance for the same kernel
-(the same bits). This file is collected last."""
+data, two calls in a row, within the tests' tolerance for the same kernel,
+and against attention computed in F64 on the host within the kernel tests'
+bound. This file is collected last."""
 import ctypes as C
 
 import numpy as np
 import pytest
 
+from test_gpu_kernels import ref_attention
 from turboembed_b200 import abi, models, runtime
 
 pytestmark = pytest.mark.gpu
@@ -67,6 +69,25 @@ def test_noalloc_attention_matches_the_allocating_entry_point_twice(dtype):
         want = runtime.attention_check(dtype, 2, lens, qkv, live, heads, 64, window)
         scale = max(np.abs(want).max(), 1e-30)
         assert np.abs(got - want).max() / scale < (1.2e-2 if dtype == BF16 else 2e-3)
+        exact = ref_attention(qkv, lens, live, heads, 64, window)
+        scale = max(np.abs(exact).max(), 1e-30)
+        assert np.abs(got - exact).max() / scale < (1.2e-2 if dtype == BF16 else 2e-3)
+
+
+def test_noalloc_attention_refuses_unaligned_buffers_before_any_launch():
+    import torch
+    torch.cuda.init()
+    qkv, live = _case(4, [64], 1, F16)
+    q = torch.from_numpy(qkv).to("cuda:0", torch.float16)
+    ctx = torch.zeros((64 * 64 + 8,), dtype=torch.float16, device="cuda:0")
+    lv = torch.from_numpy(live).to("cuda:0")
+    lens = np.full(1, 64, np.int32)
+    for qp, cp, what in [(q.data_ptr() + 2, ctx.data_ptr(), b"qkv"), (q.data_ptr(), ctx.data_ptr() + 2, b"ctx")]:
+        err = abi.new_error()
+        rc = _entry()(F16, qp, cp, lv.data_ptr(), lens.ctypes.data_as(C.c_void_p), 1, 1, 64, -1, None, None,
+                      C.byref(err))
+        assert rc == abi.TURBO_E_INVALID_ARGUMENT and what in err.message
+    assert not ctx.any().item()  # nothing was launched: ctx is untouched
 
 
 def test_noalloc_attention_refuses_work_beyond_its_scratch():

@@ -52,6 +52,7 @@ TURBO_INPUT_TOKEN_IDS = 1
 TURBO_OUTPUT_HIDDEN_STATES = 1
 TURBO_NUMERIC_F32_FMA, TURBO_NUMERIC_TF32 = 1, 2
 TURBO_NUMERIC_F16_F32ACC, TURBO_NUMERIC_F16_CHUNKACC = 4, 8
+TURBO_NUMERIC_BF16_F32ACC = 16  # appended by the B200 backend (BF16 operands, F32 sums)
 TURBO_AUTOTUNE_OFF = 1
 TURBO_CHOICES_LEN = 1024
 TURBO_ERROR_MESSAGE_LEN = 496

@@ -402,28 +402,100 @@ int32_t tb_buffer_alloc(void *ctx, const turbo_buffer_desc *d, void **out, void 
     return TURBO_OK;
 }
 
+// What the driver knows of an address; memory it does not know (pageable
+// host memory, or no address at all) reads as unregistered, and the error
+// the query may leave behind is cleared.
+cudaPointerAttributes memory_of(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        memset(&a, 0, sizeof a);
+        a.type = cudaMemoryTypeUnregistered;
+        a.device = -1;
+    }
+    return a;
+}
+
+const char *memory_name(cudaMemoryType t) {
+    switch (t) {
+    case cudaMemoryTypeHost: return "page-locked host memory";
+    case cudaMemoryTypeDevice: return "device memory";
+    case cudaMemoryTypeManaged: return "managed memory";
+    default: return "memory the driver does not know (pageable host memory)";
+    }
+}
+
+const char *placement_text(uint32_t pl) {
+    switch (pl) {
+    case TURBO_PLACE_HOST: return "HOST";
+    case TURBO_PLACE_PINNED: return "PINNED";
+    case TURBO_PLACE_DEVICE: return "DEVICE";
+    case TURBO_PLACE_SHARED: return "SHARED";
+    default: return "an unknown placement";
+    }
+}
+
+// Wrap the caller's memory without copying or owning it. The rules are the
+// reference backend's (core/cuda/backend.cpp:630-692): a CUDA_PTR is memory
+// of this context's device imported as DEVICE (device or managed memory) or
+// SHARED (managed memory); a HOST_PTR is host memory, never DEVICE, and
+// page-locked when PINNED, managed when SHARED. Every refusal is made here,
+// on the host, so no kernel is ever handed an address of the wrong kind.
 int32_t tb_buffer_import(void *ctx, const turbo_buffer_desc *d, const turbo_native_handle *h, void **out, void **host,
                          turbo_error *err) {
     auto *c = (Context *)ctx;
+    if (!c || !d || !h || !out) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "context, desc, handle and out are required");
+    if (h->kind != TURBO_HANDLE_CUDA_PTR && h->kind != TURBO_HANDLE_HOST_PTR)
+        return fail(err, TURBO_E_UNSUPPORTED, 0,
+                    "handle kind %u: the B200 backend imports TURBO_HANDLE_CUDA_PTR and TURBO_HANDLE_HOST_PTR", h->kind);
+    if (h->handle == 0) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle: a NULL pointer");
+    const uint64_t at = h->handle + h->offset;
+    if (at < h->handle || at + d->bytes < at || at + d->bytes > (uint64_t)UINTPTR_MAX)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle %#llx + offset %llu + %llu bytes runs past the address space",
+                    (unsigned long long)h->handle, (unsigned long long)h->offset, (unsigned long long)d->bytes);
+    const uint32_t pl = d->placement;
+    if (pl != TURBO_PLACE_HOST && pl != TURBO_PLACE_PINNED && pl != TURBO_PLACE_DEVICE && pl != TURBO_PLACE_SHARED)
+        return fail(err, TURBO_E_INVALID_ENUM, 0, "placement %u", pl);
+    void *p = (void *)(uintptr_t)at;
     DeviceScope ds(c->device);
-    void *p = (void *)(uintptr_t)(h->handle + h->offset);
+    const cudaPointerAttributes a = memory_of(p);
     if (h->kind == TURBO_HANDLE_CUDA_PTR) {
         if (h->aux != (uint64_t)c->device)
-            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "a CUDA pointer of device %llu on a context of device %d",
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "aux: a CUDA pointer of device %llu, and this context is on device %d",
                         (unsigned long long)h->aux, c->device);
-        cudaPointerAttributes a;
-        if (cudaPointerGetAttributes(&a, p) != cudaSuccess || (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged))
-            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle is not CUDA device memory");
-    } else if (h->kind != TURBO_HANDLE_HOST_PTR) {
-        return fail(err, TURBO_E_UNSUPPORTED, 0, "handle kind %u is not taken by the cuda backend", h->kind);
+        if (pl != TURBO_PLACE_DEVICE && pl != TURBO_PLACE_SHARED)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0,
+                        "placement: %s: a TURBO_HANDLE_CUDA_PTR is imported as DEVICE or SHARED memory", placement_text(pl));
+        const bool fits = pl == TURBO_PLACE_SHARED ? a.type == cudaMemoryTypeManaged
+                                                   : a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+        if (!fits)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle: the pointer is %s, not %s memory", memory_name(a.type),
+                        placement_text(pl));
+        if (a.type == cudaMemoryTypeDevice && a.device != c->device)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle: memory of device %d, and this context is on device %d",
+                        a.device, c->device);
+    } else {
+        if (pl == TURBO_PLACE_DEVICE)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0,
+                        "placement: DEVICE: a TURBO_HANDLE_HOST_PTR is host memory; import device memory as "
+                        "TURBO_HANDLE_CUDA_PTR");
+        if (a.type == cudaMemoryTypeDevice)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle: the pointer is device memory, not host memory");
+        if (pl == TURBO_PLACE_PINNED && a.type != cudaMemoryTypeHost)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0,
+                        "placement: PINNED: the pointer is %s, not page-locked (cudaHostRegister it, or import it as HOST)",
+                        memory_name(a.type));
+        if (pl == TURBO_PLACE_SHARED && a.type != cudaMemoryTypeManaged)
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "placement: SHARED: the pointer is %s, not managed memory",
+                        memory_name(a.type));
     }
     auto *b = new (std::nothrow) Buffer;
     if (!b) return fail(err, TURBO_E_OUT_OF_MEMORY, 0, "buffer");
     b->ctx = c;
-    b->placement = d->placement;
+    b->placement = pl;
     b->bytes = d->bytes;
     b->ptr = p;
-    b->host = h->kind == TURBO_HANDLE_HOST_PTR ? p : (d->placement == TURBO_PLACE_SHARED ? p : nullptr);
+    b->host = h->kind == TURBO_HANDLE_HOST_PTR || pl == TURBO_PLACE_SHARED ? p : nullptr;
     b->owned = false;
     *out = b;
     if (host) *host = b->host;
@@ -759,6 +831,55 @@ Dt resolve_dt(const Model *m, uint32_t precision) {
     return m->dtype == TURBO_DTYPE_F32 ? Dt::F32 : m->dtype == TURBO_DTYPE_F16 ? Dt::F16 : Dt::BF16;
 }
 
+// The numeric classes (TURBO_NUMERIC_*) a precision allows when the core
+// hands none, a session made through session_create: the core's own table
+// (core/src/tuning.rs:23-36, restated by the reference backend at
+// core/cuda/backend.cpp:1666-1669). Only F32 FMAs at EXACT and MODEL; F16
+// operands at FASTEST.
+uint32_t default_numerics(uint32_t precision) {
+    return precision == TURBO_PRECISION_FASTEST ? TURBO_NUMERIC_F16_F32ACC | TURBO_NUMERIC_F16_CHUNKACC
+                                                : TURBO_NUMERIC_F32_FMA;
+}
+
+// The class a 16-bit session's kernels compute in: every tensor-core GEMM
+// and attention kernel here takes F16 or BF16 operands and sums in F32.
+uint32_t numeric_of(Dt dt) {
+    return dt == Dt::F16 ? TURBO_NUMERIC_F16_F32ACC : dt == Dt::BF16 ? TURBO_NUMERIC_BF16_F32ACC : TURBO_NUMERIC_F32_FMA;
+}
+
+// The compute dtype a session runs in, given what the precision asks for
+// and the classes it is allowed. A 16-bit dtype whose class is not allowed
+// falls back: a BF16 model at FASTEST to F16 when F16 operands are allowed
+// (the reference's FASTEST narrows every model to F16,
+// core/cuda/backend.cpp:2920-2924), otherwise to F32, whose FFMA kernels
+// every precision may run (the reference adds TURBO_NUMERIC_F32_FMA to any
+// session it does not compute in F16, core/cuda/backend.cpp:2996-2998).
+Dt allowed_dt(const Model *m, uint32_t precision, uint32_t allowed) {
+    Dt dt = resolve_dt(m, precision);
+    if (dt == Dt::F32 || (allowed & numeric_of(dt))) return dt;
+    if (dt == Dt::BF16 && precision == TURBO_PRECISION_FASTEST && (allowed & TURBO_NUMERIC_F16_F32ACC)) return Dt::F16;
+    return Dt::F32;
+}
+
+// The classes the session's GEMM and attention kernels compute in, as the
+// core records them (turbo_backend_tuning.numerics_used): a 16-bit
+// session's one class; an F32 session's TF32 when its tf32 GEMMs run, plus
+// F32 FMAs when any of its products or its attention take an FFMA kernel.
+uint32_t numerics_run(const Session *s) {
+    if (s->dt != Dt::F32) return numeric_of(s->dt);
+    if (!s->exact_tf32) return TURBO_NUMERIC_F32_FMA;
+    const Model *m = s->m;
+    const int h = m->hidden, I = m->inter;
+    const int shapes[4][2] = {{3 * h, h}, {h, h}, {m->modern ? 2 * I : I, h}, {h, I}};
+    bool ffma = !s->tf32_attn;
+    for (const auto &nk : shapes) {
+        Epilogue probe;
+        probe.kind = EPI_STORE;
+        ffma |= !gemm_tf32_takes(nk[0], nk[1], probe);
+    }
+    return TURBO_NUMERIC_TF32 | (ffma ? TURBO_NUMERIC_F32_FMA : 0u);
+}
+
 int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_seq, uint32_t precision,
                      uint32_t max_ranges, turbo_backend_tuning *tuning, uint32_t *compute_dtype, void **out,
                      turbo_error *err) {
@@ -772,7 +893,10 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         return fail(err, TURBO_E_CAPACITY, 2, "max_seq %u past the rope table's %d positions", max_seq, m->positions);
     Context *c = m->ctx;
     DeviceScope ds(c->device);
-    const Dt dt = resolve_dt(m, precision);
+    // What the core allows this precision (turbo_backend.h: a kernel outside
+    // the set is never launched), and the dtype that follows from it.
+    const uint32_t allowed = tuning ? tuning->numerics_allowed : default_numerics(precision);
+    const Dt dt = allowed_dt(m, precision, allowed);
     if (dt != Dt::F32) {
         cudaError_t e = narrowed(m, dt);
         if (e != cudaSuccess) return cuda_fail(err, e, "narrowing the weights");
@@ -799,12 +923,14 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
                          gemm_ln_dual_takes(m->hidden, m->inter);
     }
     if (dt == Dt::F32) {
-        // The EXACT tier's GEMMs on tcgen05 kind::tf32 with the three-product
-        // split, unless the environment sets TB_EXACT_TF32=0 (then the FFMA
-        // kernel, one F32 chain over k per output); its attention on the
-        // same, unless TB_EXACT_TF32_ATTN=0 (then the FFMA attention).
+        // F32 sessions' GEMMs on tcgen05 kind::tf32 with the three-product
+        // split when TURBO_NUMERIC_TF32 is allowed, unless the environment
+        // sets TB_EXACT_TF32=0; otherwise the FFMA kernel, one F32 chain over
+        // k per output (TURBO_NUMERIC_F32_FMA, the core's table). Attention
+        // on the same tf32 split where it is built, unless
+        // TB_EXACT_TF32_ATTN=0 (then the FFMA attention).
         const char *v = getenv("TB_EXACT_TF32");
-        s->exact_tf32 = !(v && v[0] == '0');
+        s->exact_tf32 = (allowed & TURBO_NUMERIC_TF32) && !(v && v[0] == '0');
         const char *va = getenv("TB_EXACT_TF32_ATTN");
         Epilogue store;
         s->tf32_attn = s->exact_tf32 && !(va && va[0] == '0') && !m->modern && m->hidden / m->heads == 64 &&
@@ -883,7 +1009,7 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
                  : s->tf32_attn   ? "gemm=tf32x3 attention=tf32x3"
                                   : "gemm=tf32x3 attention=f32");
         if (tuning->struct_size >= offsetof(turbo_backend_tuning, numerics_used) + 4)
-            tuning->numerics_used = tuning->numerics_allowed;
+            tuning->numerics_used = numerics_run(s.get());
     }
     *compute_dtype = dtype_of(dt);
     *out = s.release();
@@ -1081,6 +1207,8 @@ int32_t write_rows_device(Session *s, const turbo_backend_embed_rows *r, turbo_e
     dr.ids = r->ids, dr.mask = r->mask, dr.types = r->types;
     dr.batch = (int)r->batch, dr.seq = (int)r->seq, dr.stride = (int)stride;
     dr.pool_mode = r->pooling == TURBO_POOLING_CLS ? 1 : (r->pooling == TURBO_POOLING_LAST ? 2 : 0);
+    dr.vocab = s->m->vocab;
+    dr.types_count = s->m->type ? std::max(s->m->types, 1) : 0;
     DevicePlan dp;
     dp.qt = attention_queries(s), dp.q2 = ATTN_TC2_QUERIES, dp.allow_pairs = s->max_attn2_items > 0;
     const size_t B = (size_t)s->max_batch;
@@ -1092,11 +1220,15 @@ int32_t write_rows_device(Session *s, const turbo_backend_embed_rows *r, turbo_e
     dp.attn = (AttnItem *)(D + s->lay.attn), dp.attn2 = (AttnItem *)(D + s->lay.attn2);
     dp.pool = (PoolItem *)(D + s->lay.pool);
     CK(pack_rows_device(dr, dp, c->stream), "embed_write_device");
-    CK(cudaMemcpyAsync(s->pack_counts, dp.counts, 5 * sizeof(int32_t), cudaMemcpyDeviceToHost, c->stream),
+    CK(cudaMemcpyAsync(s->pack_counts, dp.counts, 6 * sizeof(int32_t), cudaMemcpyDeviceToHost, c->stream),
        "embed_write_device");
     CK(cudaStreamSynchronize(c->stream), "embed_write_device");
     const int32_t *k = s->pack_counts;
     if (k[4]) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "mask row %d has no 1: a row needs a token", k[4] - 1);
+    if (k[5] != INT32_MAX)
+        return fail(err, TURBO_E_INVALID_ARGUMENT, 0,
+                    "row %d holds a token id outside the vocabulary of %d or a token type outside the model's %d",
+                    k[5], s->m->vocab, dr.types_count);
     const uint32_t L = (uint32_t)s->m->layers;
     s->h2d_bytes = 0;
     s->tokens = k[0];

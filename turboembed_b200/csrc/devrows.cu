@@ -17,7 +17,8 @@ namespace {
 // One block: per-row lengths and holes (a warp a row), starts in row order,
 // each row's rank in the longest-first order, attention item offsets in that
 // order. counts = {tokens, attention items, two-tile items, longest row,
-// first empty row + 1 (0: none)}.
+// first empty row + 1 (0: none), first row with an id or type out of range
+// (INT32_MAX: none; fill_kernel lowers it)}.
 __global__ void __launch_bounds__(1024) rows_kernel(const int32_t *__restrict__ mask, int stride, int seq, int batch,
                                                     int qt, int q2, int allow_pairs, int32_t *__restrict__ len,
                                                     int32_t *__restrict__ start, int32_t *__restrict__ holes,
@@ -67,27 +68,40 @@ __global__ void __launch_bounds__(1024) rows_kernel(const int32_t *__restrict__ 
             if (pairs) na2 += (len[b] + q2 - 1) / q2;
         }
         counts[0] = t, counts[1] = na, counts[2] = na2, counts[3] = longest, counts[4] = empty;
+        counts[5] = INT32_MAX;
     }
 }
 
-// A block a row: its tokens, its attention items and its vector.
+// A block a row: its tokens, its attention items and its vector. Host rows
+// reach the backend already checked by the core (an id inside the
+// vocabulary, core/src/session/tokens.rs:343), device rows do not: an id
+// outside [0, vocab) or a type outside [0, types) (types = 0: the model has
+// no type table and reads none) is packed as 0, so the gather stays inside
+// its tables, and the row is reported in counts[5] for the host to refuse.
 __global__ void __launch_bounds__(256) fill_kernel(const int32_t *__restrict__ ids, const int32_t *__restrict__ mask,
-                                                   const int32_t *__restrict__ types, int stride, int qt, int q2,
+                                                   const int32_t *__restrict__ types, int stride, int vocab,
+                                                   int n_types, int qt, int q2,
                                                    int pool_mode, const int32_t *__restrict__ len,
                                                    const int32_t *__restrict__ start, const int32_t *__restrict__ holes,
                                                    const int32_t *__restrict__ item0, const int32_t *__restrict__ item2,
                                                    int32_t *__restrict__ tok_id, int32_t *__restrict__ tok_type,
                                                    int32_t *__restrict__ tok_pos, uint8_t *__restrict__ tok_live,
                                                    AttnItem *__restrict__ attn, AttnItem *__restrict__ attn2,
-                                                   PoolItem *__restrict__ pool) {
+                                                   PoolItem *__restrict__ pool, int32_t *__restrict__ counts) {
     const int b = blockIdx.x, n = len[b], st = start[b];
     const size_t row = (size_t)b * stride;
+    bool bad = false;
     for (int p = threadIdx.x; p < n; p += blockDim.x) {
-        tok_id[st + p] = ids[row + p];
-        tok_type[st + p] = types ? types[row + p] : 0;
+        int32_t id = ids[row + p], ty = types ? types[row + p] : 0;
+        if (id < 0 || id >= vocab) bad = true, id = 0;
+        if (n_types > 0 && (ty < 0 || ty >= n_types)) bad = true, ty = 0;
+        if (n_types == 0) ty = 0;
+        tok_id[st + p] = id;
+        tok_type[st + p] = ty;
         tok_pos[st + p] = p;
         tok_live[st + p] = mask[row + p] != 0;
     }
+    if (bad) atomicMin(&counts[5], b);
     const int hole = holes[b];
     for (int q = threadIdx.x; q * qt < n; q += blockDim.x) attn[item0[b] + q] = AttnItem{st, n, q * qt, hole};
     if (item2[b] >= 0)
@@ -110,9 +124,9 @@ cudaError_t pack_rows_device(const DeviceRows &r, const DevicePlan &p, cudaStrea
                                    p.holes, p.item0, p.item2, p.order, p.counts);
     cudaError_t e = counted(cudaGetLastError());
     if (e != cudaSuccess) return e;
-    fill_kernel<<<r.batch, 256, 0, s>>>(r.ids, r.mask, r.types, r.stride, p.qt, p.q2, r.pool_mode, p.len, p.start,
-                                        p.holes, p.item0, p.item2, p.tok_id, p.tok_type, p.tok_pos, p.tok_live,
-                                        p.attn, p.attn2, p.pool);
+    fill_kernel<<<r.batch, 256, 0, s>>>(r.ids, r.mask, r.types, r.stride, r.vocab, r.types_count, p.qt, p.q2,
+                                        r.pool_mode, p.len, p.start, p.holes, p.item0, p.item2, p.tok_id, p.tok_type,
+                                        p.tok_pos, p.tok_live, p.attn, p.attn2, p.pool, p.counts);
     return counted(cudaGetLastError());
 }
 

@@ -81,10 +81,12 @@ struct AttnItem {
 struct DeviceRows {
     const int32_t *ids = nullptr, *mask = nullptr, *types = nullptr;
     int batch = 0, seq = 0, stride = 0, pool_mode = 0;
+    int vocab = 0, types_count = 0;  // ids must lie in [0, vocab), types in [0, types_count) (0: not read)
 };
 // The session's plan arrays (device) and the packing scratch: len, start,
-// holes, item0, item2, order [max_batch] each, counts [5] = tokens,
-// attention items, two-tile items, longest row, first empty row + 1.
+// holes, item0, item2, order [max_batch] each, counts [6] = tokens,
+// attention items, two-tile items, longest row, first empty row + 1, first
+// row holding an id or type out of range (INT32_MAX: none).
 struct DevicePlan {
     int qt = 0, q2 = 0, allow_pairs = 0;
     int32_t *len = nullptr, *start = nullptr, *holes = nullptr, *item0 = nullptr, *item2 = nullptr,

@@ -74,7 +74,11 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_noalloc(uint32_t dtype, const 
     if (head_dim != 64) return fail(err, TURBO_E_UNSUPPORTED, "the tensor-core attention takes head width 64");
     if (!qkv || !ctx || !live || !lens || batch == 0 || heads == 0)
         return fail(err, TURBO_E_INVALID_ARGUMENT, "qkv, ctx, live and lens are required, batch and heads above 0");
+    // The kernel reads qkv through TMA (16-byte aligned bases) and writes
+    // ctx with 16-byte stores: a pointer off that boundary is refused here,
+    // before any launch, rather than faulting on the GPU.
     if (((uintptr_t)qkv & 15) != 0) return fail(err, TURBO_E_INVALID_ARGUMENT, "qkv must be 16-byte aligned");
+    if (((uintptr_t)ctx & 15) != 0) return fail(err, TURBO_E_INVALID_ARGUMENT, "ctx must be 16-byte aligned");
     // Count the work before touching the device: beyond the array's room is refused.
     uint64_t tokens = 0, units = 0;
     int32_t max_len = 0;

@@ -103,6 +103,19 @@ class Context:
     def buffer(self, placement, nbytes):
         return Buffer(self, placement, nbytes)
 
+    def import_buffer(self, placement, nbytes, kind, address, aux=0, offset=0):
+        """buffer_import: wrap memory the caller owns (a CUDA_PTR of device
+        `aux`, or a HOST_PTR) as a buffer of `placement`; nothing is copied."""
+        d = abi.turbo_buffer_desc(C.sizeof(abi.turbo_buffer_desc), placement, abi.TURBO_DTYPE_U8, 1,
+                                  (abi.u64 * 2)(nbytes, 0), nbytes)
+        h = abi.turbo_native_handle(C.sizeof(abi.turbo_native_handle), kind, address, aux, offset)
+        out, host, err = C.c_void_p(), C.c_void_p(), abi.new_error()
+        _check(self.t.buffer_import(self.h, C.byref(d), C.byref(h), C.byref(out), C.byref(host), C.byref(err)), err,
+               "buffer_import")
+        b = Buffer(self, placement, nbytes, handle=out)
+        b.host = host
+        return b
+
     def release(self):
         if self.h:
             self.t.context_release(self.h)
@@ -158,8 +171,11 @@ class Model:
         err = abi.new_error()
         _check(self.t.model_load(ctx.h, C.byref(desc.struct), C.byref(self.h), C.byref(err)), err, "model_load")
 
-    def session(self, max_batch, max_seq, precision, task=abi.TURBO_TASK_EMBED, max_ranges=0, cpu_threads=0):
-        return Session(self, max_batch, max_seq, precision, task, max_ranges, cpu_threads)
+    def session(self, max_batch, max_seq, precision, task=abi.TURBO_TASK_EMBED, max_ranges=0, cpu_threads=0,
+                numerics=None):
+        """session_open with turbo_backend_tuning.numerics_allowed = `numerics`,
+        or the core's own table for the precision when None."""
+        return Session(self, max_batch, max_seq, precision, task, max_ranges, cpu_threads, numerics)
 
     def release(self):
         if self.h:
@@ -167,23 +183,35 @@ class Model:
             self.h = C.c_void_p()
 
 
+# The numeric classes the core allows each precision (core/src/tuning.rs:23-36):
+# what the core hands session_open in turbo_backend_tuning.numerics_allowed.
+CORE_NUMERICS = {
+    abi.TURBO_PRECISION_EXACT: abi.TURBO_NUMERIC_F32_FMA,
+    abi.TURBO_PRECISION_MODEL: abi.TURBO_NUMERIC_F32_FMA,
+    abi.TURBO_PRECISION_FASTEST: abi.TURBO_NUMERIC_F16_F32ACC | abi.TURBO_NUMERIC_F16_CHUNKACC,
+}
+
+
 class Session:
     """session_open, then embed_write / embed_write_ranges + session_run,
-    reading the vectors back with buffer_read."""
+    reading the vectors back with buffer_read. `numerics_used` is what the
+    backend reports its kernels compute in."""
 
-    def __init__(self, model, max_batch, max_seq, precision, task, max_ranges, cpu_threads):
+    def __init__(self, model, max_batch, max_seq, precision, task, max_ranges, cpu_threads, numerics=None):
         self.model, self.t = model, model.t
         d = abi.turbo_backend_session_desc(C.sizeof(abi.turbo_backend_session_desc), task, max_batch, max_seq,
                                            precision, cpu_threads, max_ranges, 0)
         self.tuning = abi.turbo_backend_tuning()
         self.tuning.struct_size = C.sizeof(self.tuning)
         self.tuning.mode = abi.TURBO_AUTOTUNE_OFF
-        self.tuning.numerics_allowed = 0xF
+        self.tuning.numerics_allowed = CORE_NUMERICS[precision] if numerics is None else numerics
         cd, err = C.c_uint32(), abi.new_error()
         self.h = C.c_void_p()
         _check(self.t.session_open(model.h, C.byref(d), C.byref(self.tuning), C.byref(cd), C.byref(self.h),
                                    C.byref(err)), err, "session_open")
         self.compute_dtype = cd.value
+        self.numerics_used = self.tuning.numerics_used
+        self.choices = self.tuning.choices.decode(errors="replace")
         self.hidden = model.desc.hidden
         self._out_dim, self._count = 0, 0
 

@@ -1,6 +1,7 @@
 """Data parallelism by sequence: rows shard across the ranks of one box, each
-rank running its own packed sub-batch on its own GPU; the
-pooled vectors can be gathered into one buffer with one all-gather.
+rank running its own packed sub-batch on its own GPU, as the reference's
+sessions each run their own rows (core/src/session/mod.rs); the pooled
+vectors can be gathered into one buffer with one all-gather.
 
 No row depends on another anywhere in the encoder, pooling or rerank head,
 so sharding needs no collective on the data path.
