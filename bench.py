@@ -1,7 +1,7 @@
 """Benchmark of the B200 backend on BASELINE.json's workloads.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--config c1|c2|c2x|c3|c4|c5]
+                    [--config c1|c2|c2d|c2x|c3|c4|c5]
 
 The default (c2) is the headline metric's config:
 a BERT-base encoder (12 layers, hidden 768, 12 heads, FFN 3072 GELU,
@@ -21,6 +21,12 @@ the encoder (and, for c3, the rerank head) over one batch.
   e2e_device_rows  the same with the rows already in device memory
          (turbo_b200_embed_write_device: packing on the device, no H2D);
          row writes only (null for range writes and the device head).
+  parity the benchmarked session's vectors on the CPU baseline's sample rows
+         against the oracle's (cosine min, max-abs), rank 0 at N = 1.
+Sessions are opened with the numeric classes the workload names
+(turbo_backend_tuning.numerics_allowed): the core's own table unless the
+config needs a class the table does not hold (TF32 for c2x's 3xTF32
+kernels, BF16 operands for the BF16 configs); the line reports both.
 Under torchrun (N > 1) one seeded global batch of N times the per-GPU rows is
 sharded by cost (longest-processing-time, turboembed_b200/shard.py) and each
 rank runs its rows on its own GPU (weak scaling: no collective on the data
@@ -66,8 +72,10 @@ class Workload:
     a function of a seed)."""
 
     def __init__(self, key, text, model, seed, wdtype, precision, dtype, per_gpu, seq, rows, pooling, normalize,
-                 task=abi.TURBO_TASK_EMBED, ranges=None, head=False, cpu_rows=None, ref_rows=None):
+                 task=abi.TURBO_TASK_EMBED, ranges=None, head=False, cpu_rows=None, ref_rows=None, numerics=None):
         self.key, self.text, self.model, self.seed, self.wdtype = key, text, model, seed, wdtype
+        # turbo_backend_tuning.numerics_allowed: the core's table when None.
+        self.numerics = runtime.CORE_NUMERICS[precision] if numerics is None else numerics
         self.precision, self.dtype, self.per_gpu, self.seq, self.rows = precision, dtype, per_gpu, seq, rows
         self.pooling, self.normalize, self.task, self.ranges, self.head = pooling, normalize, task, ranges, head
         self.cpu_rows, self.ref_rows = cpu_rows, ref_rows
@@ -106,33 +114,49 @@ class Workload:
         return 4.0 * 4 * self.hidden / (2 * per_tok)
 
 
+F32_TF32 = abi.TURBO_NUMERIC_F32_FMA | abi.TURBO_NUMERIC_TF32
+F32_BF16 = abi.TURBO_NUMERIC_F32_FMA | abi.TURBO_NUMERIC_BF16_F32ACC
+NUMERIC_NAMES = {abi.TURBO_NUMERIC_F32_FMA: "F32_FMA", abi.TURBO_NUMERIC_TF32: "TF32",
+                 abi.TURBO_NUMERIC_F16_F32ACC: "F16_F32ACC", abi.TURBO_NUMERIC_F16_CHUNKACC: "F16_CHUNKACC",
+                 abi.TURBO_NUMERIC_BF16_F32ACC: "BF16_F32ACC"}
+
+
+def numeric_names(bits):
+    return "|".join(n for b, n in NUMERIC_NAMES.items() if bits & b) or "none"
+
+
 WORKLOADS = {
     "c1": Workload("c1", "all-MiniLM-L6-v2 shape (BASELINE config 1): 6L h384 12 heads FFN1536, batch 32/GPU, "
                          "L~U[16,128], mean + L2, EXACT (F32)", "minilm", 0, abi.TURBO_DTYPE_F32,
                    abi.TURBO_PRECISION_EXACT, "f32", 32, 128,
                    lambda seed, n: _no_types(models.rows_bert(seed, n, 16, 128, 128)), abi.TURBO_POOLING_MEAN,
-                   abi.TURBO_NORMALIZE_L2, cpu_rows=512, ref_rows=16),
+                   abi.TURBO_NORMALIZE_L2, cpu_rows=512, ref_rows=128),
     "c2": Workload("c2", "BERT-base (BASELINE config 2): 12L h768 12 heads FFN3072 GELU, batch 256/GPU, "
                          "L~U[64,512], CLS + L2, FASTEST (F16 operands, F32 sums), varlen-packed", "bert-base", 1,
                    abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 256, 512,
                    lambda seed, n: _no_types(models.rows_bert(seed, n, 64, 512, 512)), abi.TURBO_POOLING_CLS,
-                   abi.TURBO_NORMALIZE_L2, cpu_rows=36, ref_rows=2),
+                   abi.TURBO_NORMALIZE_L2, cpu_rows=36, ref_rows=12),
+    "c2d": Workload("c2d", "BERT-base dense (the metric's seq 512): 12L h768 12 heads FFN3072 GELU, batch 256/GPU, "
+                           "every row 512 tokens (131,072 tokens a step), CLS + L2, FASTEST (F16 operands, F32 sums)",
+                    "bert-base", 1, abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 256, 512,
+                    lambda seed, n: _no_types(models.rows_bert(seed, n, 512, 512, 512)), abi.TURBO_POOLING_CLS,
+                    abi.TURBO_NORMALIZE_L2, cpu_rows=12, ref_rows=6),
     "c2x": Workload("c2x", "BERT-base (BASELINE config 2) at EXACT (F32): 12L h768, batch 256/GPU, L~U[64,512], "
                            "CLS + L2, varlen-packed", "bert-base", 1, abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_EXACT,
                     "f32", 256, 512, lambda seed, n: _no_types(models.rows_bert(seed, n, 64, 512, 512)),
-                    abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_L2, cpu_rows=36, ref_rows=2),
+                    abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_L2, cpu_rows=36, ref_rows=12, numerics=F32_TF32),
     "c3": Workload("c3", "cross-encoder rerank (BASELINE config 3): BERT-base body + 768->1 head on CLS, "
                          "1 query x 1024 passages/GPU, [101] q [102] p [102], BF16 (MODEL)", "bert-base", 2,
                    abi.TURBO_DTYPE_BF16, abi.TURBO_PRECISION_MODEL, "bf16", 1024, 512,
                    lambda seed, n: models.rows_rerank(seed, n), abi.TURBO_POOLING_CLS, abi.TURBO_NORMALIZE_NONE,
-                   task=abi.TURBO_TASK_RERANK, head=True, cpu_rows=36, ref_rows=2),
+                   task=abi.TURBO_TASK_RERANK, head=True, cpu_rows=36, ref_rows=12, numerics=F32_BF16),
     "c4": Workload("c4", "ModernBERT-base (BASELINE config 4): 22L h768 GeGLU 1152, global every 3rd layer, "
                          "local window 128, batch 8/GPU, L~U[1024,8192] unpadded, mean + L2, FASTEST (F16)",
                    "modernbert-base", 3, abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 8, 8192,
                    lambda seed, n: _no_types(models.rows_long(seed, n, 1024, 8192, 8192, 100, 50367)),
                    abi.TURBO_POOLING_MEAN, abi.TURBO_NORMALIZE_L2,
                    cpu_rows=lambda seed: _no_types(models.rows_long(seed, 4, 1024, 1024, 1024, 100, 50367)),
-                   ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 256, 256, 256, 100, 50367))),
+                   ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 1024, 1024, 1024, 100, 50367))),
     "c5": Workload("c5", "XLM-R-large / bge-m3 shape (BASELINE config 5): 24L h1024 16 heads FFN4096, 16 documents"
                          "/GPU (128 over 8 GPUs) of 8192 tokens, range pooling U[32,256] + L2, BF16 (MODEL)",
                    "xlmr-large", 4, abi.TURBO_DTYPE_BF16, abi.TURBO_PRECISION_MODEL, "bf16", 16, 8192,
@@ -140,7 +164,8 @@ WORKLOADS = {
                    abi.TURBO_POOLING_MEAN, abi.TURBO_NORMALIZE_L2,
                    ranges=lambda seed, lens: models.ranges_tiling(seed, lens, 32, 256),
                    cpu_rows=lambda seed: _no_types(models.rows_long(seed, 2, 1024, 1024, 1024, 5, 250001)),
-                   ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 128, 128, 128, 5, 250001))),
+                   ref_rows=lambda seed: _no_types(models.rows_long(seed, 1, 512, 512, 512, 5, 250001)),
+                   numerics=F32_BF16),
 }
 
 
@@ -218,32 +243,101 @@ def sample_rows(wl, spec, seed):
     return spec(seed) if callable(spec) else wl.rows(seed, spec)
 
 
+def sample_ranges(wl, lens):
+    return wl.ranges(99, lens) if wl.ranges else None
+
+
 def oracle_pass(wl, desc, rows, cores):
     """One pass of the CPU oracle (a restatement of the reference CPU encoder)
-    over rows, with the workload's pooling (and ranges, and head)."""
+    over rows, with the workload's pooling (and ranges): the vectors, and
+    for the rerank config the head's scores (else None)."""
     from oracle import oracle
     ids, mask, types, lens = rows
-    rg = wl.ranges(99, lens) if wl.ranges else None
-    out = oracle.encode(desc, ids, mask, types, pooling=wl.pooling, normalize=wl.normalize, ranges=rg,
-                        threads=cores)
+    out = oracle.encode(desc, ids, mask, types, pooling=wl.pooling, normalize=wl.normalize,
+                        ranges=sample_ranges(wl, lens), threads=cores)
+    scores = None
     if wl.head:
         w, b = head_weights(wl)
-        out = oracle.rerank_head(out, None, None, w, b)
-    return out
+        scores = oracle.rerank_head(out, None, None, w, b)
+    return out, scores
+
+
+def cpu_model():
+    """The host CPU's model name (/proc/cpuinfo), as lscpu reports it."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def timed_oracle(wl, desc, rows, cores):
+    """The oracle over rows, timed after an untimed pass over the sample's
+    first row that prepares the weights (kept for the timed pass): the time
+    of the encoder, not of the one-time weight transposition."""
+    from oracle import oracle
+    oracle.keep_weights(True)
+    try:
+        ids, mask, types, lens = rows
+        first = (ids[:1], mask[:1], None if types is None else types[:1], lens[:1])
+        oracle_pass(wl, desc, first, cores)
+        t0 = time.perf_counter()
+        out = oracle_pass(wl, desc, rows, cores)
+        dt = time.perf_counter() - t0
+    finally:
+        oracle.keep_weights(False)
+    return out, dt
 
 
 def cpu_baseline(wl, desc):
     """The CPU oracle on a bounded sample of the same workload, all host
-    threads."""
+    threads; returns the JSON object and the oracle's output on the sample
+    (the parity check's reference)."""
     cores = os.cpu_count() or 1
     rows = sample_rows(wl, wl.cpu_rows, 4242)
     lens = rows[3]
-    t0 = time.perf_counter()
-    oracle_pass(wl, desc, rows, cores)
-    dt = time.perf_counter() - t0
+    out, dt = timed_oracle(wl, desc, rows, cores)
     return {"value": float(np.sum(lens) / dt), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "cpu": cpu_model(),
             "sample": f"{len(lens)} rows of the {wl.key} distribution ({int(np.sum(lens))} live tokens), F32, "
-                      f"all {wl.layers} layers, {dt:.1f} s"}
+                      f"all {wl.layers} layers, weights prepared before the timed pass, {dt:.1f} s"}, rows, out
+
+
+def parity(wl, sess, rows, want):
+    """The benchmarked session's vectors on the CPU sample's rows against
+    the oracle's: cosine min and max-abs (and for the rerank config the
+    scores' max-abs), written max_batch rows at a time."""
+    vecs, scores = want
+    ids, mask, types, lens = rows
+    rg = sample_ranges(wl, lens)
+    got, got_scores = [], []
+    if rg is not None:
+        sess.write_ranges(ids, mask, rg, types=types, normalize=wl.normalize)
+        sess.run()
+        got.append(sess.read().copy())
+    else:
+        step = sess.max_batch
+        for i in range(0, len(lens), step):
+            sl = slice(i, i + step)
+            sess.write(ids[sl], mask[sl], None if types is None else types[sl], pooling=wl.pooling,
+                       normalize=wl.normalize)
+            sess.run()
+            if wl.head:
+                got_scores.append(sess.head_scores().copy())
+            got.append(sess.read().copy())
+    got = np.concatenate(got).astype(np.float64)
+    want64 = vecs.astype(np.float64)
+    cos = (got * want64).sum(1) / np.maximum(np.linalg.norm(got, axis=1) * np.linalg.norm(want64, axis=1), 1e-300)
+    out = {"rows": int(len(lens)), "vectors": int(len(got)), "cos_min": float(cos.min()),
+           "max_abs": float(np.abs(got - want64).max()),
+           "bound": "cosine >= 0.9999 and max-abs <= 1e-4" if wl.dtype == "f32" else "cosine >= 0.999"}
+    if got_scores:
+        out["scores_max_abs"] = float(np.abs(np.concatenate(got_scores) - scores).max())
+    out["ok"] = bool(out["cos_min"] >= (0.9999 if wl.dtype == "f32" else 0.999) and
+                     (wl.dtype != "f32" or out["max_abs"] <= 1e-4))
+    return out
 
 
 def metric_of(wl):
@@ -254,9 +348,14 @@ def run_reference(args, wl):
     rank, world, _ = env_rank()
     if rank != 0:
         return
+    from oracle import oracle
     desc = wl.desc()
     cores = os.cpu_count() or 1
     times, toks = [], []
+    # The weights are prepared (transposed) once for the process, as the
+    # reference's CPU backend prepares them at model load; every step is
+    # then the encoder alone on a fresh sample.
+    oracle.keep_weights(True)
     for step in range(args.warmup + args.steps):
         rows = sample_rows(wl, wl.ref_rows, 7000 + step)
         t0 = time.perf_counter()
@@ -264,16 +363,18 @@ def run_reference(args, wl):
         if step >= args.warmup:
             times.append(time.perf_counter() - t0)
             toks.append(int(np.sum(rows[3])))
+    oracle.keep_weights(False)
     value = sum(toks) / sum(times)
-    sample = (f"each step {len(rows[3])} row(s) of the {wl.key} distribution through all {wl.layers} layers in F32 "
-              f"(the reference CPU encoder's algorithm, oracle/; the Rust original is not buildable here)")
+    sample = (f"each step {len(rows[3])} row(s) of the {wl.key} distribution ({int(np.mean(toks))} live tokens on "
+              f"average) through all {wl.layers} layers in F32, weights prepared once per process (the reference CPU "
+              f"encoder's algorithm, oracle/; the Rust original is not buildable here)")
     print(json.dumps({"impl": "reference", "metric": metric_of(wl), "value": value, "unit": "tokens/s",
                       "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                       "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True, "scaling": "weak",
                       "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                      "config": {"workload": wl.text, "config": wl.key, "seq_len": wl.seq},
+                      "config": {"workload": wl.text, "config": wl.key, "numerics_allowed": numeric_names(wl.numerics), "seq_len": wl.seq},
                       "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                                       "sample": sample},
+                                       "cpu": cpu_model(), "sample": sample},
                       "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
           flush=True)
 
@@ -358,7 +459,9 @@ def main():
     types = None if types_all is None else types_all[mine]
     ranges = wl.ranges(2000 + rank, lens) if wl.ranges else None
     max_ranges = 0 if ranges is None else len(ranges)
-    sess = model.session(max(counts), wl.seq, wl.precision, task=wl.task, max_ranges=max_ranges)
+    sess = model.session(max(counts), wl.seq, wl.precision, task=wl.task, max_ranges=max_ranges,
+                         numerics=wl.numerics)
+    sess.max_batch = max(counts)
     live = int(mask.sum())
     if wl.head:
         hw, hb = head_weights(wl)
@@ -400,6 +503,16 @@ def main():
         wall = time.perf_counter() - t0
     launches = int(lib.turbo_b200_kernel_launches() - launches0)
     barrier()
+    # Each rank's live tokens and device ms a step, so a 1 -> N curve shows
+    # whether sharding (tokens) or the GPUs (ms per token) limit it.
+    per_rank = None
+    if dist is not None:
+        import torch
+        mine_t = torch.tensor([float(live), sum(dev_ms) / args.steps], dtype=torch.float64, device=f"cuda:{local}")
+        every = [torch.zeros_like(mine_t) for _ in range(world)]
+        dist.all_gather(every, mine_t)
+        per_rank = {"live_tokens": [int(t[0].item()) for t in every],
+                    "ms_per_step": [round(float(t[1].item()), 3) for t in every]}
     total_ms = max_over_ranks(sum(dev_ms))
     wall = max_over_ranks(wall)
     tokens_all = sum_over_ranks(float(live))
@@ -478,18 +591,29 @@ def main():
         local_vec = torch.empty((n_vec, wl.hidden), dtype=torch.float32, device=f"cuda:{local}")
         assert lib.turbo_b200_buffer_copy(run.output, local_vec.data_ptr(), local_vec.numel() * 4, None) == 0
         torch.cuda.synchronize(local)
-        t0 = time.perf_counter()
+        # The first all-gather brings the communicator up: untimed. Then 10
+        # timed by CUDA events on torch's stream (NCCL runs on it), max over
+        # ranks.
         allv = shard.gather_vectors(local_vec, vec_counts)
         torch.cuda.synchronize(local)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            allv = shard.gather_vectors(local_vec, vec_counts)
+        e1.record()
+        torch.cuda.synchronize(local)
+        g_ms = max_over_ranks(e0.elapsed_time(e1) / 10)
         off = sum(vec_counts[:rank])
-        gather = {"ms": 1000 * (time.perf_counter() - t0), "rows": int(allv.shape[0]),
-                  "bytes": int(allv.numel() * 4),
+        gather = {"ms": g_ms, "repeats": 10, "rows": int(allv.shape[0]), "bytes": int(allv.numel() * 4),
+                  "GB_per_s": allv.numel() * 4 / (g_ms / 1000) / 1e9,
                   "matches_local": bool(torch.equal(allv[off:off + vec_counts[rank]], local_vec))}
 
     if rank == 0:
-        cpu = None
+        cpu = par = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_baseline(wl, desc)
+            cpu, cpu_rows, want = cpu_baseline(wl, desc)
+            par = parity(wl, sess, cpu_rows, want)
         kernel = "gemm_tf32 (tcgen05 kind::tf32, three products a multiply-add" if f32 else "gemm_tc (tcgen05 GEMM"
         out = {
             "metric": metric_of(wl), "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -515,6 +639,9 @@ def main():
                          "launches_per_step": g_n // 3},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "e2e_device_rows": e2e_dev,
+            "numerics_used": numeric_names(sess.numerics_used),
+            "choices": sess.choices,
+            "pdl": os.environ.get("TB_PDL", "1") != "0",
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
@@ -522,6 +649,10 @@ def main():
             out["pairs_per_s"] = wl.per_gpu * world * args.steps / (total_ms / 1000.0)
         if cpu is not None:
             out["cpu_baseline"] = cpu
+        if par is not None:
+            out["parity"] = par
+        if per_rank is not None:
+            out["per_rank"] = per_rank
         if gather is not None:
             out["allgather"] = gather
         print(json.dumps(out), flush=True)

@@ -109,8 +109,10 @@ TB_EXPORT int32_t turbo_b200_wait_check(uint64_t limit_ns, int32_t *fault_out, i
  * mma.sync kernel, 1 the SIMT kernel (any dtype), 2 the tcgen05 kernel with
  * one 128-query tile a CTA, 3 the tcgen05 kernel with two (whole rows only),
  * 4 (F32 only) the EXACT tier's tcgen05 kind::tf32 kernel with the
- * three-product split (the lo halves of qkv made on the host), the last
- * three for head width 64. ctx_out [tokens, hidden]. */
+ * three-product split (the lo halves of qkv made on the host), 5 the
+ * tcgen05 kernel with double-buffered scores on head pairs, 6 the same on
+ * query pairs (whole rows only), the last five for head width 64. ctx_out
+ * [tokens, hidden]. */
 TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t variant, uint32_t batch, const int32_t *lens,
                                              const float *qkv, const uint8_t *live, uint32_t heads,
                                              uint32_t head_dim, int32_t window, float *ctx_out, turbo_error *err);

@@ -59,6 +59,12 @@ void oracle_rerank_head(const float *x, uint32_t n, uint32_t hidden, const float
 int32_t oracle_quantize(uint32_t quantization, const float *x, uint32_t rows, uint32_t dim, const float *ranges,
                         uint8_t *out);
 
+/* Keep the model of the next pass prepared (its F32 tensors and transposed
+ * linears) for later passes on the same model while `on` is set; 0 frees
+ * it. Off by default: a timed CPU baseline turns it on so its passes time
+ * the encoder alone. */
+void oracle_keep_weights(int32_t on);
+
 #ifdef __cplusplus
 }
 #endif

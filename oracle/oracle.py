@@ -36,6 +36,7 @@ def lib():
         _lib.oracle_rope_table.argtypes = [C.c_double, C.c_double, C.c_uint32, C.c_uint32, C.c_void_p]
         _lib.oracle_quantize.argtypes = [C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
         _lib.oracle_quantize.restype = C.c_int32
+        _lib.oracle_keep_weights.argtypes = [C.c_int32]
         _lib.oracle_rerank_head.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                             C.c_void_p, C.c_void_p]
     return _lib
@@ -95,6 +96,12 @@ def rerank_head(x, pooler_w, pooler_b, cls_w, cls_b):
                              *[None if a is None else a.ctypes.data_as(C.c_void_p) for a in args],
                              scores.ctypes.data_as(C.c_void_p))
     return scores
+
+
+def keep_weights(on):
+    """Keep the next pass's model prepared for the passes after it (True),
+    or free it (False): for timed loops over one model."""
+    lib().oracle_keep_weights(1 if on else 0)
 
 
 def quantize(quantization, x, ranges=None):

@@ -23,8 +23,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", str(ROOT / "include"),
          "--expt-relaxed-constexpr"]
 SOURCES = ["backend.cpp", "hooks.cpp", "rowwise.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "attention_tc.cu",
-           "noalloc.cu", "quantize.cu", "gemm_tf32.cu", "devrows.cu", "attention_tf32.cu"]
-HEADERS = [CSRC / "kernels.h", CSRC / "common.cuh", CSRC / "tcgen05.cuh", ROOT / "include/turbo_b200.h", ROOT / "include/turbo/turbo_abi.h"]
+           "noalloc.cu", "quantize.cu", "gemm_tf32.cu", "devrows.cu", "attention_tf32.cu", "attention_fa.cu"]
+HEADERS = [CSRC / "kernels.h", CSRC / "common.cuh", CSRC / "tcgen05.cuh", CSRC / "softmax.cuh", ROOT / "include/turbo_b200.h", ROOT / "include/turbo/turbo_abi.h"]
 
 
 def _stale(obj: Path, src: Path) -> bool:

@@ -815,6 +815,17 @@ bool attention_pairs(const Session *s) {
     }();
     return on && attention_kind(s) == AttnKind::TC;
 }
+// The tcgen05 attention of F16/BF16 sessions at head width 64 runs
+// attention_fa (scores double-buffered in tensor memory) when the
+// environment sets TB_ATTN_FA=1, else attention_tc and attention_tc2 (an
+// A/B switch, read once).
+bool attention_fa_on() {
+    static const bool on = [] {
+        const char *v = getenv("TB_ATTN_FA");
+        return v && v[0] == '1';
+    }();
+    return on;
+}
 int attention_queries(const Session *s) {
     switch (attention_kind(s)) {
     case AttnKind::TC:
@@ -1325,6 +1336,14 @@ cudaError_t encode(Session *s) {
     cudaError_t e;
     auto attention_raw = [&](int window) -> cudaError_t {
         const AttnKind kind = attention_kind(s);
+        if (kind == AttnKind::TC && attention_fa_on()) {
+            // Double-buffered scores, one CTA an SM: query pairs sharing K
+            // and V for whole rows of long batches, head pairs otherwise.
+            const bool qpair = window < 0 && s->n_attn2 > 0;
+            return attention_fa(dt, s->map_qkv, s->map_qkv64, s->ctxb, pk.tok_live,
+                                (const AttnItem *)(s->plan_dev + (qpair ? s->lay.attn2 : s->lay.attn)),
+                                qpair ? s->n_attn2 : s->n_attn, m->heads, dh, h, window, qpair, s->ctx->fault_dev, st);
+        }
         if (kind == AttnKind::TC && window < 0 && s->n_attn2)
             return attention_tc2(dt, s->map_qkv, s->map_qkv64, s->ctxb, pk.tok_live,
                                  (const AttnItem *)(s->plan_dev + s->lay.attn2), s->n_attn2, m->heads, dh, h,

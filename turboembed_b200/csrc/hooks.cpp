@@ -318,11 +318,14 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
     int T = 0, max_len = 0;
     if (variant == 4 && (dt != Dt::F32 || head_dim != 64))
         return hook_fail(err, TURBO_E_UNSUPPORTED, "variant 4 takes F32 at head width 64", cudaSuccess);
+    if ((variant == 5 || variant == 6) && (dt == Dt::F32 || head_dim != 64))
+        return hook_fail(err, TURBO_E_UNSUPPORTED, "variants 5 and 6 take F16 or BF16 at head width 64", cudaSuccess);
     const int qt = variant == 0   ? ATTN_MMA_QUERIES
-                   : variant == 2 || variant == 4 ? ATTN_TC_QUERIES
-                   : variant == 3 ? ATTN_TC2_QUERIES
+                   : variant == 2 || variant == 4 || variant == 5 ? ATTN_TC_QUERIES
+                   : variant == 3 || variant == 6 ? ATTN_TC2_QUERIES
                                   : ATTN_F32_QUERIES;
-    if (variant == 3 && window >= 0) return hook_fail(err, TURBO_E_INVALID_ARGUMENT, "variant 3 has no window", cudaSuccess);
+    if ((variant == 3 || variant == 6) && window >= 0)
+        return hook_fail(err, TURBO_E_INVALID_ARGUMENT, "variants 3 and 6 have no window", cudaSuccess);
     for (uint32_t b = 0; b < batch; ++b) {
         int holes = 0;
         for (int p = 0; p < lens[b]; ++p) holes |= !live[T + p];
@@ -343,7 +346,7 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
     if (e != cudaSuccess) return hook_fail(err, TURBO_E_RUNTIME, "attention_check setup", e);
     int *fault = (int *)dv.get(4);
     if (variant == 0) e = attention_mma(dt, dq, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, 0);
-    else if (variant == 2 || variant == 3) {
+    else if (variant == 2 || variant == 3 || variant == 5 || variant == 6) {
         CUtensorMap map, map64;
         e = make_operand_map(dt, dq, (uint64_t)T, (uint64_t)3 * h, (uint64_t)3 * h, 128, &map);
         if (e == cudaSuccess) e = make_operand_map(dt, dq, (uint64_t)T, (uint64_t)3 * h, (uint64_t)3 * h, 64, &map64);
@@ -351,6 +354,9 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
             e = attention_tc(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window, fault, 0);
         if (e == cudaSuccess && variant == 3)
             e = attention_tc2(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, fault, 0);
+        if (e == cudaSuccess && (variant == 5 || variant == 6))
+            e = attention_fa(dt, map, map64, dc, dl, di, (int)items.size(), (int)heads, (int)head_dim, h, window,
+                             variant == 6, fault, 0);
     }
     else if (variant == 4) {
         // The lo halves the EXACT QKV GEMM writes beside qkv, made here.
