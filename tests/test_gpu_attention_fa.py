@@ -1,7 +1,8 @@
 """The double-buffered tcgen05 attention (attention_fa.cu) alone, through the
 attention check hook, against attention in F64 on the same narrowed
-operands: variant 5 runs head pairs (any window, items of 128 queries),
-variant 6 query pairs sharing K and V (whole rows, items of 256 queries).
+operands: variant 5 runs head pairs (any window, items of 128 queries; head
+widths 64 and 32), variant 6 query pairs sharing K and V (whole rows, items
+of 256 queries; width 64).
 The cases cover rows of one chunk and of many, odd head counts (a unit with
 one tile), rows whose last 256-query item has one tile, masked keys,
 windows, many units a persistent CTA, and the lazy rescale of O."""
@@ -23,12 +24,11 @@ CASES = [([128], 2, -1), ([300, 5, 129], 12, -1), ([500, 130], 2, 64), ([1], 1, 
 @pytest.mark.parametrize("dtype", [F16, BF16])
 @pytest.mark.parametrize("case", CASES)
 @pytest.mark.parametrize("holes", [True, False])
-@pytest.mark.parametrize("variant", [5, 6])
-def test_double_buffered_attention(dtype, case, holes, variant):
+@pytest.mark.parametrize("variant,d", [(5, 64), (6, 64), (5, 32)])
+def test_double_buffered_attention(dtype, case, holes, variant, d):
     lens, heads, window = case
     if variant == 6 and window >= 0:
         pytest.skip("query pairs run whole rows only")
-    d = 64
     T = sum(lens)
     rng = np.random.default_rng(T + heads + 11)
     qkv = narrow(rng.standard_normal((T, 3 * heads * d)).astype(np.float32) * 2, dtype)
@@ -40,12 +40,12 @@ def test_double_buffered_attention(dtype, case, holes, variant):
 
 
 @pytest.mark.parametrize("dtype", [F16, BF16])
-@pytest.mark.parametrize("variant", [5, 6])
-def test_double_buffered_attention_rescales_when_the_max_grows(dtype, variant):
+@pytest.mark.parametrize("variant,d", [(5, 64), (6, 64), (5, 32)])
+def test_double_buffered_attention_rescales_when_the_max_grows(dtype, variant, d):
     # Key magnitudes ramp up along the row, so later 64-key chunks raise the
     # running max far past the first: O in tensor memory is rescaled while
     # the next chunk's P V may still be in flight.
-    lens, heads, d = [400, 70, 700], 2, 64
+    lens, heads = [400, 70, 700], 2
     T = sum(lens)
     rng = np.random.default_rng(97)
     qkv = rng.standard_normal((T, 3 * heads * d)).astype(np.float32)

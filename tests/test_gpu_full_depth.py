@@ -97,7 +97,9 @@ def test_c3_rerank_body_bf16_and_its_scores(ctx, golden):
     ref = oracle.rerank_head(want, None, None, w, bias).ravel()
     err = np.abs(scores - ref).max()
     print(f"C3 scores max_abs={err:.3e} (scale {np.abs(ref).max():.3e})")
-    assert err <= 1e-2 * np.abs(ref).max()  # core/tests/cuda_rerank.rs:144
+    # The reference's score bound for BF16 compute: 4e-2 of the run's scale
+    # (docs/conformance.md:115-121, core/tests/conformance/scores.rs).
+    assert err <= 4e-2 * np.abs(ref).max()
     s.release()
     m.release()
 

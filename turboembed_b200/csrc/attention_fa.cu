@@ -1,5 +1,5 @@
-// attention_fa.cu -- varlen flash attention at head width 64 on the 5th-gen
-// tensor cores, F16/BF16 operands, F32 sums, with the score tile
+// attention_fa.cu -- varlen flash attention at head widths 64 and 32 on the
+// 5th-gen tensor cores, F16/BF16 operands, F32 sums, with the score tile
 // double-buffered in tensor memory so the tensor pipe computes the next
 // chunk's S = Q K^T while the softmax works on this one.
 //
@@ -7,7 +7,14 @@
 // attend.rs:95-198): a key whose mask entry is 0, past the row's end, or
 // outside a sliding window scores -inf; a query that reads no live key gets
 // a zero context. It replaces the reference's FASTEST attention_fa_kernel
-// (core/cuda/kernels.cu:4142, mma.sync m16n8k16) for head width 64.
+// (core/cuda/kernels.cu:4142, mma.sync m16n8k16) for head widths 64 and 32.
+//
+// Head width 32 runs head pairs only: heads h and h + 1 (h even) are one
+// 64-column TMA box of Q, of K and of V, loaded once for both tiles. Tile
+// t's S = Q K^T takes the two 16-wide k steps of its head (columns 32 t ..
+// 32 t + 31 of both boxes); its P V runs N = 64 over both heads' V, and the
+// tile keeps columns 32 t .. 32 t + 31 of O (the softmax, not the tensor
+// pipe, bounds attention at this width, so the spare half costs little).
 //
 // One persistent CTA an SM, 320 threads, looping over units; a unit is two
 // 128-query tiles, each with its own softmax warpgroup:
@@ -50,9 +57,9 @@ namespace {
 using namespace tc;
 using namespace sm;
 
-constexpr int KT = 64, D = 64;
+constexpr int KT = 64, D = 64;  // keys a chunk; columns of a Q / K / V box (one head of 64, two of 32)
 constexpr int Q_BYTES = QT * D * 2;   // 16 KB: one tile's Q
-constexpr int KV_BYTES = KT * D * 2;  // 8 KB: one head's K (or V) chunk
+constexpr int KV_BYTES = KT * D * 2;  // 8 KB: one box of a K (or V) chunk
 constexpr int NKV = 3;                // K and V stages (two heads' chunks each)
 constexpr int SQ = 0;                             // Q [2 units in flight][2 tiles]
 constexpr int SK = SQ + 4 * Q_BYTES;              // K [NKV][2 heads]
@@ -61,7 +68,10 @@ constexpr int SB = SV + NKV * 2 * KV_BYTES;       // barriers, TMEM slot, abort 
 constexpr int SMEM = SB + 512 + 1024;             // + alignment slack
 constexpr int TILE_COLS = 192, O_COL = 128;
 constexpr float RESCALE = 8.0f;  // log2 units
-constexpr float SCALE_LOG2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+// 1/sqrt(head width) * log2(e)
+template <int DH> __device__ __forceinline__ constexpr float scale_log2() {
+    return DH == 64 ? 0.125f * 1.4426950408889634f : 0.17677669529663688f * 1.4426950408889634f;
+}
 
 // Barrier offsets (bytes from SB): q_full[2], q_empty[2], k_full[NKV],
 // k_empty[NKV], v_full[NKV], v_empty[NKV], then per tile s_full[2],
@@ -81,6 +91,7 @@ struct Unit {
     bool kv2;   // the tiles read two heads' K and V (head pairs)
 };
 
+template <int DH>
 __device__ __forceinline__ Unit unit_of(const AttnItem *__restrict__ items, int u, int heads, int window, bool qpair) {
     Unit n;
     int head0, head1;
@@ -99,13 +110,13 @@ __device__ __forceinline__ Unit unit_of(const AttnItem *__restrict__ items, int 
         head1 = head0 + 1;
         n.q[0] = n.q[1] = it.q0;
         n.has1 = head1 < heads;
-        n.kv2 = n.has1;
+        n.kv2 = DH == 64 && n.has1;  // head width 32: both heads in one box
     }
     n.start = it.start;
     n.len = it.len;
     n.holes = it.holes;
-    n.col[0] = head0 * D;
-    n.col[1] = head1 * D;
+    n.col[0] = head0 * DH;
+    n.col[1] = head1 * DH;
     int klo, khi;
     key_range(it.len, it.q0, window, klo, khi);  // query pairs run whole rows only (window < 0)
     n.klo = klo;
@@ -121,8 +132,8 @@ struct Bars {
 // the head at column col): chunks of keys from n.klo; `g` counts this
 // tile's chunks (barrier phases) over the units. lane_base addresses this
 // warp's TMEM lanes at the tile's first column.
-template <class T>
-__device__ __forceinline__ bool softmax_unit(const Unit &n, int q0, int col, int window, T *__restrict__ ctx, int h,
+template <class T, int DH>
+__device__ __forceinline__ bool softmax_unit(const Unit &n, int t, int q0, int col, int window, T *__restrict__ ctx, int h,
                                              const uint8_t *__restrict__ live, uint32_t lane_base, int r,
                                              const Bars &b, uint32_t &g, volatile int *abort_flag, int *fault) {
     const int lane = threadIdx.x & 31;
@@ -174,7 +185,7 @@ __device__ __forceinline__ bool softmax_unit(const Unit &n, int q0, int col, int
 #pragma unroll
         for (int k = 0; k < 4; ++k) m4[k] = fmaxf(m4[k], sv[60 + k]);
         float mx = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
-        mx = mx == -INFINITY ? mx : mx * SCALE_LOG2;
+        mx = mx == -INFINITY ? mx : mx * scale_log2<DH>();
         const bool move = mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + RESCALE);
         float f = 1.0f;
         if (move) {
@@ -187,17 +198,19 @@ __device__ __forceinline__ bool softmax_unit(const Unit &n, int q0, int col, int
             if (!mbar_wait(b.o[(g - 1) & 1], ((g - 1) >> 1) & 1, abort_flag, fault)) return false;
             tc_fence_after();
             __syncwarp();
+            // This tile's O columns: all 64, or its head's 32 at width 32.
+            const uint32_t o0 = lane_base + O_COL + (DH == 32 ? t * 32 : 0);
 #pragma unroll 1
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < DH / 16; ++q) {
                 float o[16];
-                tmem_ld16(lane_base + O_COL + q * 16, o);
+                tmem_ld16(o0 + q * 16, o);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) o[i] *= f;
-                tmem_st16(lane_base + O_COL + q * 16, o);
+                tmem_st16(o0 + q * 16, o);
             }
         }
         const float mu = m_ref == -INFINITY ? 0.0f : m_ref;
-        const uint64_t c2 = pk2(SCALE_LOG2, SCALE_LOG2), nmu = pk2(-mu, -mu);
+        const uint64_t c2 = pk2(scale_log2<DH>(), scale_log2<DH>()), nmu = pk2(-mu, -mu);
         uint64_t s4[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
@@ -229,9 +242,9 @@ __device__ __forceinline__ bool softmax_unit(const Unit &n, int q0, int col, int
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     T *out = ctx + ((int64_t)n.start + qi) * h + col;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
+    for (int half = 0; half < DH / 32; ++half) {
         float o[32];
-        tmem_ld32(lane_base + O_COL + half * 32, o);
+        tmem_ld32(lane_base + O_COL + (DH == 32 ? t * 32 : half * 32), o);
         if (qi < n.len) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -249,7 +262,7 @@ __device__ __forceinline__ bool softmax_unit(const Unit &n, int q0, int col, int
     return true;
 }
 
-template <class T>
+template <class T, int DH>
 __global__ void __launch_bounds__(320, 1)
 attn_fa_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv, T *__restrict__ ctx,
                const uint8_t *__restrict__ live, const AttnItem *__restrict__ items, int n_items, int heads, int h,
@@ -314,12 +327,13 @@ attn_fa_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             bool ok = true;
             int un = 0;
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++un) {
-                const Unit n = unit_of(items, u, heads, window, qp);
+                const Unit n = unit_of<DH>(items, u, heads, window, qp);
                 const uint32_t qb = un & 1;
                 if (un >= 2 && !(ok = mbar_wait(bar + B_QE + 8 * qb, ((un >> 1) - 1) & 1, abort_flag, fault))) break;
-                mbar_expect_tx(bar + B_QF + 8 * qb, (n.has1 ? 2 : 1) * Q_BYTES);
+                const bool q2 = DH == 64 && n.has1;  // width 32: one box holds both heads' Q
+                mbar_expect_tx(bar + B_QF + 8 * qb, (q2 ? 2 : 1) * Q_BYTES);
                 tma_load_2d(s0 + SQ + (qb * 2) * Q_BYTES, &tq, n.col[0], n.start + n.q[0], bar + B_QF + 8 * qb);
-                if (n.has1)
+                if (q2)
                     tma_load_2d(s0 + SQ + (qb * 2 + 1) * Q_BYTES, &tq, n.col[1], n.start + n.q[1], bar + B_QF + 8 * qb);
                 const uint32_t kv_bytes = (n.kv2 ? 2 : 1) * KV_BYTES;
                 for (int j = 0; j < n.nch && ok; ++j, ++c) {
@@ -354,7 +368,7 @@ attn_fa_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             auto start = [&](Cursor &k) {
                 k.u = blockIdx.x, k.un = 0, k.j = 0, k.c = 0, k.g1 = 0;
                 k.valid = k.u < units;
-                if (k.valid) k.n = unit_of(items, k.u, heads, window, qp);
+                if (k.valid) k.n = unit_of<DH>(items, k.u, heads, window, qp);
             };
             auto advance = [&](Cursor &k) {
                 if (k.n.has1) ++k.g1;
@@ -364,7 +378,7 @@ attn_fa_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 k.u += gridDim.x;
                 ++k.un;
                 k.valid = k.u < units;
-                if (k.valid) k.n = unit_of(items, k.u, heads, window, qp);
+                if (k.valid) k.n = unit_of<DH>(items, k.u, heads, window, qp);
             };
             bool ok = true;
             // S of the chunk at cursor k for both tiles (Q and K waited for).
@@ -378,12 +392,15 @@ attn_fa_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                     if (t == 1 && !k.n.has1) break;
                     const uint32_t g = t ? k.g1 : k.c;
                     const uint32_t d = tmem + t * TILE_COLS + (g & 1) * 64;
-                    const uint32_t q = s0 + SQ + (qb * 2 + t) * Q_BYTES;
+                    const uint32_t q = s0 + SQ + (qb * 2 + (DH == 32 ? 0 : t)) * Q_BYTES;
                     const uint32_t kk_base = s0 + SK + (st * 2 + (k.n.kv2 ? t : 0)) * KV_BYTES;
+                    // Width 64: the box's four k steps; width 32: the head's
+                    // two (columns 32 t .. 32 t + 31 of the shared box).
+                    const int k_first = DH == 32 ? 2 * t : 0;
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; ++kk)
-                        umma_f16(d, smem_desc(q) + (uint64_t)(kk * 2), smem_desc(kk_base) + (uint64_t)(kk * 2), ids,
-                                 kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < DH / 16; ++kk)
+                        umma_f16(d, smem_desc(q) + (uint64_t)((k_first + kk) * 2),
+                                 smem_desc(kk_base) + (uint64_t)((k_first + kk) * 2), ids, kk > 0 ? 1u : 0u);
                     umma_commit(tile_bars(t).s[g & 1]);
                 }
                 umma_commit(bar + B_KE + 8 * st);  // K stage free once these S are done
@@ -435,10 +452,10 @@ attn_fa_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         const Bars b = tile_bars(t);
         uint32_t g = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
-            const Unit n = unit_of(items, u, heads, window, qp);
+            const Unit n = unit_of<DH>(items, u, heads, window, qp);
             if (t == 1 && !n.has1) continue;
-            if (!softmax_unit<T>(n, t ? n.q[1] : n.q[0], t ? n.col[1] : n.col[0], window, ctx, h, live, lane_base, r, b,
-                                 g, abort_flag, fault))
+            if (!softmax_unit<T, DH>(n, t, t ? n.q[1] : n.q[0], t ? n.col[1] : n.col[0], window, ctx, h, live,
+                                     lane_base, r, b, g, abort_flag, fault))
                 break;
         }
     }
@@ -457,32 +474,38 @@ int sm_count() {
     return sms;
 }
 
-template <class T>
+template <class T, int DH>
 cudaError_t launch(const CUtensorMap &mq, const CUtensorMap &mkv, void *ctx, const uint8_t *live,
                    const AttnItem *items, int n_items, int heads, int h, int window, bool qpair, int *fault,
                    cudaStream_t s) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fa_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaError_t e = cudaFuncSetAttribute(attn_fa_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return e;
     const int units = qpair ? n_items * heads : n_items * ((heads + 1) / 2);
     const int sms = sm_count();
     const int grid = units < sms ? units : sms;
-    return launch_pdl(attn_fa_kernel<T>, grid, 320, SMEM, s, mq, mkv, (T *)ctx, live, items, n_items, heads, h, window,
-                      qpair ? 1 : 0, fault);
+    return launch_pdl(attn_fa_kernel<T, DH>, grid, 320, SMEM, s, mq, mkv, (T *)ctx, live, items, n_items, heads, h,
+                      window, qpair ? 1 : 0, fault);
 }
 
 }  // namespace
+
+bool attention_fa_takes(int head_dim, bool qpair) { return head_dim == 64 || (head_dim == 32 && !qpair); }
 
 cudaError_t attention_fa(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_map, void *ctx,
                          const uint8_t *tok_live, const AttnItem *items, int n_items, int heads, int head_dim,
                          int hidden, int window, bool qpair, int *fault, cudaStream_t s) {
     if (n_items == 0) return cudaSuccess;
-    if (head_dim != D || (qpair && window >= 0)) return cudaErrorNotSupported;
-    if (dt == Dt::F16)
-        return launch<__half>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, qpair, fault, s);
-    if (dt == Dt::BF16)
-        return launch<__nv_bfloat16>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, qpair,
-                                     fault, s);
-    return cudaErrorNotSupported;
+    if (!attention_fa_takes(head_dim, qpair) || (qpair && window >= 0)) return cudaErrorNotSupported;
+    if (dt != Dt::F16 && dt != Dt::BF16) return cudaErrorNotSupported;
+    const bool f16 = dt == Dt::F16;
+    if (head_dim == 64)
+        return f16 ? launch<__half, 64>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, qpair,
+                                        fault, s)
+                   : launch<__nv_bfloat16, 64>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window,
+                                               qpair, fault, s);
+    return f16 ? launch<__half, 32>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, false, fault, s)
+               : launch<__nv_bfloat16, 32>(q_map, kv_map, ctx, tok_live, items, n_items, heads, hidden, window, false,
+                                           fault, s);
 }
 
 }  // namespace tb

@@ -798,10 +798,12 @@ PlanLayout plan_layout(int tokens, int vectors, int attn_items, int attn2_items)
 // mma.sync for 16 and 32; at EXACT tcgen05 kind::tf32 (three products) when
 // the session's QKV GEMM writes the lo halves, else the FFMA kernel; SIMT
 // for other widths.
-enum class AttnKind { TC, MMA, SIMT, TF32 };
+enum class AttnKind { TC, FA, MMA, SIMT, TF32 };
+bool attention_fa_on();
 AttnKind attention_kind(const Session *s) {
     const int dh = s->m->hidden / s->m->heads;
     if (s->dt == Dt::F32) return s->tf32_attn ? AttnKind::TF32 : AttnKind::SIMT;
+    if (attention_fa_on() && attention_fa_takes(dh, false)) return AttnKind::FA;
     if (dh == 64) return AttnKind::TC;
     return attention_mma_takes(dh) ? AttnKind::MMA : AttnKind::SIMT;
 }
@@ -813,7 +815,8 @@ bool attention_pairs(const Session *s) {
         const char *v = getenv("TB_ATTN2");
         return !(v && v[0] == '0');
     }();
-    return on && attention_kind(s) == AttnKind::TC;
+    const AttnKind k = attention_kind(s);
+    return on && (k == AttnKind::TC || (k == AttnKind::FA && attention_fa_takes(s->m->hidden / s->m->heads, true)));
 }
 // The tcgen05 attention of F16/BF16 sessions at head width 64 runs
 // attention_fa (scores double-buffered in tensor memory) when the
@@ -829,6 +832,7 @@ bool attention_fa_on() {
 int attention_queries(const Session *s) {
     switch (attention_kind(s)) {
     case AttnKind::TC:
+    case AttnKind::FA:
     case AttnKind::TF32: return ATTN_TC_QUERIES;
     case AttnKind::MMA: return ATTN_MMA_QUERIES;
     default: return ATTN_F32_QUERIES;
@@ -1336,7 +1340,7 @@ cudaError_t encode(Session *s) {
     cudaError_t e;
     auto attention_raw = [&](int window) -> cudaError_t {
         const AttnKind kind = attention_kind(s);
-        if (kind == AttnKind::TC && attention_fa_on()) {
+        if (kind == AttnKind::FA) {
             // Double-buffered scores, one CTA an SM: query pairs sharing K
             // and V for whole rows of long batches, head pairs otherwise.
             const bool qpair = window < 0 && s->n_attn2 > 0;

@@ -210,10 +210,11 @@ cudaError_t attention_tc2(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv
                           int hidden, int *fault, cudaStream_t s);
 
 // The same with the score tile double-buffered in tensor memory, one CTA an
-// SM and two 128-query tiles a unit (attention_fa.cu): qpair = false takes
-// items of 128 queries (units: item x head pair), any window; qpair = true
-// items of 256 queries (units: item x head, the two halves sharing K and V),
-// whole rows only (window < 0).
+// SM and two 128-query tiles a unit (attention_fa.cu), head widths 64 and
+// 32: qpair = false takes items of 128 queries (units: item x head pair),
+// any window; qpair = true (width 64) items of 256 queries (units: item x
+// head, the two halves sharing K and V), whole rows only (window < 0).
+bool attention_fa_takes(int head_dim, bool qpair);
 cudaError_t attention_fa(Dt dt, const CUtensorMap &q_map, const CUtensorMap &kv_map, void *ctx,
                          const uint8_t *tok_live, const AttnItem *items, int n_items, int heads, int head_dim,
                          int hidden, int window, bool qpair, int *fault, cudaStream_t s);
