@@ -469,8 +469,9 @@ int32_t tb_buffer_import(void *ctx, const turbo_buffer_desc *d, const turbo_nati
         const bool fits = pl == TURBO_PLACE_SHARED ? a.type == cudaMemoryTypeManaged
                                                    : a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
         if (!fits)
-            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle: the pointer is %s, not %s memory", memory_name(a.type),
-                        placement_text(pl));
+            return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle: the pointer is %s; a CUDA_PTR as %s takes %s",
+                        memory_name(a.type), placement_text(pl),
+                        pl == TURBO_PLACE_SHARED ? "managed memory" : "device or managed memory");
         if (a.type == cudaMemoryTypeDevice && a.device != c->device)
             return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "handle: memory of device %d, and this context is on device %d",
                         a.device, c->device);
