@@ -130,7 +130,7 @@ WORKLOADS = {
                          "L~U[16,128], mean + L2, EXACT (F32)", "minilm", 0, abi.TURBO_DTYPE_F32,
                    abi.TURBO_PRECISION_EXACT, "f32", 32, 128,
                    lambda seed, n: _no_types(models.rows_bert(seed, n, 16, 128, 128)), abi.TURBO_POOLING_MEAN,
-                   abi.TURBO_NORMALIZE_L2, cpu_rows=512, ref_rows=128),
+                   abi.TURBO_NORMALIZE_L2, cpu_rows=512, ref_rows=128, numerics=F32_TF32),
     "c2": Workload("c2", "BERT-base (BASELINE config 2): 12L h768 12 heads FFN3072 GELU, batch 256/GPU, "
                          "L~U[64,512], CLS + L2, FASTEST (F16 operands, F32 sums), varlen-packed", "bert-base", 1,
                    abi.TURBO_DTYPE_F32, abi.TURBO_PRECISION_FASTEST, "f16", 256, 512,

@@ -316,10 +316,13 @@ def test_f32_attention(case):
 
 @pytest.mark.parametrize("case", TC_CASES)
 @pytest.mark.parametrize("holes", [True, False])
-def test_tf32x3_attention_has_f32_accuracy(case, holes):
+@pytest.mark.parametrize("width", [64, 32])
+def test_tf32x3_attention_has_f32_accuracy(case, holes, width):
     # The EXACT tier's tensor-core attention (kind::tf32, three products for
-    # Q K^T and for P V): to the bound of the FFMA kernel against F64.
+    # Q K^T and for P V): to the bound of the FFMA kernel against F64, at
+    # head widths 64 and 32.
     lens, heads, d, window = case
+    d = width
     T = sum(lens)
     rng = np.random.default_rng(T + d + 7)
     qkv = rng.standard_normal((T, 3 * heads * d)).astype(np.float32)

@@ -63,11 +63,20 @@ def test_exact_with_tf32_allowed_reports_tf32(ctx):
 
 
 def test_exact_with_tf32_allowed_reports_the_ffma_attention_too(ctx):
-    # MiniLM shape (head width 32): the tf32 attention is not built at that
-    # width, so attention runs the FFMA kernel and both classes are reported.
+    # MiniLM shape (head width 32): the tf32 attention runs at that width
+    # too, so TF32 alone. A rotary model (ModernBERT) keeps the FFMA
+    # attention at EXACT, so both classes are reported.
     d = models.synthetic("minilm", 0, layers=1)
     m = ctx.load(d)
     s = open_session(m, 4, 128, EXACT_TF32)
+    assert s.numerics_used == TF32, s.numerics_used
+    cos, mad = _run(s, d, lo=16, hi=128)
+    assert cos >= 0.9999 and mad <= 1e-4, (cos, mad)
+    s.release()
+    m.release()
+    d = models.synthetic("modernbert-base", 3, layers=1)
+    m = ctx.load(d)
+    s = open_session(m, 2, 256, EXACT_TF32)
     assert s.numerics_used == TF32 | F32_FMA, s.numerics_used
     s.release()
     m.release()

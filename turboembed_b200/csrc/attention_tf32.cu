@@ -1,6 +1,6 @@
 // attention_tf32.cu -- the EXACT tier's attention on the 5th-gen tensor
 // cores: F32 operands to F32 accuracy by the three-product split of the
-// EXACT GEMMs (gemm_tf32.cu; Markidis et al., 2018), head width 64.
+// EXACT GEMMs (gemm_tf32.cu; Markidis et al., 2018), head widths 64 and 32.
 //
 // Semantics as attention.cu's F32 kernel (core/src/cpu/kernels/attend.rs:
 // 95-198): a key whose mask entry is 0, past the row's end, or outside a
@@ -11,17 +11,19 @@
 // tensor core reads of an F32 operand of kind::tf32) and lo = x - hi. The
 // QKV GEMM's epilogue writes lo of every output into qkv_lo (same layout as
 // qkv), so Q's and K's halves arrive by TMA; V and P are split here:
-//   S  = Q_lo K^T + Q K_lo^T + Q K^T    M 128 x N 64, 8 steps of K = 8
-//   O += P_lo V + P V_lo + P V          M 128 x N 64, 8 steps of K = 8
+//   S  = Q_lo K^T + Q K_lo^T + Q K^T    M 128 x N 64, DH / 8 steps of K = 8
+//   O += P_lo V + P V_lo + P V          M 128 x N DH, 8 steps of K = 8
 // P (F32) is written by the softmax over its chunk's S columns in TMEM and
 // P_lo = P - hi(P) beside it: the A operands of P V, read from TMEM. The
 // lo x lo products are below F32 precision and left out.
 //
 // Operand tiles are [rows x 32] F32 with the 128-byte swizzle (one swizzle
-// row is 32 floats), all K-major: Q [128 x 64] and K [64 keys x 64] arrive
-// as two TMA boxes each along d; the B operand of P V is V transposed, [64 d
-// x 64 keys] as two boxes along the keys, written by a transposer warpgroup
-// that reads V from global memory (and splits it into hi and lo on the way).
+// row is 32 floats), all K-major: Q [128 x DH] and K [64 keys x DH] arrive
+// as DH / 32 TMA boxes each along d; the B operand of P V is V transposed,
+// [DH d x 64 keys] as two boxes along the keys, written by a transposer
+// warpgroup that reads V from global memory (and splits it into hi and lo
+// on the way). At head width 32 each box holds the head's 32 d rows of a
+// box laid out for 64.
 // An MN-major B of kind::tf32 read as V stands, with A in tensor memory,
 // gave no products on B200 (the accumulator stayed zero at N = 32 and 64),
 // so this kernel does not use one.
@@ -48,15 +50,18 @@ namespace {
 
 using namespace tc;
 
-constexpr int QT = ATTN_TC_QUERIES, KT = 64, D = 64;
+constexpr int QT = ATTN_TC_QUERIES, KT = 64, D = 64;  // D: the widest head the buffers are laid out for
 constexpr int Q_BOX = QT * 32 * 4;       // 16 KB: [128 rows x 32 F32]
 constexpr int K_BOX = KT * 32 * 4;       // 8 KB: [64 rows x 32 F32]
 constexpr int Q_BYTES = 2 * Q_BOX;       // a [128 x 64] F32 tile
 constexpr int KV_BYTES = 2 * K_BOX;      // a [64 x 64] F32 tile
 constexpr int BUF_BYTES = 4 * KV_BYTES;  // a chunk: K, K_lo, V^T, V^T_lo
 constexpr int SMEM = 2 * Q_BYTES + 2 * BUF_BYTES + 256 + 1024;
-constexpr float RESCALE = 8.0f;                              // log2 units
-constexpr float SCALE_LOG2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
+constexpr float RESCALE = 8.0f;  // log2 units
+// 1/sqrt(head width) * log2(e)
+template <int DH> __device__ __forceinline__ constexpr float scale_log2() {
+    return DH == 64 ? 0.125f * 1.4426950408889634f : 0.17677669529663688f * 1.4426950408889634f;
+}
 static_assert(SMEM <= 227 * 1024, "one CTA an SM");
 
 __device__ __forceinline__ float ex2(float x) {
@@ -121,6 +126,7 @@ __device__ __forceinline__ void key_range(int len, int q0, int window, int &klo,
 // each pair of per-buffer barriers (chunk g uses buffer g & 1, so that every
 // wait finds the phase before the awaited one complete). lane_base addresses this warp's TMEM lanes at column 0. Returns
 // false when the kernel must stop.
+template <int DH>
 __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int khi, int window, int head,
                                              float *__restrict__ ctx, int h, const uint8_t *__restrict__ live,
                                              uint32_t lane_base, int r, uint32_t bar_s, uint32_t bar_p,
@@ -172,7 +178,7 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
 #pragma unroll
             for (int k = 0; k < 4; ++k) m4[k] = fmaxf(m4[k], sv[i + k]);
         float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-        mx = mx == -INFINITY ? mx : mx * SCALE_LOG2;
+        mx = mx == -INFINITY ? mx : mx * scale_log2<DH>();
         const bool move = mx != -INFINITY && (m_ref == -INFINITY || mx > m_ref + RESCALE);
         float f = 1.0f;
         if (move) {
@@ -187,7 +193,7 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
             tc_fence_after();
             __syncwarp();
 #pragma unroll 1
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < DH / 16; ++q) {
                 float o[16];
                 tmem_ld16(lane_base + 256 + q * 16, o);
 #pragma unroll
@@ -199,7 +205,7 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
         float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-            sv[i] = ex2(fmaf(sv[i], SCALE_LOG2, -mu));  // 0 for an invalid key (2^-inf)
+            sv[i] = ex2(fmaf(sv[i], scale_log2<DH>(), -mu));  // 0 for an invalid key (2^-inf)
             s4[i & 3] += sv[i];
         }
         // P over the chunk's S columns and P_lo beside it: four stores, one wait.
@@ -222,9 +228,9 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
     tc_fence_after();
     __syncwarp();
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-    float *out = ctx + ((int64_t)it.start + qi) * h + head * D;
+    float *out = ctx + ((int64_t)it.start + qi) * h + head * DH;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
+    for (int half = 0; half < DH / 32; ++half) {
         float o[32];
         tmem_ld32(lane_base + 256 + half * 32, o);
         if (qi < it.len) {
@@ -247,13 +253,23 @@ __device__ __forceinline__ bool softmax_tile(const AttnItem &it, int klo, int kh
 // keys of one d (the 8 lanes of a store phase hit 8 distinct 16-byte bank
 // groups). The loads of the next chunk are issued before this chunk is
 // stored, so two chunks' loads are in flight.
+// At head width 32 (8 groups of d, 16 of keys: 128 blocks) each thread
+// moves one block: warp w takes d groups 4 (w & 1) .. + 3 and key groups
+// 8 (w >> 1) .. + 7.
+template <int DH> __device__ __forceinline__ int vt_group(int lane, int w) {
+    return DH == 64 ? (lane >> 3) + 4 * w : (lane >> 3) + 4 * (w & 1);
+}
+template <int DH> __device__ __forceinline__ int vt_keys(int lane, int w, int itr) {
+    return DH == 64 ? (lane & 7) + 8 * itr : (lane & 7) + 8 * (w >> 1);
+}
+template <int DH>
 __device__ __forceinline__ void load_v(const float *__restrict__ qkv, int64_t ld, int start, int k0, int khi, int col,
                                        int t, float4 (&v)[8]) {
     const int lane = t & 31, w = t >> 5;
-    const int g = (lane >> 3) + 4 * w;  // d columns 4 g .. 4 g + 3
+    const int g = vt_group<DH>(lane, w);  // d columns 4 g .. 4 g + 3
 #pragma unroll
-    for (int itr = 0; itr < 2; ++itr) {
-        const int kq = (lane & 7) + 8 * itr;  // keys 4 kq .. 4 kq + 3 of the chunk
+    for (int itr = 0; itr < DH / 32; ++itr) {
+        const int kq = vt_keys<DH>(lane, w, itr);  // keys 4 kq .. 4 kq + 3 of the chunk
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int k = k0 + 4 * kq + r;
@@ -262,12 +278,13 @@ __device__ __forceinline__ void load_v(const float *__restrict__ qkv, int64_t ld
         }
     }
 }
+template <int DH>
 __device__ __forceinline__ void store_vt(const float4 (&vv)[8], uint8_t *vth, uint8_t *vtl, int t) {
     const int lane = t & 31, w = t >> 5;
-    const int g = (lane >> 3) + 4 * w;
+    const int g = vt_group<DH>(lane, w);
 #pragma unroll
-    for (int itr = 0; itr < 2; ++itr) {
-        const int kq = (lane & 7) + 8 * itr;
+    for (int itr = 0; itr < DH / 32; ++itr) {
+        const int kq = vt_keys<DH>(lane, w, itr);
         const float4 *v = vv + 4 * itr;
         const int box = kq >> 3, c = kq & 7;
 #pragma unroll
@@ -283,6 +300,7 @@ __device__ __forceinline__ void store_vt(const float4 (&vv)[8], uint8_t *vth, ui
     }
 }
 
+template <int DH>
 __global__ void __launch_bounds__(320, 1)
 attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
                  const __grid_constant__ CUtensorMap tq_lo, const __grid_constant__ CUtensorMap tkv_lo,
@@ -352,7 +370,7 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             // has just read (in issue order) once K(y + 2) (and, for a
             // unit's first chunk, its Q) is in. Each S commits its buffer's
             // S barrier and frees its K buffer; a unit's last S frees Q.
-            const uint32_t ids = idesc_tf32(KT, false), idpv = idesc_tf32(D, false);
+            const uint32_t ids = idesc_tf32(KT, false), idpv = idesc_tf32(DH, false);
             const uint32_t aq = smem_u32(sQ), aql = aq + Q_BYTES, ab = smem_u32(sBuf);
             Cur sc{(int)blockIdx.x, 0, nch_of(blockIdx.x)}, pc = sc;
             uint32_t zs = 0, y = 0, qn = 0;  // S issued, P V issued, units begun
@@ -366,7 +384,7 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                 tc_fence_after();
                 const uint32_t kh = ab + b * BUF_BYTES, kl = kh + KV_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < D / 8; ++kk) {
+                for (int kk = 0; kk < DH / 8; ++kk) {
                     const uint32_t box = (uint32_t)(kk >> 2);
                     const uint64_t off = (uint64_t)((kk & 3) * 2);  // 32 bytes a K = 8 step, in 16-byte units
                     const uint64_t qh = smem_desc(aq + box * Q_BOX) + off, ql = smem_desc(aql + box * Q_BOX) + off;
@@ -420,12 +438,12 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                 const AttnItem it = items[c.u / heads];
                 int klo, khi;
                 key_range(it.len, it.q0, window, klo, khi);
-                const int col = (c.u % heads) * D;
+                const int col = (c.u % heads) * DH;
                 if (c.j == 0) {
                     if (qn >= 1 && !mbar_wait(bar_qf, (qn - 1) & 1, abort_flag, fault)) break;
-                    mbar_expect_tx(bar_q, 2 * Q_BYTES);
+                    mbar_expect_tx(bar_q, DH / 32 * 2 * Q_BOX);
 #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
+                    for (int hf = 0; hf < DH / 32; ++hf) {
                         tma_load_2d(aq + hf * Q_BOX, &tq, col + 32 * hf, it.start + it.q0, bar_q);
                         tma_load_2d(aql + hf * Q_BOX, &tq_lo, col + 32 * hf, it.start + it.q0, bar_q);
                     }
@@ -433,9 +451,9 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                 }
                 const uint32_t b = z & 1;
                 if (z >= 2 && !mbar_wait(bar_kf + 8 * b, ((z >> 1) & 1) ^ 1, abort_flag, fault)) break;
-                mbar_expect_tx(bar_k + 8 * b, 2 * KV_BYTES);
+                mbar_expect_tx(bar_k + 8 * b, DH / 32 * 2 * K_BOX);
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
+                for (int hf = 0; hf < DH / 32; ++hf) {
                     const int x = h + col + 32 * hf, yrow = it.start + klo + c.j * KT;
                     tma_load_2d(ab + b * BUF_BYTES + hf * K_BOX, &tkv, x, yrow, bar_k + 8 * b);
                     tma_load_2d(ab + b * BUF_BYTES + KV_BYTES + hf * K_BOX, &tkv_lo, x, yrow, bar_k + 8 * b);
@@ -454,7 +472,7 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             const AttnItem it = items[c.u / heads];
             int klo, khi;
             key_range(it.len, it.q0, window, klo, khi);
-            load_v(qkv, ld, it.start, klo + c.j * KT, khi, 2 * h + (c.u % heads) * D, t, v);
+            load_v<DH>(qkv, ld, it.start, klo + c.j * KT, khi, 2 * h + (c.u % heads) * DH, t, v);
         };
         Cur c{(int)blockIdx.x, 0, nch_of(blockIdx.x)};
         float4 cur[8];
@@ -467,7 +485,7 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             const uint32_t b = y & 1;
             if (y >= 2 && !mbar_wait(bar_vf + 8 * b, ((y >> 1) & 1) ^ 1, abort_flag, fault)) break;
             uint8_t *vth = sBuf + b * BUF_BYTES + 2 * KV_BYTES;
-            store_vt(cur, vth, vth + KV_BYTES, t);
+            store_vt<DH>(cur, vth, vth + KV_BYTES, t);
             fence_async_smem();  // written by threads, read by the tensor core
             mbar_arrive(bar_v + 8 * b);
 #pragma unroll
@@ -482,8 +500,8 @@ attn_tf32_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             const AttnItem it = items[u / heads];
             int klo, khi;
             key_range(it.len, it.q0, window, klo, khi);
-            if (!softmax_tile(it, klo, khi, window, u % heads, ctx, h, live, lane_base, r, bar_s, bar_p, bar_o, g,
-                              abort_flag, fault))
+            if (!softmax_tile<DH>(it, klo, khi, window, u % heads, ctx, h, live, lane_base, r, bar_s, bar_p, bar_o, g,
+                                  abort_flag, fault))
                 break;
         }
     }
@@ -523,6 +541,8 @@ cudaError_t make_map(const float *ptr, uint64_t rows, uint64_t cols, uint32_t bo
 
 }  // namespace
 
+bool attention_tf32_takes(int head_dim) { return head_dim == 64 || head_dim == 32; }
+
 cudaError_t make_attn_maps_f32(const float *qkv, uint64_t rows, int hidden, AttnMapsF32 *out) {
     cudaError_t e = make_map(qkv, rows, (uint64_t)3 * hidden, QT, &out->q);
     if (e == cudaSuccess) e = make_map(qkv, rows, (uint64_t)3 * hidden, KT, &out->kv);
@@ -534,16 +554,17 @@ cudaError_t attention_tf32(const AttnMapsF32 &hi, const AttnMapsF32 &lo, const f
                            const AttnItem *items, int n_items, int heads, int head_dim, int hidden, int window,
                            int *fault, cudaStream_t s) {
     if (n_items == 0) return cudaSuccess;
-    if (head_dim != D || hidden % 4 != 0) return cudaErrorNotSupported;  // TMA x: 16-byte multiples
-    cudaError_t e = cudaFuncSetAttribute(attn_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (!attention_tf32_takes(head_dim) || hidden % 4 != 0) return cudaErrorNotSupported;  // TMA x: 16-byte multiples
+    auto kern = head_dim == 64 ? attn_tf32_kernel<64> : attn_tf32_kernel<32>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int units = n_items * heads;
     const int grid = units < sms ? units : sms;
-    return launch_pdl(attn_tf32_kernel, grid, 320, SMEM, s, hi.q, hi.kv, lo.q, lo.kv, qkv, ctx, tok_live, items,
-                      n_items, heads, hidden, window, fault);
+    return launch_pdl(kern, grid, 320, SMEM, s, hi.q, hi.kv, lo.q, lo.kv, qkv, ctx, tok_live, items, n_items, heads,
+                      hidden, window, fault);
 }
 
 }  // namespace tb

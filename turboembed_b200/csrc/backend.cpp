@@ -218,7 +218,7 @@ struct Session {
     // residual GEMM into it: the GEMM writes x and xn = LN(x) (same switch).
     bool fuse_ln_pre = false;
     bool exact_tf32 = false;  // F32 sessions: GEMMs on kind::tf32 x3 (else FFMA)
-    // F32 sessions of head width 64 without rotary positions: the QKV GEMM
+    // F32 sessions of head width 64 or 32 without rotary positions: the QKV GEMM
     // (kind::tf32) also writes qkv's lo halves into qkv_lo, and attention
     // runs on kind::tf32 x3 (attention_tf32) through these maps.
     bool tf32_attn = false;
@@ -949,8 +949,8 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         s->exact_tf32 = (allowed & TURBO_NUMERIC_TF32) && !(v && v[0] == '0');
         const char *va = getenv("TB_EXACT_TF32_ATTN");
         Epilogue store;
-        s->tf32_attn = s->exact_tf32 && !(va && va[0] == '0') && !m->modern && m->hidden / m->heads == 64 &&
-                       gemm_tf32_takes(3 * m->hidden, m->hidden, store);
+        s->tf32_attn = s->exact_tf32 && !(va && va[0] == '0') && !m->modern &&
+                       attention_tf32_takes(m->hidden / m->heads) && gemm_tf32_takes(3 * m->hidden, m->hidden, store);
     }
     const int qt = attention_queries(s.get());
     s->max_attn_items = (int)(cap / qt) + s->max_batch + 1;

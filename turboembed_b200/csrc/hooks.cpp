@@ -316,8 +316,8 @@ extern "C" TB_EXPORT int32_t turbo_b200_attention_check(uint32_t dtype, uint32_t
     const int h = (int)(heads * head_dim);
     std::vector<AttnItem> items;
     int T = 0, max_len = 0;
-    if (variant == 4 && (dt != Dt::F32 || head_dim != 64))
-        return hook_fail(err, TURBO_E_UNSUPPORTED, "variant 4 takes F32 at head width 64", cudaSuccess);
+    if (variant == 4 && (dt != Dt::F32 || !attention_tf32_takes((int)head_dim)))
+        return hook_fail(err, TURBO_E_UNSUPPORTED, "variant 4 takes F32 at head width 64 or 32", cudaSuccess);
     if ((variant == 5 || variant == 6) && (dt == Dt::F32 || !attention_fa_takes((int)head_dim, variant == 6)))
         return hook_fail(err, TURBO_E_UNSUPPORTED, "variant 5 takes F16 or BF16 at head width 64 or 32, 6 at 64",
                          cudaSuccess);

@@ -172,6 +172,7 @@ struct AttnMapsF32 {
     CUtensorMap q, kv;
 };
 cudaError_t make_attn_maps_f32(const float *qkv, uint64_t rows, int hidden, AttnMapsF32 *out);
+bool attention_tf32_takes(int head_dim);  // head widths 64 and 32
 cudaError_t attention_tf32(const AttnMapsF32 &hi, const AttnMapsF32 &lo, const float *qkv, float *ctx,
                            const uint8_t *tok_live,
                            const AttnItem *items, int n_items, int heads, int head_dim, int hidden, int window,
