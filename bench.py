@@ -302,7 +302,9 @@ def cpu_baseline(wl, desc):
     return {"value": float(np.sum(lens) / dt), "unit": "tokens/s", "cores": cores, "kind": "port",
             "cpu": cpu_model(),
             "sample": f"{len(lens)} rows of the {wl.key} distribution ({int(np.sum(lens))} live tokens), F32, "
-                      f"all {wl.layers} layers, weights prepared before the timed pass, {dt:.1f} s"}, rows, out
+                      f"all {wl.layers} layers, varlen-packed as the reference CPU encoder packs them (not padded to "
+                      f"the session's {wl.seq}: padding would only slow the CPU), weights prepared before the timed "
+                      f"pass, {dt:.1f} s"}, rows, out
 
 
 def parity(wl, sess, rows, want):

@@ -68,6 +68,94 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(T *__restrict__ x, Packed
     }
 }
 
+// The same with 16-byte loads: lane l holds columns 4 (l + 32 i) .. + 3 of
+// the three table rows (CPL float4 chunks a lane), two tokens a warp in
+// flight. Sums as the LayerNorm kernels take them: F64 at F32 (the EXACT
+// tier, the reference's LayerNorm sums, rowwise.rs:10-29), two-pass F32 at
+// F16/BF16 (the reference's FASTEST embedding kernel sums in F32,
+// core/cuda/kernels.cu:394-429).
+template <class T, int CPL>
+__global__ void __launch_bounds__(256) embed_ln_vec_kernel(T *__restrict__ x, Packed p, const float *__restrict__ word,
+                                                           const float *__restrict__ pos, const float *__restrict__ type,
+                                                           int pos_offset, const float *__restrict__ ln_w,
+                                                           const float *__restrict__ ln_b, int h, double eps) {
+    using Acc = typename std::conditional<sizeof(T) == 4, double, float>::type;
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    const int q = h >> 2;  // float4 chunks a row
+    for (int t0 = 2 * ((blockIdx.x * blockDim.x + threadIdx.x) >> 5); t0 < p.tokens; t0 += 2 * warps) {
+        float4 v[2][CPL];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int t = t0 + k < p.tokens ? t0 + k : t0;
+            const float4 *wr = reinterpret_cast<const float4 *>(word + (int64_t)p.tok_id[t] * h);
+            const float4 *pr = pos ? reinterpret_cast<const float4 *>(pos + (int64_t)(p.tok_pos[t] + pos_offset) * h) : nullptr;
+            const float4 *tr =
+                type ? reinterpret_cast<const float4 *>(type + (int64_t)(p.tok_type ? p.tok_type[t] : 0) * h) : nullptr;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                const int c = lane + 32 * i;
+                float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (c < q) {
+                    a = wr[c];
+                    if (pr) {
+                        const float4 b = pr[c];
+                        a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+                    }
+                    if (tr) {
+                        const float4 b = tr[c];
+                        a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+                    }
+                }
+                v[k][i] = a;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int t = t0 + k;
+            if (t >= p.tokens) break;
+            Acc s = 0;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i)
+                s += ((Acc)v[k][i].x + (Acc)v[k][i].y) + ((Acc)v[k][i].z + (Acc)v[k][i].w);
+            const Acc mean = warp_sum(s) / (Acc)h;
+            Acc ss = 0;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                if (lane + 32 * i < q) {
+                    const Acc a = (Acc)v[k][i].x - mean, b = (Acc)v[k][i].y - mean, c = (Acc)v[k][i].z - mean,
+                              d = (Acc)v[k][i].w - mean;
+                    ss += (a * a + b * b) + (c * c + d * d);
+                }
+            }
+            const Acc inv = (Acc)1 / sqrt(warp_sum(ss) / (Acc)h + (Acc)(float)eps);
+            T *out = x + (int64_t)t * h;
+            const float4 *w4 = reinterpret_cast<const float4 *>(ln_w), *b4 = reinterpret_cast<const float4 *>(ln_b);
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                const int c = lane + 32 * i;
+                if (c < q) {
+                    const float4 w = w4[c], b = ln_b ? b4[c] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    const float z[4] = {(float)(((Acc)v[k][i].x - mean) * inv) * w.x + b.x,
+                                        (float)(((Acc)v[k][i].y - mean) * inv) * w.y + b.y,
+                                        (float)(((Acc)v[k][i].z - mean) * inv) * w.z + b.z,
+                                        (float)(((Acc)v[k][i].w - mean) * inv) * w.w + b.w};
+                    if constexpr (sizeof(T) == 4) {
+                        reinterpret_cast<float4 *>(out)[c] = make_float4(z[0], z[1], z[2], z[3]);
+                    } else {
+                        uint2 u;
+                        u.x = pack2<T>(z[0], z[1]);
+                        u.y = pack2<T>(z[2], z[3]);
+                        reinterpret_cast<uint2 *>(out)[c] = u;
+                    }
+                }
+            }
+        }
+    }
+}
+
 // 16 bytes of T as floats: 8 halves/bf16s or 4 floats.
 template <class T> struct Vec {
     static constexpr int N = 16 / sizeof(T);
@@ -494,6 +582,29 @@ cudaError_t embed_layer_norm(Dt dt, void *x, const Packed &p, const float *word,
     if (hidden > 32 * MAXV) return cudaErrorInvalidValue;
     if (p.tokens == 0) return cudaSuccess;
     int g = grid_for(p.tokens);
+    // 16-byte rows (hidden a multiple of 4, tables 16-byte aligned): the
+    // vectorised kernel, sized by float4 chunks a lane.
+    const bool aligned = ((uintptr_t)word | (uintptr_t)pos | (uintptr_t)type | (uintptr_t)ln_w | (uintptr_t)ln_b |
+                          (uintptr_t)x) % 16 == 0;
+    if (hidden % 4 == 0 && aligned) {
+        const int cpl = (hidden / 4 + 31) / 32;
+        g = grid_for((p.tokens + 1) / 2);  // two tokens a warp
+        auto go = [&](auto tag) -> cudaError_t {
+            using T = decltype(tag);
+            T *out = (T *)x;
+            switch (cpl) {
+            case 1: return launch_pdl(embed_ln_vec_kernel<T, 1>, g, 256, 0, s, out, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+            case 2: return launch_pdl(embed_ln_vec_kernel<T, 2>, g, 256, 0, s, out, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+            case 3: return launch_pdl(embed_ln_vec_kernel<T, 3>, g, 256, 0, s, out, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+            case 4: return launch_pdl(embed_ln_vec_kernel<T, 4>, g, 256, 0, s, out, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+            case 6: return launch_pdl(embed_ln_vec_kernel<T, 6>, g, 256, 0, s, out, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+            case 8: return launch_pdl(embed_ln_vec_kernel<T, 8>, g, 256, 0, s, out, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
+            default: return cudaErrorNotSupported;
+            }
+        };
+        cudaError_t e = dt == Dt::F32 ? go(float()) : dt == Dt::F16 ? go(__half()) : go(__nv_bfloat16());
+        if (e != cudaErrorNotSupported) return e;
+    }
     switch (dt) {
     case Dt::F32: return launch_pdl(embed_ln_kernel<float>, g, 256, 0, s, (float *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
     case Dt::F16: return launch_pdl(embed_ln_kernel<__half>, g, 256, 0, s, (__half *)x, p, word, pos, type, pos_offset, ln_w, ln_b, hidden, eps);
