@@ -217,6 +217,12 @@ struct Session {
     // Pre-norm layers (ModernBERT) fold the LayerNorm that follows each
     // residual GEMM into it: the GEMM writes x and xn = LN(x) (same switch).
     bool fuse_ln_pre = false;
+    // The fused LayerNorm's grid form: each row's partial statistics
+    // [rows rounded to 256][6] float2, and per fused launch of a run a
+    // counter a 32-row group ([2 layers][ln_stride] u32, zeroed at each run).
+    float2 *ln_stats = nullptr;
+    uint32_t *ln_count = nullptr;
+    int ln_stride = 0, ln_launches = 0, ln_next = 0;
     bool exact_tf32 = false;  // F32 sessions: GEMMs on kind::tf32 x3 (else FFMA)
     // F32 sessions of head width 64 or 32 without rotary positions: the QKV GEMM
     // (kind::tf32) also writes qkv's lo halves into qkv_lo, and attention
@@ -245,7 +251,7 @@ struct Session {
     ~Session() {
         DeviceScope ds(ctx->device);
         for (void *p : {x, xn, qkv, qkv_lo, ctxb, ffn, (void *)plan_dev, (void *)head_wt, (void *)head_bp, (void *)head_wc,
-                        (void *)head_scores, (void *)pack_dev})
+                        (void *)head_scores, (void *)pack_dev, (void *)ln_stats, (void *)ln_count})
             cudaFree(p);
         if (plan_host) cudaFreeHost(plan_host);
         if (pack_counts) cudaFreeHost(pack_counts);
@@ -976,6 +982,13 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
     if (e == cudaSuccess && s->tf32_attn) e = alloc(&s->qkv_lo, rows * 3 * h * 4);
     if (e == cudaSuccess) e = alloc(&s->ctxb, rows * h * es);
     if (e == cudaSuccess) e = alloc(&s->ffn, rows * I * es);
+    if (e == cudaSuccess && (s->fuse_ln || s->fuse_ln_pre)) {
+        const size_t padded = (rows + 255) / 256 * 256;
+        s->ln_stride = (int)(padded / 32);
+        s->ln_launches = 2 * m->layers;
+        e = alloc((void **)&s->ln_stats, padded * 6 * sizeof(float2));
+        if (e == cudaSuccess) e = alloc((void **)&s->ln_count, (size_t)s->ln_launches * s->ln_stride * sizeof(uint32_t));
+    }
     if (e == cudaSuccess) e = alloc((void **)&s->plan_dev, s->lay.total);
     if (e == cudaSuccess) e = cudaHostAlloc((void **)&s->plan_host, s->lay.total, cudaHostAllocDefault);
     if (e == cudaSuccess) e = alloc((void **)&s->pack_dev, (6 * (size_t)s->max_batch + 8) * sizeof(int32_t));
@@ -1309,7 +1322,13 @@ cudaError_t linear_launch(Session *s, const CUtensorMap *amap, const void *a, co
 // Epilogue::out2's (pre-norm fused LayerNorm).
 cudaError_t linear(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi, int M,
                    const CUtensorMap *out_map = nullptr, const CUtensorMap *out2_map = nullptr) {
-    return timed(s, 0, 2.0 * M * L.n * L.k, [&] { return linear_launch(s, amap, a, L, epi, M, out_map, out2_map); });
+    Epilogue e2 = epi;
+    if (epi.kind == EPI_RESIDUAL_LN && s->ln_stats && s->ln_next < s->ln_launches) {
+        // The grid form of the fused LayerNorm: this launch's counters.
+        e2.ln_stats = s->ln_stats;
+        e2.ln_count = s->ln_count + (size_t)s->ln_next++ * s->ln_stride;
+    }
+    return timed(s, 0, 2.0 * M * L.n * L.k, [&] { return linear_launch(s, amap, a, L, e2, M, out_map, out2_map); });
 }
 
 // Block k of a tapped range write: the ranges pooled from layer l's states
@@ -1481,7 +1500,11 @@ int32_t tb_session_run(void *p, turbo_backend_run *out, turbo_error *err) {
     *c->fault = 0;
     s->prof_n = 0;
     cudaEventRecord(s->run0, c->stream);
-    cudaError_t e = encode(s);
+    cudaError_t e = cudaSuccess;
+    s->ln_next = 0;
+    if (s->ln_count)  // the fused LayerNorm's arrival counters start at zero every run
+        e = cudaMemsetAsync(s->ln_count, 0, (size_t)s->ln_launches * s->ln_stride * sizeof(uint32_t), c->stream);
+    if (e == cudaSuccess) e = encode(s);
     if (e == cudaSuccess)
         e = pool_vectors(s->dt, s->x, s->plan_dev + s->lay.tok_live, (const PoolItem *)(s->plan_dev + s->lay.pool),
                          s->n_vectors, s->m->hidden, (int)s->output_dim, s->normalize == TURBO_NORMALIZE_L2,

@@ -378,7 +378,31 @@ struct LnStep {
     bool arm;                // this lane arms the quarter's barrier for this tile (one lane a quarter)
 };
 
-template <class T, int COLS, int LNS, int PARTS, bool RS, class Release>
+// Wait until the counter at c reaches target (an acquire at GPU scope), at
+// most WAIT_NS, or until another role gave up. For the grid form of the
+// fused LayerNorm: the pairs holding a row's other column slices arrive
+// there once their parts of the row's statistics are written.
+__device__ __forceinline__ bool wait_count(const uint32_t *c, uint32_t target, volatile int *abort_flag, int *fault) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+        if (v >= target) return true;
+        if ((i & 63) == 0) {
+            if (*abort_flag) return false;
+            const uint64_t t = globaltimer();
+            if (i == 0) t0 = t;
+            else if (t - t0 > WAIT_NS) {
+                *abort_flag = 1;
+                atomicExch(fault, 1);
+                return false;
+            }
+        }
+        __nanosleep(64);
+    }
+}
+
+template <class T, int COLS, int LNS, int PARTS, bool RS, bool LG, class Release>
 __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float *bias_s, uint32_t tbase, int row,
                                                  bool row_ok, int col_base, const uint4 *res, StoreStage &ss,
                                                  const CUtensorMap *out_map, const CUtensorMap *out2_map,
@@ -453,28 +477,58 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
     }
     const float mean_p = k + s1 / (float)COLS;
     const float m2 = fmaxf(s2 - s1 * (s1 / (float)COLS), 0.0f);
-    // This row's part to the LNS CTAs holding the row: asynchronous stores
-    // that complete their bytes on the receiver's barrier, which one lane a
-    // quarter arms with all PARTS x 32 rows' bytes.
-    const uint32_t mine = L.stats + (uint32_t)((L.slot * 32 + lane) * 8);
+    float2 parts[PARTS];
+    if constexpr (LG) {
+        // Grid form: this row's part into the statistics buffer (L2), a
+        // fence, one arrival a warp on the 32-row group's counter; once all
+        // PARTS warps holding these rows (every column slice's pair) have
+        // arrived, the parts are read back from L2.
+        float2 *st = e.ln_stats + (int64_t)(ss.row0 + lane) * PARTS;
+        __stcg(st + L.slot, make_float2(mean_p, m2));
+        __threadfence();
+        __syncwarp();
+        uint32_t *cnt = e.ln_count + (ss.row0 >> 5);
+        bool ok = true;
+        if (lane == 0) {
+            __threadfence();  // every lane's part, seen through the warp barrier, before the arrival
+            atomicAdd(cnt, 1u);
+            ok = wait_count(cnt, PARTS, abort_flag, fault);
+        }
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+            release();
+            return false;
+        }
+        uint32_t seen;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(cnt) : "memory");
+        (void)seen;
 #pragma unroll
-    for (int j = 0; j < LNS; ++j) st_async_v2(mapa(mine, L.half + 2 * j), mean_p, m2, mapa(L.bar, L.half + 2 * j));
-    if (L.arm) mbar_expect_tx(L.bar, (uint32_t)(PARTS * 32 * 8));
-    if (!mbar_wait_cluster(L.bar, L.phase, abort_flag, fault)) {
-        release();
-        return false;
+        for (int p = 0; p < PARTS; ++p) parts[p] = __ldcg(st + p);
+    } else {
+        // Cluster form: this row's part to the LNS CTAs holding the row:
+        // asynchronous stores that complete their bytes on the receiver's
+        // barrier, which one lane a quarter arms with all PARTS x 32 rows'
+        // bytes.
+        const uint32_t mine = L.stats + (uint32_t)((L.slot * 32 + lane) * 8);
+#pragma unroll
+        for (int j = 0; j < LNS; ++j) st_async_v2(mapa(mine, L.half + 2 * j), mean_p, m2, mapa(L.bar, L.half + 2 * j));
+        if (L.arm) mbar_expect_tx(L.bar, (uint32_t)(PARTS * 32 * 8));
+        if (!mbar_wait_cluster(L.bar, L.phase, abort_flag, fault)) {
+            release();
+            return false;
+        }
+#pragma unroll
+        for (int p = 0; p < PARTS; ++p) parts[p] = L.stats_p[p * 32 + lane];
     }
     // Chan: mean = the PARTS parts' mean (equal counts), M2 = sum M2_p + COLS sum (mean_p - mean)^2.
     float ms = 0.0f;
 #pragma unroll
-    for (int p = 0; p < PARTS; ++p) ms += L.stats_p[p * 32 + lane].x;
+    for (int p = 0; p < PARTS; ++p) ms += parts[p].x;
     const float mean = ms / (float)PARTS;
     float M2 = 0.0f;
 #pragma unroll
     for (int p = 0; p < PARTS; ++p) {
-        const float2 q = L.stats_p[p * 32 + lane];
-        const float d = q.x - mean;
-        M2 += q.y + (float)COLS * d * d;
+        const float d = parts[p].x - mean;
+        M2 += parts[p].y + (float)COLS * d * d;
     }
     const float inv = 1.0f / sqrtf(M2 / (float)(PARTS * COLS) + e.ln_eps);
     // Pass 2: normalise and store, 64 columns a step.
@@ -550,7 +604,7 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
 // and 2 j + 1 the pair of column slice j, loops over 256-row blocks; every
 // pair takes the same block, so each row's statistics meet within the
 // cluster (epilogue_ln_tile).
-template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false>
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false, bool LG = false>
 __global__ void __launch_bounds__(128 + 128 * EPI_WG, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
                const __grid_constant__ CUtensorMap tout, const __grid_constant__ CUtensorMap tout2, int use_tma_store,
@@ -583,7 +637,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     const uint32_t rank = PAIR ? cluster_rank() : 0;
     const uint32_t pr = rank & 1u, lead = rank & ~1u;  // this CTA's half of its pair; the pair's leader
     const bool leader = pr == 0;
-    constexpr int CL = LNS ? 2 * LNS : (PAIR ? 2 : 1);  // CTAs a cluster (1: no cluster)
+    static_assert(!LG || LNS > 0, "the grid form is a form of the fused LayerNorm");
+    constexpr int CL = LG ? 2 : (LNS ? 2 * LNS : (PAIR ? 2 : 1));  // CTAs a cluster (1: no cluster)
     const int unit = (int)(blockIdx.x / CL);
     const int units = (int)(gridDim.x / CL);
     if (threadIdx.x == 0) {
@@ -625,9 +680,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     const int kblocks = (K + BK - 1) / BK;
     // Tile t's row block and column block: with LNS the cluster's pairs all
     // take row block t, pair j column slice j.
-    const int tiles = LNS ? m_tiles : m_tiles * n_tiles;
-    auto tile_m = [&](int t) { return LNS ? t : t / n_tiles; };
-    auto tile_n = [&](int t) { return LNS ? (int)(rank >> 1) : t % n_tiles; };
+    // Grid form (LG): tile t = row block t / LNS, slice t % LNS; the pairs
+    // come in groups of LNS (units a multiple of LNS), so a group's pairs
+    // take the slices of the same row blocks at the same time.
+    const int tiles = LG ? m_tiles * LNS : (LNS ? m_tiles : m_tiles * n_tiles);
+    auto tile_m = [&](int t) { return LG ? t / LNS : (LNS ? t : t / n_tiles); };
+    auto tile_n = [&](int t) { return LG ? t % LNS : (LNS ? (int)(rank >> 1) : t % n_tiles); };
 
     if (warp == 0) {
         if (lane == 0) {
@@ -777,8 +835,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
             if constexpr (LNS > 0) {
                 const uint32_t qb = (it & 1) * 4 + quad;  // this tile's buffer, this quarter
                 LnStep L{lnw_s, lnb_s, stats0 + qb * (C::PARTS * 32 * 8), stats_s + qb * (C::PARTS * 32),
-                         sbar0 + 8 * qb, (it >> 1) & 1, pr, (int)(rank >> 1) * EPI_WG + part, lane == 0 && part == 0};
-                if (!epilogue_ln_tile<T, COLS, LNS, C::PARTS, RS>(e, bias_s, tbase, row, row_ok, col_base, res, ss,
+                         sbar0 + 8 * qb, (it >> 1) & 1, pr, tile_n(tile) * EPI_WG + part, lane == 0 && part == 0};
+                if (!epilogue_ln_tile<T, COLS, LNS, C::PARTS, RS, LG>(e, bias_s, tbase, row, row_ok, col_base, res, ss,
                                                                   &tout, &tout2, L, abort_flag, fault, release))
                     break;
                 if constexpr (RS)
@@ -857,18 +915,51 @@ template <class T, int LNS, bool RS = false> int ln_clusters() {
     return n;
 }
 
-template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false>
+// The CTA pairs of the grid form that fit the device at once.
+template <class T, int LNS, bool RS = false> int ln_pairs() {
+    static const int n = [] {
+        using C = Cfg<256, true, LNS, LN_EPI_WG, RS>;
+        auto kern = gemm_tc_kernel<T, 256, LN_EPI_WG, true, LNS, -1, RS, true>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) return 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(128 + 128 * LN_EPI_WG);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return clusters;
+    }();
+    return n;
+}
+
+template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false, bool LG = false>
 cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     using C = Cfg<BN, PAIR, LNS, EPI_WG, RS>;
-    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS, KIND, RS>;
+    auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS, KIND, RS, LG>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (err != cudaSuccess) return err;
     const int TM = PAIR ? 2 * BM : BM;
-    constexpr int CL = LNS ? 2 * LNS : (PAIR ? 2 : 1);
-    const int tiles = LNS ? (M + TM - 1) / TM : ((M + TM - 1) / TM) * ((N + BN - 1) / BN);
-    const int units = LNS ? ln_clusters<T, LNS, RS>() : sms / CL;
+    constexpr int CL = LG ? 2 : (LNS ? 2 * LNS : (PAIR ? 2 : 1));
+    const int m_tiles = (M + TM - 1) / TM;
+    const int tiles = LG ? m_tiles * LNS : (LNS ? m_tiles : m_tiles * ((N + BN - 1) / BN));
+    // Grid form: every pair resident at once (they wait on one another's
+    // statistics), in whole groups of LNS.
+    int units;
+    if constexpr (LG) units = ln_pairs<T, LNS, RS>() / LNS * LNS;
+    else if constexpr (LNS > 0) units = ln_clusters<T, LNS, RS>();
+    else units = sms / CL;
     if (units <= 0) return cudaErrorNotSupported;
-    const int grid_units = tiles < units ? tiles : units;
+    const int grid_units = LG ? (m_tiles * LNS < units ? m_tiles * LNS : units) : (tiles < units ? tiles : units);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(CL * grid_units);
     cfg.blockDim = dim3(128 + 128 * EPI_WG);
@@ -894,6 +985,13 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     if (e.kind == EPI_RESIDUAL_LN) {
+        // With the statistics buffer: the grid form (pairs anywhere, groups
+        // of three), else clusters of three pairs.
+        if (N == 768 && e.ln_stats && e.ln_count) {
+            if (K <= LN_STAGED_MAX_K && maps.has_out)
+                return launch<T, 256, LN_EPI_WG, true, 3, -1, true, true>(maps, M, N, K, e, sms, fault, s);
+            return launch<T, 256, LN_EPI_WG, true, 3, -1, false, true>(maps, M, N, K, e, sms, fault, s);
+        }
         // Short mainloops (K up to 1280: attention-out, and the gated
         // models' FFN-out) are bound by the epilogue: they take the staged
         // residual rows and 4 stages.

@@ -43,6 +43,13 @@ struct Epilogue {
     // product's input), row stride ldo2.
     void *out2 = nullptr;
     int64_t ldo2 = 0;
+    // EPI_RESIDUAL_LN on CTA pairs across the grid (no clusters of slices):
+    // each row's partial statistics go through ln_stats [rows][parts]
+    // (float2 mean and M2, rows rounded up to the 256-row blocks) and one
+    // arrival a warp on its 32-row group's counter in ln_count [rows / 32],
+    // which must be zero at launch. Null: the cluster form.
+    float2 *ln_stats = nullptr;
+    uint32_t *ln_count = nullptr;
     // EPI_STORE of the EXACT tier's tf32 GEMM: also x - hi(x) of each output
     // (hi = x with the low 13 mantissa bits cleared), same index and stride:
     // the lo halves attention_tf32 reads.
