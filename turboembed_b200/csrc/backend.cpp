@@ -218,7 +218,7 @@ struct Session {
     // residual GEMM into it: the GEMM writes x and xn = LN(x) (same switch).
     bool fuse_ln_pre = false;
     // The fused LayerNorm's grid form: each row's partial statistics
-    // [rows rounded to 256][6] float2, and per fused launch of a run a
+    // [rows rounded to 256][hidden / 128] float2, and per fused launch of a run a
     // counter a 32-row group ([2 layers][ln_stride] u32, zeroed at each run).
     float2 *ln_stats = nullptr;
     uint32_t *ln_count = nullptr;
@@ -986,7 +986,7 @@ int32_t open_session(Model *m, uint32_t task, uint32_t max_batch, uint32_t max_s
         const size_t padded = (rows + 255) / 256 * 256;
         s->ln_stride = (int)(padded / 32);
         s->ln_launches = 2 * m->layers;
-        e = alloc((void **)&s->ln_stats, padded * 6 * sizeof(float2));
+        e = alloc((void **)&s->ln_stats, padded * (m->hidden / 128) * sizeof(float2));  // parts: 128 columns each
         if (e == cudaSuccess) e = alloc((void **)&s->ln_count, (size_t)s->ln_launches * s->ln_stride * sizeof(uint32_t));
     }
     if (e == cudaSuccess) e = alloc((void **)&s->plan_dev, s->lay.total);

@@ -992,6 +992,11 @@ cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e,
                 return launch<T, 256, LN_EPI_WG, true, 3, -1, true, true>(maps, M, N, K, e, sms, fault, s);
             return launch<T, 256, LN_EPI_WG, true, 3, -1, false, true>(maps, M, N, K, e, sms, fault, s);
         }
+        if (N == 1024 && e.ln_stats && e.ln_count && !e.out2) {
+            if (K <= LN_STAGED_MAX_K && maps.has_out)
+                return launch<T, 256, LN_EPI_WG, true, 4, -1, true, true>(maps, M, N, K, e, sms, fault, s);
+            return launch<T, 256, LN_EPI_WG, true, 4, -1, false, true>(maps, M, N, K, e, sms, fault, s);
+        }
         // Short mainloops (K up to 1280: attention-out, and the gated
         // models' FFN-out) are bound by the epilogue: they take the staged
         // residual rows and 4 stages.
@@ -1054,11 +1059,16 @@ cudaError_t make_store_map(Dt dt, const void *ptr, uint64_t rows, uint64_t cols,
 bool gemm_ln_dual_takes(int n, int k) { return n == 768 && k <= LN_STAGED_MAX_K; }
 
 bool gemm_ln_fusable(Dt dt, int n) {
-    // 1024-column rows take clusters of 8, of which too few fit the GPCs:
-    // measured slower than the separate LayerNorm, so only 768 is fused.
-    if (n != 768) return false;
-    if (dt == Dt::F16) return ln_clusters<__half, 3>() > 0 && ln_clusters<__half, 3, true>() > 0;
-    if (dt == Dt::BF16) return ln_clusters<__nv_bfloat16, 3>() > 0 && ln_clusters<__nv_bfloat16, 3, true>() > 0;
+    // Post-LN rows of 768 or 1024 columns: the grid form (groups of three
+    // or four CTA pairs exchanging row statistics through L2) fits any
+    // device with at least one group of pairs.
+    if (n != 768 && n != 1024) return false;
+    if (dt == Dt::F16)
+        return n == 768 ? ln_pairs<__half, 3>() >= 3 && ln_pairs<__half, 3, true>() >= 3
+                        : ln_pairs<__half, 4>() >= 4 && ln_pairs<__half, 4, true>() >= 4;
+    if (dt == Dt::BF16)
+        return n == 768 ? ln_pairs<__nv_bfloat16, 3>() >= 3 && ln_pairs<__nv_bfloat16, 3, true>() >= 3
+                        : ln_pairs<__nv_bfloat16, 4>() >= 4 && ln_pairs<__nv_bfloat16, 4, true>() >= 4;
     return false;
 }
 

@@ -212,10 +212,10 @@ int32_t gemm_ln_run(uint32_t dtype, uint32_t M, uint32_t N, uint32_t K, const fl
     ep.ln_w = dlw;
     ep.ln_b = dlb;
     ep.ln_eps = eps;
-    if (N == 768) {
+    if (N == 768 || (N == 1024 && !ln_out)) {
         // The grid form, as sessions run it: statistics and zeroed counters.
         const size_t padded = ((size_t)M + 255) / 256 * 256;
-        ep.ln_stats = (float2 *)dv.get(padded * 6 * sizeof(float2));
+        ep.ln_stats = (float2 *)dv.get(padded * (N / 128) * sizeof(float2));
         ep.ln_count = (uint32_t *)dv.get(padded / 32 * sizeof(uint32_t));
         if (!ep.ln_stats || !ep.ln_count) return hook_fail(err, TURBO_E_RUNTIME, "gemm_ln_check setup", cudaErrorMemoryAllocation);
     }

@@ -44,7 +44,7 @@ struct Epilogue {
     void *out2 = nullptr;
     int64_t ldo2 = 0;
     // EPI_RESIDUAL_LN on CTA pairs across the grid (no clusters of slices):
-    // each row's partial statistics go through ln_stats [rows][parts]
+    // each row's partial statistics go through ln_stats [rows][N / 128]
     // (float2 mean and M2, rows rounded up to the 256-row blocks) and one
     // arrival a warp on its 32-row group's counter in ln_count [rows / 32],
     // which must be zero at launch. Null: the cluster form.
