@@ -1323,7 +1323,13 @@ cudaError_t linear_launch(Session *s, const CUtensorMap *amap, const void *a, co
 cudaError_t linear(Session *s, const CUtensorMap *amap, const void *a, const Linear &L, const Epilogue &epi, int M,
                    const CUtensorMap *out_map = nullptr, const CUtensorMap *out2_map = nullptr) {
     Epilogue e2 = epi;
-    if (epi.kind == EPI_RESIDUAL_LN && s->ln_stats && s->ln_next < s->ln_launches) {
+    // The grid form unless the environment sets TB_LNGRID=0 (an A/B switch
+    // back to clusters of slices, read once).
+    static const bool grid = [] {
+        const char *v = getenv("TB_LNGRID");
+        return !(v && v[0] == '0');
+    }();
+    if (grid && epi.kind == EPI_RESIDUAL_LN && s->ln_stats && s->ln_next < s->ln_launches) {
         // The grid form of the fused LayerNorm: this launch's counters.
         e2.ln_stats = s->ln_stats;
         e2.ln_count = s->ln_count + (size_t)s->ln_next++ * s->ln_stride;
@@ -1401,9 +1407,10 @@ cudaError_t encode(Session *s) {
             if ((e = attention(-1)) != cudaSuccess) return e;
             Epilogue o;
             o.kind = EPI_RESIDUAL, o.bias = L.out.bias, o.out = s->x, o.ldo = h;
-            if (s->fuse_ln) o.kind = EPI_RESIDUAL_LN, o.ln_w = L.ln1_w, o.ln_b = L.ln1_b, o.ln_eps = (float)m->eps;
+            const bool fuse_out = s->fuse_ln;
+            if (fuse_out) o.kind = EPI_RESIDUAL_LN, o.ln_w = L.ln1_w, o.ln_b = L.ln1_b, o.ln_eps = (float)m->eps;
             if ((e = linear(s, &s->map_ctx, s->ctxb, L.out, o, T, &s->out_x)) != cudaSuccess) return e;
-            if (!s->fuse_ln &&
+            if (!fuse_out &&
                 (e = timed(s, 2, 0.0, [&] { return layer_norm(dt, s->x, s->x, L.ln1_w, L.ln1_b, T, h, m->eps, st); })) !=
                     cudaSuccess)
                 return e;

@@ -985,13 +985,14 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     if (e.kind == EPI_RESIDUAL_LN) {
-        // With the statistics buffer: the grid form (pairs anywhere, groups
-        // of three), else clusters of three pairs.
-        if (N == 768 && e.ln_stats && e.ln_count) {
-            if (K <= LN_STAGED_MAX_K && maps.has_out)
-                return launch<T, 256, LN_EPI_WG, true, 3, -1, true, true>(maps, M, N, K, e, sms, fault, s);
+        // At 768 columns: short mainloops (K up to 1280, the staged residual)
+        // on clusters of three pairs, whose DSMEM exchange keeps the
+        // epilogue that bounds them short (the grid form's L2 handshake
+        // measured 30% slower there); long ones on the grid form with the
+        // statistics buffer (all groups of three pairs: 4-6% faster at K =
+        // 3072).
+        if (N == 768 && e.ln_stats && e.ln_count && !(K <= LN_STAGED_MAX_K && maps.has_out))
             return launch<T, 256, LN_EPI_WG, true, 3, -1, false, true>(maps, M, N, K, e, sms, fault, s);
-        }
         if (N == 1024 && e.ln_stats && e.ln_count && !e.out2) {
             if (K <= LN_STAGED_MAX_K && maps.has_out)
                 return launch<T, 256, LN_EPI_WG, true, 4, -1, true, true>(maps, M, N, K, e, sms, fault, s);
