@@ -42,16 +42,24 @@ using namespace tc;
 // pair) that exchange row statistics through distributed shared memory.
 // RS (with LNS): each epilogue warp's 8 KB buffer holds its next tile's
 // residual rows (TMA loads) and then its output rows (one TMA store group).
-template <int BN, bool PAIR, int LNS = 0, int EPI_WG = 2, bool RS = false> struct Cfg {
+template <int BN, bool PAIR, int LNS = 0, int EPI_WG = 2, bool RS = false, int KIND = -1> struct Cfg {
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // W rows this CTA loads a stage
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    // The plain-store kernel on CTA pairs (QKV) reads the bias from global
+    // memory (L1) and takes a sixth stage in its room: its MMA thread waited
+    // 15-19% of its time for operands with five (the ring's lookahead is
+    // short of the L2 latency under load); 3-5% faster. The heavier
+    // epilogues (GELU, GeGLU) measured slower with the bias out of shared
+    // memory, so they keep five.
+    static constexpr bool SIX = LNS == 0 && PAIR && BN == 256 && KIND == EPI_STORE;
     // 16 epilogue warps (with the fused LayerNorm) take the room of two stages.
-    static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : (RS ? 4 : (LNS && EPI_WG > 2 ? 3 : 5));
+    static constexpr int STAGES = STAGE_BYTES > 32768 ? 3 : (RS ? 4 : (LNS && EPI_WG > 2 ? 3 : (SIX ? 6 : 5)));
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int MAX_BIAS = LNS ? 1024 : 4096;  // the bias vector, staged in shared memory once per CTA
+    // The bias vector, staged in shared memory once per CTA (none: read from global).
+    static constexpr int MAX_BIAS = LNS ? 1024 : (SIX ? 0 : 4096);
     // Output staging for TMA stores: two [32 x 32] 16-bit tiles per epilogue
     // warp (RS: four, the warp's 128 columns).
     static constexpr int WARP_STAGE = RS ? 4 * 2048 : 2 * 2048;
@@ -62,6 +70,7 @@ template <int BN, bool PAIR, int LNS = 0, int EPI_WG = 2, bool RS = false> struc
     static constexpr int LN_BYTES = LNS ? 2 * 1024 * 4 + 2 * 4 * PARTS * 32 * 8 : 0;
     // ring | barriers (padded to 1 KB) | store staging | bias | LayerNorm
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + STORE_BYTES + MAX_BIAS * 4 + LN_BYTES + 1024;
+    static_assert(SMEM <= 227 * 1024, "one CTA an SM");
 };
 
 // Instruction descriptor of kind::f16: F32 accumulator, A and B the same
@@ -611,7 +620,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                int M, int N, int K, Epilogue e, int *fault) {
     static_assert(LNS == 0 || (PAIR && BN == 256), "the fused LayerNorm runs on 256-column CTA pairs");
     static_assert(!RS || (LNS > 0 && BN / EPI_WG == 128), "staged residual rows: LayerNorm tiles of 128 columns a warp");
-    using C = Cfg<BN, PAIR, LNS, EPI_WG, RS>;
+    using C = Cfg<BN, PAIR, LNS, EPI_WG, RS, KIND>;
     constexpr int TM = PAIR ? 2 * BM : BM;  // rows a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -622,7 +631,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     volatile int *abort_flag = (volatile int *)(bars + 16 * C::STAGES + 40);
     uint8_t *staging = bars + 1024;
     float *bias_s = (float *)(staging + C::STORE_BYTES);
-    for (int i = threadIdx.x; i < N && e.bias; i += blockDim.x) bias_s[i] = e.bias[i];
+    if constexpr (C::MAX_BIAS > 0)
+        for (int i = threadIdx.x; i < N && e.bias; i += blockDim.x) bias_s[i] = e.bias[i];
+    // Where the epilogues read the bias: shared memory, or global memory.
+    const float *bias_src = C::MAX_BIAS > 0 ? (const float *)bias_s : e.bias;
     float *lnw_s = bias_s + C::MAX_BIAS, *lnb_s = lnw_s + 1024;
     float2 *stats_s = (float2 *)(lnb_s + 1024);  // [2 tiles][4 quarters][PARTS][32]
     const uint32_t stats0 = smem_u32(stats_s), sbar0 = full0 + 16 * C::STAGES + 64;  // [2 tiles][4 quarters]
@@ -846,7 +858,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
                         res_pending = true;
                     }
             } else {
-                epilogue_tile<T, COLS, KIND>(e, bias_s, tbase, row, row_ok, col_base, N, res, ss, &tout, release);
+                epilogue_tile<T, COLS, KIND>(e, bias_src, tbase, row, row_ok, col_base, N, res, ss, &tout, release);
             }
             if (++acc == 2) acc = 0, acc_phase ^= 1;
         }
@@ -944,7 +956,7 @@ template <class T, int LNS, bool RS = false> int ln_pairs() {
 
 template <class T, int BN, int EPI_WG, bool PAIR, int LNS = 0, int KIND = -1, bool RS = false, bool LG = false>
 cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
-    using C = Cfg<BN, PAIR, LNS, EPI_WG, RS>;
+    using C = Cfg<BN, PAIR, LNS, EPI_WG, RS, KIND>;
     auto kern = gemm_tc_kernel<T, BN, EPI_WG, PAIR, LNS, KIND, RS, LG>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (err != cudaSuccess) return err;
