@@ -159,8 +159,8 @@ __global__ void __launch_bounds__(256) embed_ln_vec_kernel(T *__restrict__ x, Pa
 // 16 bytes of T as floats: 8 halves/bf16s or 4 floats.
 template <class T> struct Vec {
     static constexpr int N = 16 / sizeof(T);
-    __device__ __forceinline__ static void load(const T *p, float *v) {
-        uint4 u = *reinterpret_cast<const uint4 *>(p);
+    __device__ __forceinline__ static void load(const T *p, float *v) { unpack(*reinterpret_cast<const uint4 *>(p), v); }
+    __device__ __forceinline__ static void unpack(const uint4 &u, float *v) {
         if constexpr (sizeof(T) == 4) {
             v[0] = __uint_as_float(u.x), v[1] = __uint_as_float(u.y), v[2] = __uint_as_float(u.z), v[3] = __uint_as_float(u.w);
         } else {
@@ -502,6 +502,104 @@ __global__ void __launch_bounds__(256) pool_kernel(const T *__restrict__ x, cons
     }
 }
 
+// Pooling for long rows and few vectors: one block per pooled vector, its
+// threads in `groups` groups of nq threads, thread q of a group owning the
+// V = 16 / sizeof(T) columns from q V. Group g sums its contiguous share of
+// the item's tokens in position order with AHEAD 16-byte loads in flight;
+// group 0 then adds the groups' sums in group order and scales by 1/n (as
+// F32), as the reference's split pooling does (core/cuda/kernels.cu:655-740).
+// One group is the CPU path's order exactly. The grouping depends only on
+// the item's token span, so a range over a whole row pools bit for bit as
+// the row does. L2 in F64 over the block.
+constexpr int POOL_THREADS = 1024, POOL_GROUPS = 16, POOL_AHEAD = 8;
+
+template <class T>
+__global__ void __launch_bounds__(POOL_THREADS) pool_split_kernel(const T *__restrict__ x,
+                                                                  const uint8_t *__restrict__ live,
+                                                                  const PoolItem *__restrict__ items, int h, int od,
+                                                                  int l2, float *__restrict__ out) {
+    constexpr int V = Vec<T>::N;
+    __shared__ float part[POOL_THREADS * V];
+    __shared__ uint32_t cnt[POOL_GROUPS];
+    __shared__ double red[POOL_THREADS / 32];
+    pdl_wait();
+    pdl_trigger();
+    const PoolItem it = items[blockIdx.x];
+    const int nq = (od + V - 1) / V;
+    const int groups = min(POOL_GROUPS, (int)blockDim.x / nq);
+    const int g = threadIdx.x / nq, q = threadIdx.x % nq;
+    if (g < groups) {
+        const int per = (it.c1 - it.c0 + groups - 1) / groups;
+        const int lo = it.c0 + g * per, hi = min(it.c1, lo + per);
+        const T *base = x + (int64_t)it.start * h + q * V;
+        const uint8_t *lv = live + it.start;
+        float acc[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = 0.0f;
+        uint32_t c = 0;
+        for (int t0 = lo; t0 < hi; t0 += POOL_AHEAD) {
+            uint4 v[POOL_AHEAD];
+            bool k[POOL_AHEAD];
+#pragma unroll
+            for (int u = 0; u < POOL_AHEAD; ++u) {
+                const int t = t0 + u;
+                k[u] = t < hi;
+                v[u] = k[u] ? __ldg(reinterpret_cast<const uint4 *>(base + (int64_t)t * h)) : make_uint4(0, 0, 0, 0);
+                if (it.live_only) k[u] = k[u] && lv[t];
+            }
+#pragma unroll
+            for (int u = 0; u < POOL_AHEAD; ++u) {
+                if (!k[u]) continue;
+                float f[V];
+                Vec<T>::unpack(v[u], f);
+#pragma unroll
+                for (int i = 0; i < V; ++i) acc[i] += f[i];
+                ++c;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) part[threadIdx.x * V + i] = acc[i];
+        if (q == 0) cnt[g] = c;
+    }
+    __syncthreads();
+    float val[V];
+    double sq = 0.0;
+    if (threadIdx.x < nq) {
+        uint32_t n = 0;
+#pragma unroll
+        for (int i = 0; i < V; ++i) val[i] = part[q * V + i];
+        for (int g2 = 1; g2 < groups; ++g2)
+#pragma unroll
+            for (int i = 0; i < V; ++i) val[i] += part[(g2 * nq + q) * V + i];
+        for (int g2 = 0; g2 < groups; ++g2) n += cnt[g2];
+        const float inv_n = 1.0f / (float)(n > 0 ? n : 1);
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            val[i] *= inv_n;
+            if (q * V + i < od) sq += (double)val[i] * (double)val[i];
+        }
+    }
+    float scale = 1.0f;
+    if (l2) {
+        sq = warp_sum(sq);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            double s2 = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+            s2 = warp_sum(s2);
+            if (threadIdx.x == 0) red[0] = s2;
+        }
+        __syncthreads();
+        scale = (float)(1.0 / fmax(sqrt(red[0]), 1e-12));
+    }
+    if (threadIdx.x < nq) {
+        float *dst = out + (int64_t)blockIdx.x * od;
+#pragma unroll
+        for (int i = 0; i < V; ++i)
+            if (q * V + i < od) dst[q * V + i] = l2 ? val[i] * scale : val[i];
+    }
+}
+
 // One thread per (token, part, pair): Q (part 0) and K (part 1) rotated.
 template <class T>
 __global__ void rope_kernel(T *qkv, const int32_t *__restrict__ tok_pos, const float *__restrict__ cos_t,
@@ -658,10 +756,19 @@ cudaError_t pool_vectors(Dt dt, const void *x, const uint8_t *tok_live, const Po
                          int output_dim, int normalize_l2, float *out, cudaStream_t s) {
     if (output_dim > 1024 || output_dim > hidden) return cudaErrorInvalidValue;
     if (count == 0) return cudaSuccess;
+    // 16-byte rows (every hidden width the model families have) take the
+    // split form; others the one-group form.
+    const bool split = hidden % (dt == Dt::F32 ? 4 : 8) == 0;
     switch (dt) {
-    case Dt::F32: return launch_pdl(pool_kernel<float>, count, 256, 0, s, (const float *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
-    case Dt::F16: return launch_pdl(pool_kernel<__half>, count, 256, 0, s, (const __half *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
-    case Dt::BF16: return launch_pdl(pool_kernel<__nv_bfloat16>, count, 256, 0, s, (const __nv_bfloat16 *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+    case Dt::F32:
+        if (split) return launch_pdl(pool_split_kernel<float>, count, POOL_THREADS, 0, s, (const float *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+        return launch_pdl(pool_kernel<float>, count, 256, 0, s, (const float *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+    case Dt::F16:
+        if (split) return launch_pdl(pool_split_kernel<__half>, count, POOL_THREADS, 0, s, (const __half *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+        return launch_pdl(pool_kernel<__half>, count, 256, 0, s, (const __half *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+    case Dt::BF16:
+        if (split) return launch_pdl(pool_split_kernel<__nv_bfloat16>, count, POOL_THREADS, 0, s, (const __nv_bfloat16 *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
+        return launch_pdl(pool_kernel<__nv_bfloat16>, count, 256, 0, s, (const __nv_bfloat16 *)x, tok_live, items, hidden, output_dim, normalize_l2, out);
     }
     return cudaErrorInvalidValue;
 }
