@@ -426,17 +426,23 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
     // Pass 1: v = accumulator + bias + residual, written back to TMEM (pass
     // 2 reads it from there); the part's sums of (v - k) and (v - k)^2 about
     // k, its first value (a shift that keeps the one-pass variance from
-    // cancelling).
-    float s1 = 0.0f, s2 = 0.0f, k = 0.0f;
+    // cancelling). Packed F32x2 arithmetic (each half rounds as the scalar
+    // operation would): the sums run over even and odd columns apart.
+    uint64_t s1p = 0, s2p = 0;  // 0 bits = +0.0f pairs
+    float k = 0.0f;
+    uint64_t nk = 0;
 #pragma unroll
     for (int c = 0; c < COLS; c += 32) {
         __syncwarp();
         tmem_ld32(tbase + c, v);
-        const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col_base + c);
+        if (e.bias) {
+            const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col_base + c);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 bb = e.bias ? b4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            v[4 * i] += bb.x, v[4 * i + 1] += bb.y, v[4 * i + 2] += bb.z, v[4 * i + 3] += bb.w;
+            for (int i = 0; i < 8; ++i) {
+                const float4 bb = b4[i];
+                upk2(add2(pk2(v[4 * i], v[4 * i + 1]), pk2(bb.x, bb.y)), v[4 * i], v[4 * i + 1]);
+                upk2(add2(pk2(v[4 * i + 2], v[4 * i + 3]), pk2(bb.z, bb.w)), v[4 * i + 2], v[4 * i + 3]);
+            }
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -450,8 +456,8 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float2 f = unpack2<T>(w4[j]);
-                v[8 * i + 2 * j] += f.x;
-                v[8 * i + 2 * j + 1] += f.y;
+                const int q = 8 * i + 2 * j;
+                upk2(add2(pk2(v[q], v[q + 1]), pk2(f.x, f.y)), v[q], v[q + 1]);
             }
         }
         if (dual) {
@@ -467,13 +473,24 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
             }
         }
         tmem_st32(tbase + c, v);
-        if (c == 0) k = v[0];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const float d = v[i] - k;
-            s1 += d;
-            s2 = fmaf(d, d, s2);
+        if (c == 0) {
+            k = v[0];
+            nk = pk2(-k, -k);
         }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const uint64_t d = add2(pk2(v[2 * i], v[2 * i + 1]), nk);
+            s1p = add2(s1p, d);
+            s2p = fma2(d, d, s2p);
+        }
+    }
+    float s1, s2;
+    {
+        float a, b, c2, d2;
+        upk2(s1p, a, b);
+        upk2(s2p, c2, d2);
+        s1 = a + b;
+        s2 = c2 + d2;
     }
     if (dual) {
         fence_async_smem();
@@ -540,6 +557,9 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
         M2 += parts[p].y + (float)COLS * d * d;
     }
     const float inv = 1.0f / sqrtf(M2 / (float)(PARTS * COLS) + e.ln_eps);
+    // (v - mean) inv as one packed FMA, v inv - mean inv: the rounding of
+    // mean inv is far below the F16 / BF16 rounding of the output.
+    const uint64_t ia = pk2(inv, inv), ib = pk2(-mean * inv, -mean * inv);
     // Pass 2: normalise and store, 64 columns a step.
     static_assert(COLS % 64 == 0, "the LayerNorm epilogue stores 64 columns a step");
     if (dual) {
@@ -548,13 +568,12 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
     }
 #pragma unroll 1
     for (int c = 0; c < COLS; c += 64) {
-        uint32_t raw[2][32];
+        float w[2][32];  // the accumulator's v, normalised in place
         __syncwarp();
-        tmem_ld32_async(tbase + c, raw[0]);
-        tmem_ld32_async(tbase + c + 32, raw[1]);
+        tmem_ld32_async(tbase + c, w[0]);
+        tmem_ld32_async(tbase + c + 32, w[1]);
         tmem_wait_ld();
         if (c + 64 >= COLS) release();
-        float w[2][32];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int col = col_base + c + 32 * hh;
@@ -563,11 +582,9 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const float4 ww = w4[i], bb = b4[i];
-                const float *r = reinterpret_cast<const float *>(raw[hh]) + 4 * i;
-                w[hh][4 * i] = (r[0] - mean) * inv * ww.x + bb.x;
-                w[hh][4 * i + 1] = (r[1] - mean) * inv * ww.y + bb.y;
-                w[hh][4 * i + 2] = (r[2] - mean) * inv * ww.z + bb.z;
-                w[hh][4 * i + 3] = (r[3] - mean) * inv * ww.w + bb.w;
+                float *r = w[hh] + 4 * i;
+                upk2(fma2(fma2(pk2(r[0], r[1]), ia, ib), pk2(ww.x, ww.y), pk2(bb.x, bb.y)), r[0], r[1]);
+                upk2(fma2(fma2(pk2(r[2], r[3]), ia, ib), pk2(ww.z, ww.w), pk2(bb.z, bb.w)), r[2], r[3]);
             }
         }
         if constexpr (RS) {
