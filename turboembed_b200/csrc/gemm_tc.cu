@@ -209,22 +209,27 @@ __device__ __forceinline__ void rope_tile(const Epilogue &e, const float *bias_s
 #pragma unroll
             for (int i = 0; i < 64; ++i) v[i] += (col + i < N) ? bias_s[col + i] : 0.0f;
         if (row_ok && col < e.rope_cols) {
-            // The row's table entries, four at a time (HALF is a multiple of 4).
+            // The row's table entries, four at a time (HALF is a multiple of
+            // 4), applied to pairs of neighbouring k in packed F32x2: each
+            // half rounds as the scalar multiply and add would, and x1 c -
+            // x2 s is x1 c + x2 (-s) bit for bit.
             const float4 *cs = reinterpret_cast<const float4 *>(e.cos + (int64_t)e.tok_pos[row] * HALF);
             const float4 *sn = reinterpret_cast<const float4 *>(e.sin + (int64_t)e.tok_pos[row] * HALF);
 #pragma unroll
             for (int k4 = 0; k4 < HALF / 4; ++k4) {
                 const float4 c4 = cs[k4], s4 = sn[k4];
-                const float ck[4] = {c4.x, c4.y, c4.z, c4.w}, sk[4] = {s4.x, s4.y, s4.z, s4.w};
+                const uint64_t cp[2] = {pk2(c4.x, c4.y), pk2(c4.z, c4.w)}, sp[2] = {pk2(s4.x, s4.y), pk2(s4.z, s4.w)};
+                const uint64_t np[2] = {pk2(-s4.x, -s4.y), pk2(-s4.z, -s4.w)};
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int k = 4 * k4 + t;
+                for (int t = 0; t < 2; ++t) {
+                    const int k = 4 * k4 + 2 * t;
 #pragma unroll
                     for (int sg = 0; sg < 64; sg += HD) {
                         if (col + sg < e.rope_cols) {
-                            const float x1 = v[sg + k], x2 = v[sg + k + HALF];
-                            v[sg + k] = __fsub_rn(__fmul_rn(x1, ck[t]), __fmul_rn(x2, sk[t]));
-                            v[sg + k + HALF] = __fadd_rn(__fmul_rn(x2, ck[t]), __fmul_rn(x1, sk[t]));
+                            const uint64_t x1 = pk2(v[sg + k], v[sg + k + 1]);
+                            const uint64_t x2 = pk2(v[sg + k + HALF], v[sg + k + HALF + 1]);
+                            upk2(add2(mul2(x1, cp[t]), mul2(x2, np[t])), v[sg + k], v[sg + k + 1]);
+                            upk2(add2(mul2(x2, cp[t]), mul2(x1, sp[t])), v[sg + k + HALF], v[sg + k + HALF + 1]);
                         }
                     }
                 }
@@ -288,8 +293,10 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                     } else {
                         gelu_erf_fast2(g0, g1);
                     }
-                    o[hh * 16 + i] = gated_out<T>(g0 * u0);
-                    o[hh * 16 + i + 1] = gated_out<T>(g1 * u1);
+                    float y0, y1;
+                    upk2(mul2(pk2(g0, g1), pk2(u0, u1)), y0, y1);
+                    o[hh * 16 + i] = gated_out<T>(y0);
+                    o[hh * 16 + i + 1] = gated_out<T>(y1);
                 }
             stage_store32<T>(o, col / 2, ss, out_map);
             continue;
@@ -308,11 +315,9 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                 const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    float4 bb = b4[i];
-                    v[4 * i] += bb.x;
-                    v[4 * i + 1] += bb.y;
-                    v[4 * i + 2] += bb.z;
-                    v[4 * i + 3] += bb.w;
+                    const float4 bb = b4[i];
+                    upk2(add2(pk2(v[4 * i], v[4 * i + 1]), pk2(bb.x, bb.y)), v[4 * i], v[4 * i + 1]);
+                    upk2(add2(pk2(v[4 * i + 2], v[4 * i + 3]), pk2(bb.z, bb.w)), v[4 * i + 2], v[4 * i + 3]);
                 }
             }
             if (kind == EPI_GATED) {
@@ -348,8 +353,8 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const float2 f = unpack2<T>(w4[j]);
-                        v[8 * i + 2 * j] += f.x;
-                        v[8 * i + 2 * j + 1] += f.y;
+                        const int q = 8 * i + 2 * j;
+                        upk2(add2(pk2(v[q], v[q + 1]), pk2(f.x, f.y)), v[q], v[q + 1]);
                     }
                 }
             }
