@@ -605,10 +605,10 @@ def main():
             allv = shard.gather_vectors(local_vec, vec_counts)
         e1.record()
         torch.cuda.synchronize(local)
-        g_ms = max_over_ranks(e0.elapsed_time(e1) / 10)
+        ag_ms = max_over_ranks(e0.elapsed_time(e1) / 10)
         off = sum(vec_counts[:rank])
-        gather = {"ms": g_ms, "repeats": 10, "rows": int(allv.shape[0]), "bytes": int(allv.numel() * 4),
-                  "GB_per_s": allv.numel() * 4 / (g_ms / 1000) / 1e9,
+        gather = {"ms": ag_ms, "repeats": 10, "rows": int(allv.shape[0]), "bytes": int(allv.numel() * 4),
+                  "GB_per_s": allv.numel() * 4 / (ag_ms / 1000) / 1e9,
                   "matches_local": bool(torch.equal(allv[off:off + vec_counts[rank]], local_vec))}
 
     if rank == 0:
