@@ -35,6 +35,7 @@ namespace {
 
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
 constexpr int LN_STAGED_MAX_K = 1280;  // fused LayerNorm GEMMs with the staged residual (K up to this)
+constexpr int LN_CLUSTER_MAX_K = 768;  // fused LayerNorm GEMMs at 768 columns on DSMEM clusters (K up to this)
 using namespace tc;
 
 // LNS > 0: the fused residual + LayerNorm epilogue over rows of N = 256 LNS
@@ -516,13 +517,14 @@ __device__ __forceinline__ bool epilogue_ln_tile(const Epilogue &e, const float 
         // arrived, the parts are read back from L2.
         float2 *st = e.ln_stats + (int64_t)(ss.row0 + lane) * PARTS;
         __stcg(st + L.slot, make_float2(mean_p, m2));
-        __threadfence();
         __syncwarp();
         uint32_t *cnt = e.ln_count + (ss.row0 >> 5);
         bool ok = true;
         if (lane == 0) {
-            __threadfence();  // every lane's part, seen through the warp barrier, before the arrival
-            atomicAdd(cnt, 1u);
+            // A release at GPU scope: every lane's part, ordered before it
+            // through the warp barrier, is visible to whoever acquires the
+            // count.
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
             ok = wait_count(cnt, PARTS, abort_flag, fault);
         }
         if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
@@ -1019,14 +1021,17 @@ cudaError_t launch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, i
 template <class T>
 cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e, int sms, int *fault, cudaStream_t s) {
     if (e.kind == EPI_RESIDUAL_LN) {
-        // At 768 columns: short mainloops (K up to 1280, the staged residual)
-        // on clusters of three pairs, whose DSMEM exchange keeps the
-        // epilogue that bounds them short (the grid form's L2 handshake
-        // measured 30% slower there); long ones on the grid form with the
-        // statistics buffer (all groups of three pairs: 4-6% faster at K =
-        // 3072).
-        if (N == 768 && e.ln_stats && e.ln_count && !(K <= LN_STAGED_MAX_K && maps.has_out))
+        // At 768 columns: K = 768 (attention-out) on clusters of three
+        // pairs, whose DSMEM exchange keeps the epilogue that bounds so
+        // short a mainloop short (the grid form's L2 handshake measured
+        // 20-25% slower there); longer ones on the grid form with the
+        // statistics buffer (all groups of three pairs: 7% faster at K =
+        // 1152 with the staged residual, 4-6% at K = 3072).
+        if (N == 768 && e.ln_stats && e.ln_count && K > LN_CLUSTER_MAX_K) {
+            if (K <= LN_STAGED_MAX_K && maps.has_out)
+                return launch<T, 256, LN_EPI_WG, true, 3, -1, true, true>(maps, M, N, K, e, sms, fault, s);
             return launch<T, 256, LN_EPI_WG, true, 3, -1, false, true>(maps, M, N, K, e, sms, fault, s);
+        }
         if (N == 1024 && e.ln_stats && e.ln_count && !e.out2) {
             if (K <= LN_STAGED_MAX_K && maps.has_out)
                 return launch<T, 256, LN_EPI_WG, true, 4, -1, true, true>(maps, M, N, K, e, sms, fault, s);
