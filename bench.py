@@ -540,14 +540,20 @@ def main():
     # the algorithmic FLOPs is the dense TF32 rate (half the BF16 rate) / 3.
     peak = sustained / 2 / 3 if f32 else sustained
 
-    # End to end through the C table with host buffers.
+    # End to end through the C table with host buffers. The result lands in
+    # page-locked host memory, allocated once (in the first warm-up step), as
+    # a caller that reads every step keeps it.
     e2e_t = []
+    out_host = None
     barrier()
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
         write()
         run = sess.run()
-        res = sess.head_scores() if wl.head else sess.read()
+        if not wl.head and out_host is None:
+            import torch
+            out_host = torch.empty(sess._count * sess._out_dim, dtype=torch.float32, pin_memory=True).numpy()
+        res = sess.head_scores() if wl.head else sess.read(out=out_host)
         if i >= args.warmup:
             e2e_t.append(time.perf_counter() - t0)
     barrier()

@@ -1176,7 +1176,7 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
             for (int q0 = 0; q0 < s->row_len[b]; q0 += ATTN_TC2_QUERIES)
                 attn2[na2++] = AttnItem{s->row_start[b], s->row_len[b], q0, holes};
     }
-    // One copy: the token arrays through the last attention item.
+    // The used part of each plan array, one copy each.
     const size_t tok_bytes = (size_t)t;
     CK(cudaMemcpyAsync(s->plan_dev + s->lay.tok_id, H + s->lay.tok_id, tok_bytes * 4, cudaMemcpyHostToDevice, c->stream), "upload");
     CK(cudaMemcpyAsync(s->plan_dev + s->lay.tok_type, H + s->lay.tok_type, tok_bytes * 4, cudaMemcpyHostToDevice, c->stream), "upload");

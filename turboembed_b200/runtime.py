@@ -272,6 +272,8 @@ class Session:
     def read(self, out=None):
         """The last run's vectors, [count, output_dim] F32, via buffer_read."""
         n = self._count * self._out_dim
+        if out is not None and (out.dtype != np.float32 or out.size != n or not out.flags.c_contiguous):
+            raise ValueError(f"read into a contiguous F32 array of {n} values, not {out.dtype} x {out.size}")
         dst = np.empty(n, np.float32) if out is None else out
         err = abi.new_error()
         _check(self.t.buffer_read(self.last_run.output, _ptr(dst), n * 4, C.byref(err)), err, "buffer_read")
