@@ -72,11 +72,15 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t tmem_d, uint64_t da, uin
 // lo = x - hi(x), hi = x with its low 13 mantissa bits cleared.
 __device__ __forceinline__ float tf32_lo(float x) { return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)); }
 
-template <bool PAIR>
+// TN1: the one-CTA kernel's tile width, 128 or 64 (64 when 128-wide tiles
+// would leave SMs idle: the W tile still loads and splits 128 rows, of which
+// the MMA reads the first 64).
+template <bool PAIR, int TN1 = 128>
 __global__ void __launch_bounds__(512, 1)
 gemm_tf32_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw, int M, int N, int K,
                  Epilogue e, int *fault) {
-    constexpr int TN = PAIR ? 256 : 128;  // output columns a tile (TMEM columns an accumulator)
+    static_assert(PAIR || TN1 == 128 || TN1 == 64, "one-CTA tiles of 128 or 64 columns");
+    constexpr int TN = PAIR ? 256 : TN1;  // output columns a tile (TMEM columns an accumulator)
     constexpr int TM = PAIR ? 256 : 128;  // output rows a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -384,10 +388,14 @@ cudaError_t gemm_tf32(const CUtensorMap &a_map, const CUtensorMap &w_map, int M,
         cfg.numAttrs = 2;
         return counted(cudaLaunchKernelEx(&cfg, kern, a_map, w_map, M, N, K, epi, fault));
     }
-    auto kern = gemm_tf32_kernel<false>;
+    // 128 x 64 tiles when 128 x 128 ones would not fill the SMs (small
+    // batches: MiniLM's 384-column products on a few thousand tokens).
+    const int m_tiles = (M + TBM - 1) / TBM;
+    const bool narrow = m_tiles * (N / 128) < sms;
+    auto kern = narrow ? gemm_tf32_kernel<false, 64> : gemm_tf32_kernel<false, 128>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (err != cudaSuccess) return err;
-    const int tiles = ((M + TBM - 1) / TBM) * (N / 128);
+    const int tiles = m_tiles * (N / (narrow ? 64 : 128));
     const int grid = tiles < sms ? tiles : sms;
     return launch_pdl(kern, grid, 512, SMEM, s, a_map, w_map, M, N, K, epi, fault);
 }
