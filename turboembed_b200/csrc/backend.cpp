@@ -1115,22 +1115,29 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
         furthest[g.row] = std::max(furthest[g.row], g.end);
     }
     int t = 0, max_len = 0;
+    std::vector<uint8_t> row_holes(r->batch, 0);
     for (uint32_t b = 0; b < r->batch; ++b) {
         const int32_t *mk = r->mask + (size_t)b * stride;
-        int live = 0;
-        for (uint32_t p = 0; p < r->seq; ++p)
-            if (mk[p]) live = (int)p + 1;
+        int live = 0;  // one past the row's last live token
+        for (int p = (int)r->seq - 1; p >= 0; --p)
+            if (mk[p]) {
+                live = p + 1;
+                break;
+            }
         const int len = count ? std::max(live, (int)furthest[b]) : live;
         if (len == 0) return fail(err, TURBO_E_INVALID_ARGUMENT, 0, "mask row %u has no 1: a row needs a token", b);
         s->row_start[b] = t;
         s->row_len[b] = len;
         const int32_t *ids = r->ids + (size_t)b * stride, *ty = r->types ? r->types + (size_t)b * stride : nullptr;
+        uint8_t holes = 0;
         for (int p = 0; p < len; ++p) {
             tok_id[t + p] = ids[p];
             tok_type[t + p] = ty ? ty[p] : 0;
             tok_pos[t + p] = p;
             tok_live[t + p] = mk[p] != 0;
+            holes |= mk[p] == 0;
         }
+        row_holes[b] = holes;
         t += len;
         max_len = std::max(max_len, len);
     }
@@ -1169,8 +1176,7 @@ int32_t write_rows(Session *s, const turbo_backend_embed_rows *r, const turbo_to
     const bool pairs = s->max_attn2_items > 0 && t >= 1024 * (int)r->batch;
     int na = 0, na2 = 0;
     for (int b : order) {
-        int holes = 0;
-        for (int p = 0; p < s->row_len[b]; ++p) holes |= !tok_live[s->row_start[b] + p];
+        const int holes = row_holes[b];
         for (int q0 = 0; q0 < s->row_len[b]; q0 += qt) attn[na++] = AttnItem{s->row_start[b], s->row_len[b], q0, holes};
         if (pairs)
             for (int q0 = 0; q0 < s->row_len[b]; q0 += ATTN_TC2_QUERIES)
