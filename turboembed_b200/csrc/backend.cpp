@@ -1478,6 +1478,11 @@ cudaError_t encode(Session *s) {
         }
         Epilogue g;
         g.kind = EPI_GATED, g.out = s->ffn, g.ldo = I, g.act = m->act;
+        // GeGLU at FASTEST takes the tanh form of GELU, as the reference's
+        // FASTEST does for a 16-bit output (core/cuda/kernels.h:468, the
+        // default of gelu_named, core/cuda/backend.cpp:1564-1573); F32
+        // outputs keep erf, as there.
+        if (m->act == 1 && s->precision == TURBO_PRECISION_FASTEST && dt != Dt::F32) g.act = 3;
         if ((e = linear(s, &s->map_xn, s->xn, L.ffn_in, g, T, &s->out_ffn)) != cudaSuccess) return e;
         Epilogue f2;
         f2.kind = EPI_RESIDUAL, f2.out = s->x, f2.ldo = h;

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T *__restrict__ a,
                 // thread's four columns hold two whole pairs.
                 if ((j & 1) == 0 && c + 1 < N) {
                     float u = acc[i][j + 1] + (e.bias ? e.bias[c + 1] : 0.0f);
-                    float g = e.act == 2 ? silu(v) : gelu_erf(v);
+                    float g = e.act == 2 ? silu(v) : e.act == 3 ? gelu_tanh(v) : gelu_erf(v);
                     st((T *)e.out + (int64_t)r * e.ldo + c / 2, gated_out<T>(g * u));
                 }
                 continue;

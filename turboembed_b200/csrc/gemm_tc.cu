@@ -36,6 +36,11 @@ namespace {
 constexpr int BM = 128, BK = 64, UMMA_K = 16;
 constexpr int LN_STAGED_MAX_K = 1280;  // fused LayerNorm GEMMs with the staged residual (K up to this)
 constexpr int LN_CLUSTER_MAX_K = 768;  // fused LayerNorm GEMMs at 768 columns on DSMEM clusters (K up to this)
+// The gated product with GELU in its tanh form (EPI_GATED with act 3): a
+// kernel KIND of its own, so the erf form's code stays out of it (one kernel
+// holding both forms measured slower in both).
+constexpr int KIND_GATED_TANH = 100;
+__host__ __device__ constexpr bool gated_kind(int kind) { return kind == EPI_GATED || kind == KIND_GATED_TANH; }
 using namespace tc;
 
 // LNS > 0: the fused residual + LayerNorm epilogue over rows of N = 256 LNS
@@ -271,7 +276,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
         if (c2 + 32 < COLS) tmem_ld32_async(tbase + c2 + 32, raw[1]);
         tmem_wait_ld();
         if (c2 + 64 >= COLS) release();
-        if (kind == EPI_GATED && ss.tma) {
+        if (gated_kind(kind) && ss.tma) {
             // 64 interleaved (gate, up) columns -> 32 outputs, one staged tile.
             const int col = col_base + c2;
             if (col >= N) continue;
@@ -288,7 +293,9 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                         g1 += bias_s[col + hh * 32 + 2 * i + 2];
                         u1 += bias_s[col + hh * 32 + 2 * i + 3];
                     }
-                    if (e.act == 2) {
+                    if (kind == KIND_GATED_TANH || (KIND < 0 && e.act == 3)) {
+                        gelu_tanh2(g0, g1);
+                    } else if (e.act == 2) {
                         g0 = silu(g0);
                         g1 = silu(g1);
                     } else {
@@ -310,7 +317,7 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
             const int c = c2 + hh * 32;
             const int col = col_base + c;
             if (c >= COLS || col >= N) continue;
-            if (!row_ok && (kind == EPI_GATED || !ss.tma)) continue;
+            if (!row_ok && (gated_kind(kind) || !ss.tma)) continue;
             float *v = vv[hh];
             if (e.bias) {
                 const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col);
@@ -321,12 +328,14 @@ __device__ __forceinline__ void epilogue_tile(const Epilogue &e, const float *bi
                     upk2(add2(pk2(v[4 * i + 2], v[4 * i + 3]), pk2(bb.z, bb.w)), v[4 * i + 2], v[4 * i + 3]);
                 }
             }
-            if (kind == EPI_GATED) {
+            if (gated_kind(kind)) {
                 float o[16];
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
                     float g0 = v[2 * i], g1 = v[2 * i + 2];
-                    if (e.act == 2) {
+                    if (kind == KIND_GATED_TANH || (KIND < 0 && e.act == 3)) {
+                        gelu_tanh2(g0, g1);
+                    } else if (e.act == 2) {
                         g0 = silu(g0);
                         g1 = silu(g1);
                     } else {
@@ -795,7 +804,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         const uint32_t tempty_leader = PAIR ? mapa(tempty0, lead) : tempty0;
         // Gated tiles store 32 outputs per 64 columns: whole tiles need N % 64 == 0.
         const int kind = LNS ? EPI_RESIDUAL_LN : (KIND >= 0 ? KIND : e.kind);
-        const bool tma_out = use_tma_store && (kind != EPI_GATED || N % 64 == 0);
+        const bool tma_out = use_tma_store && (!gated_kind(kind) || N % 64 == 0);
         StoreStage ss{tma_out, staging + ew * C::WARP_STAGE, 0, 0};
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -1054,7 +1063,9 @@ cudaError_t dispatch(const TcMaps &maps, int M, int N, int K, const Epilogue &e,
         case EPI_STORE: return launch<T, 256, 2, true, 0, EPI_STORE>(maps, M, N, K, e, sms, fault, s);
         case EPI_GELU: return launch<T, 256, 2, true, 0, EPI_GELU>(maps, M, N, K, e, sms, fault, s);
         case EPI_RESIDUAL: return launch<T, 256, 2, true, 0, EPI_RESIDUAL>(maps, M, N, K, e, sms, fault, s);
-        case EPI_GATED: return launch<T, 256, 2, true, 0, EPI_GATED>(maps, M, N, K, e, sms, fault, s);
+        case EPI_GATED:
+            if (e.act == 3) return launch<T, 256, 2, true, 0, KIND_GATED_TANH>(maps, M, N, K, e, sms, fault, s);
+            return launch<T, 256, 2, true, 0, EPI_GATED>(maps, M, N, K, e, sms, fault, s);
         case EPI_ROPE: return launch<T, 256, 2, true, 0, EPI_ROPE>(maps, M, N, K, e, sms, fault, s);
         case EPI_GELU_TANH: return launch<T, 256, 2, true, 0, EPI_GELU_TANH>(maps, M, N, K, e, sms, fault, s);
         default: return cudaErrorNotSupported;

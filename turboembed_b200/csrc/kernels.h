@@ -28,7 +28,7 @@ struct Epilogue {
     const float *bias = nullptr;  // [N] F32, or null for none
     void *out = nullptr;          // y, element type = the GEMM's
     int64_t ldo = 0;              // y's row stride, elements
-    int act = 1;                  // EPI_GATED: 1 GELU (erf), 2 SiLU
+    int act = 1;                  // EPI_GATED: 1 GELU (erf), 2 SiLU, 3 GELU (tanh form; 16-bit outputs only)
     // EPI_ROPE: cos/sin tables [positions][head_dim / 2] F32 for this layer's
     // base, each token's position, the head width, and the first column
     // that is not rotated (2 * hidden: V is left alone).
