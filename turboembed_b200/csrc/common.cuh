@@ -163,12 +163,11 @@ __device__ __forceinline__ void gelu_erf_fast2(float &x0, float &x1) {
     const float z0 = fminf(fabsf(x0) * 0.70710678118654752f, 4.5f), z1 = fminf(fabsf(x1) * 0.70710678118654752f, 4.5f);
     const uint64_t z = pk2(z0, z1);
     const uint64_t d = fma2(pk2(0.3275911f, 0.3275911f), z, pk2(1.0f, 1.0f));
-    float d0, d1;
+    float d0, d1, r0, r1;
     upk2(d, d0, d1);
-    uint64_t r = pk2(__int_as_float(0x7EF311C7 - __float_as_int(d0)), __int_as_float(0x7EF311C7 - __float_as_int(d1)));
-    const uint64_t two = pk2(2.0f, 2.0f), nd = pk2(-d0, -d1);
-#pragma unroll
-    for (int i = 0; i < 3; ++i) r = mul2(r, fma2(nd, r, two));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+    const uint64_t r = pk2(r0, r1);
     uint64_t p = fma2(pk2(1.061405429f, 1.061405429f), r, pk2(-1.453152027f, -1.453152027f));
     p = fma2(p, r, pk2(1.421413741f, 1.421413741f));
     p = fma2(p, r, pk2(-0.284496736f, -0.284496736f));
